@@ -1,0 +1,205 @@
+/*
+ * qwen_b200.h -- C ABI of the B200 decode engine for the Qwen2.5-1.5B
+ * architecture with Q4 block-32 weights (libqwen_b200.so).
+ *
+ * Plain C types only: device buffers are raw pointers, fp16 values are
+ * uint16_t bit patterns, streams are cudaStream_t passed as void*.  Every
+ * entry point returns a status (QWEN_OK == 0); qwen_last_error() gives a
+ * thread-local message for the last failure.  Nothing here exits or aborts.
+ *
+ * Each declaration names the reference interface it replaces
+ * (Raiden-Makoto/QwenInferenceEngine, file:line).
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------
+ * The reference throws WeightLoadingError.fileNotFound / bufferCreationFailed
+ * (WeightLoader.swift:11-14) and MetalSetupError (MetalManager.swift:12-18)
+ * and calls fatalError on device failures (InferenceEngine.swift:18,63,84,88);
+ * here each of those is a status code. */
+#define QWEN_OK 0
+#define QWEN_ERR_INVALID_ARGUMENT 1
+#define QWEN_ERR_CUDA 2
+#define QWEN_ERR_FILE_NOT_FOUND 3   /* WeightLoadingError.fileNotFound */
+#define QWEN_ERR_BAD_WEIGHT_FILE 4  /* WeightLoadingError.bufferCreationFailed, wrong size */
+#define QWEN_ERR_OUT_OF_MEMORY 5
+#define QWEN_ERR_DEVICE_TIMEOUT 6   /* a bounded device-side wait gave up */
+#define QWEN_ERR_NO_DEVICE 7        /* MetalSetupError.deviceInitializationFailed */
+#define QWEN_ERR_STATE 8            /* call order (e.g. forward before weights) */
+
+const char* qwen_last_error(void);
+int qwen_abi_version(void);
+
+/* ======================================================================
+ * Operators: one entry per reference Metal pipeline (MetalManager.swift:43-49
+ * registers them; InferenceEngine.swift:107-264 binds buffers by index).
+ * Arguments keep the reference buffer meaning and layout.  All pointers are
+ * device pointers; work is enqueued on `stream` (NULL = default stream).
+ * ====================================================================== */
+
+/* gemv_q4_0, matmul.metal:9-73 (buffers 0..5 = packed, scales, x, y,
+ * constants[K,..], bias).  packed: [n_rows][k/2] bytes, low nibble = even k;
+ * scales: [n_rows][k/32] fp16; y[r] = half(sum_k ((q-8)*s) x_k + bias[r]).
+ * bias may be NULL.  k must be a multiple of 32. */
+int qwen_gemv_q4_0(const uint8_t* packed, const uint16_t* scales, const uint16_t* x,
+                   uint16_t* y, uint32_t k, const uint16_t* bias, uint32_t n_rows,
+                   void* stream);
+
+/* gemv_fp16, matmul.metal:75-113 (LM head, InferenceEngine.swift:259-264).
+ * w: [n_rows][k] fp16 row-major; y = half(w x), fp32 accumulation. */
+int qwen_gemv_fp16(const uint16_t* w, const uint16_t* x, uint16_t* y, uint32_t k,
+                   uint32_t n_rows, void* stream);
+
+/* rms_norm_q4, rmsnorm.metal:9-46: out = half(half(x*s)*gamma) over 1536. */
+int qwen_rms_norm_q4(const uint16_t* x, const uint16_t* gamma, uint16_t* out, void* stream);
+
+/* apply_rope_q4, rope.metal:12-39: in place on n_heads*128 fp16, position =
+ * *seq_len - 1 (device uint32, as the reference's seqLen buffer). */
+int qwen_apply_rope_q4(uint16_t* vec, uint32_t n_heads, const uint32_t* seq_len,
+                       void* stream);
+
+/* write_kv_cache, attention.metal:67-84: cache[(seq_len-1)*256 + i] = k/v[i];
+ * positions >= max_ctx are skipped (the reference guards 1024). */
+int qwen_write_kv_cache(const uint16_t* k, const uint16_t* v, uint16_t* k_cache,
+                        uint16_t* v_cache, const uint32_t* seq_len, uint32_t max_ctx,
+                        void* stream);
+
+/* attention_scores, attention.metal:9-32: scores[h*L + t] (fp32, L = *seq_len).
+ * max_ctx bounds the launch (L must not exceed it). */
+int qwen_attention_scores(const uint16_t* q, const uint16_t* k_cache, float* scores,
+                          const uint32_t* seq_len, uint32_t max_ctx, void* stream);
+/* softmax, activations.metal:29-55 (12 heads, in place). */
+int qwen_softmax(float* scores, const uint32_t* seq_len, void* stream);
+/* attn_weighted_sum, attention.metal:34-56. */
+int qwen_attn_weighted_sum(const float* scores, const uint16_t* v_cache, uint16_t* out,
+                           const uint32_t* seq_len, void* stream);
+
+/* residual_add, attention.metal:58-65: out = half(a + b). */
+int qwen_residual_add(const uint16_t* a, const uint16_t* b, uint16_t* out, uint32_t n,
+                      void* stream);
+/* swiglu, activations.metal:9-27: gate = half(silu(gate) * up), in place. */
+int qwen_swiglu(uint16_t* gate, const uint16_t* up, uint32_t n, void* stream);
+
+/* Fused GQA decode attention (the engine's split-K kernel; replaces the
+ * attention_scores -> softmax -> attn_weighted_sum chain,
+ * InferenceEngine.swift:162-182).  q: 12x128 fp16 (after RoPE); caches in the
+ * reference layout [pos][256]; L = *seq_len positions; out: 1536 fp16. */
+int qwen_attention_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                          uint16_t* out, const uint32_t* seq_len, uint32_t max_ctx,
+                          void* stream);
+
+/* (q-8)*scale for n_weights weights, low nibble first (matmul.metal:37-42). */
+int qwen_dequant_q4(const uint8_t* packed, const uint16_t* scales, size_t n_weights,
+                    float* out, void* stream);
+
+/* packAndSave4Bit, QwenPipelines.swift:97-145, on the device: symmetric
+ * block-32 quantisation of n fp32 weights (flattened). */
+int qwen_quantize_q4(const float* w, size_t n, uint8_t* packed, uint16_t* scales,
+                     void* stream);
+
+/* extractNextTokenID, InferenceEngine.swift:273-368, on the device.
+ * logits: fp16 [n_seq][row_stride], the first `vocab` entries sampled.
+ * temperature <= 0 -> greedy (:277-294).  Otherwise top-p with the fixed-point
+ * nucleus rule: E_i = trunc(exp(l_i/T - max) * 2^31), keep the shortest prefix
+ * of (E desc, id asc) whose sum reaches floor(sum(E) * trunc(top_p*2^24) / 2^24),
+ * draw R = floor(kept * u24 / 2^24) and return the first kept id whose running
+ * sum exceeds R.  u24[n_seq] are 24-bit uniforms (device).
+ * out_ids: int32 [n_seq], device. */
+int qwen_sample(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uint32_t vocab,
+                float temperature, float top_p, const uint32_t* u24, int32_t* out_ids,
+                void* stream);
+
+/* 24-bit uniform for (seed, sequence, step), SplitMix64 based; host helper. */
+uint32_t qwen_uniform24(uint64_t seed, uint64_t sequence, uint64_t step);
+
+/* ======================================================================
+ * Engine: QwenEngine (InferenceEngine.swift:9-52) with QwenModel /
+ * QwenLayer / WeightLoader (weights) and InferenceManager (state) behind one
+ * opaque handle.
+ * ====================================================================== */
+typedef struct qwen_engine qwen_engine;
+
+#define QWEN_KERNELS_FUSED 0 /* fused decode step (default) */
+#define QWEN_KERNELS_OPS 1   /* the reference dispatch order, one kernel per op */
+
+typedef struct qwen_engine_config {
+  int device;          /* CUDA device ordinal */
+  int max_ctx;         /* KV slots per sequence (QwenConfig.maxContextWindow = 1024) */
+  int batch;           /* independent sequences decoded together */
+  int n_layers;        /* decoder layers (28; fewer only for tests) */
+  int kernels;         /* QWEN_KERNELS_FUSED or QWEN_KERNELS_OPS */
+  float temperature;   /* extractNextTokenID default 0.7 (:273); <= 0 -> greedy */
+  float top_p;         /* default 0.8 (:273) */
+  uint64_t seed;       /* uniform stream seed (the reference's RNG is unseeded) */
+  int stop_on_eos;     /* generate() stops at 151645 / 151643 (:41) */
+} qwen_engine_config;
+
+void qwen_engine_config_default(qwen_engine_config* cfg);
+
+/* QwenEngine.init(weightsPath:kernelsPath:), InferenceEngine.swift:16-27:
+ * selects the device and allocates state; weights come from
+ * qwen_engine_load_weights or qwen_engine_init_random. */
+int qwen_engine_create(const qwen_engine_config* cfg, qwen_engine** out);
+int qwen_engine_destroy(qwen_engine* e);
+
+/* QwenModel(device:weightsPath:), QwenModel.swift:22-34, with
+ * WeightLoader.loadBuffer / loadLayerWeight (WeightLoader.swift:26-52): reads
+ * the reference directory layout global/embed_tokens.bin, global/final_norm.bin,
+ * layer{i}/{name}.bin (names QwenLayer.swift:31-51). */
+int qwen_engine_load_weights(qwen_engine* e, const char* weights_dir);
+
+/* Random-init weights on the device (linear N(0,0.02) quantised by the
+ * packAndSave4Bit rule, embeddings N(0,0.02) fp16, norms 1+N(0,0.02),
+ * biases N(0,0.02)). */
+int qwen_engine_init_random(qwen_engine* e, uint64_t seed);
+
+/* Clears positions (KV contents become unreachable). */
+int qwen_engine_reset(qwen_engine* e);
+
+/* forward(tokenID:position:), InferenceEngine.swift:54-271, for sequence 0 of
+ * a batch-1 engine: runs one decode step, samples with the configured
+ * temperature / top-p, returns the next token id.  Positions past max_ctx-1
+ * are clamped as the reference does (:55). */
+int qwen_engine_forward(qwen_engine* e, int32_t token, int32_t position, int32_t* next_token);
+
+/* generate(prompt:maxTokens:), InferenceEngine.swift:29-52, on token ids for
+ * every sequence of the batch: prompt_ids [batch][n_prompt]; out_ids
+ * [batch][max_tokens] receives the generated ids (the reference prints them);
+ * n_out[batch] how many each sequence produced. */
+int qwen_engine_generate(qwen_engine* e, const int32_t* prompt_ids, int32_t n_prompt,
+                         int32_t max_tokens, int32_t* out_ids, int32_t* n_out);
+
+/* Decode `n_steps` further tokens for every sequence from the engine's current
+ * state (after generate / prefill), without host synchronisation between
+ * steps; writes the ids to out_ids [batch][n_steps] (host). */
+int qwen_engine_decode(qwen_engine* e, int32_t n_steps, int32_t* out_ids);
+
+/* Prefill only: consume prompt_ids [batch][n_prompt] and leave the first
+ * sampled token pending (generate = prefill + decode). */
+int qwen_engine_prefill(qwen_engine* e, const int32_t* prompt_ids, int32_t n_prompt);
+
+/* fp16 logits of the last step for sequence `seq` (151936 values, host). */
+int qwen_engine_get_logits(qwen_engine* e, int32_t seq, uint16_t* host_logits);
+
+/* Copies one layer's KV cache of sequence `seq` to the host in the reference
+ * layout [n_pos][256] fp16 (InferenceManager.swift:63-65). */
+int qwen_engine_get_kv(qwen_engine* e, int32_t seq, int32_t layer, int32_t n_pos,
+                       uint16_t* host_k, uint16_t* host_v);
+
+/* Current position (tokens consumed) of sequence `seq`. */
+int qwen_engine_position(qwen_engine* e, int32_t seq, int32_t* position);
+
+/* Device and stream the engine runs on (for callers that time it). */
+int qwen_engine_stream(qwen_engine* e, void** stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

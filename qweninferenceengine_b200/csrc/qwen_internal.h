@@ -1,0 +1,75 @@
+// qwen_internal.h -- declarations shared by the CUDA translation units and the
+// C++ host engine of libqwen_b200.so (not installed; include/qwen_b200.h is
+// the public ABI).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace qwen {
+
+// ---------------------------------------------------------- attention ----
+struct AttnParams {
+  const __half* q;          // [n_seq][12][128] (after RoPE)
+  long long q_seq_stride;   // elements between sequences
+  const __half* k;          // cache bases (element (seq,pos,head,d) at
+  const __half* v;          //   seq*kv_seq_stride + pos*kv_pos_stride + head*kv_head_stride + d)
+  long long kv_seq_stride, kv_pos_stride, kv_head_stride;
+  const uint32_t* seq_len;  // L per sequence (device)
+  int seq_len_stride;       // uint32 elements between sequences' L
+  uint32_t max_ctx;         // L must be in [1, max_ctx]
+  __half* out;              // [n_seq][1536]
+  long long out_seq_stride;
+  float* part_o;            // scratch: [n_seq][2][max_splits][6][128]
+  float* part_ml;           // scratch: [n_seq][2][max_splits][6][2]
+  uint32_t* counters;       // scratch: [n_seq][2], zero between launches
+  int* err;                 // device error word (may be null)
+};
+int attn_max_splits(int max_ctx, int n_seq);
+size_t attn_scratch_bytes(int max_splits, int n_seq);
+void attn_bind_scratch(AttnParams& p, void* scratch, int max_splits, int n_seq);
+void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st);
+
+// ------------------------------------------------------- op launchers ----
+int launch_gemv_q4_rowmajor(const uint8_t* packed, const __half* scales, const __half* x,
+                            __half* y, const __half* bias, int n_rows, int k, void* stream);
+int launch_gemv_fp16_rowmajor(const __half* w, const __half* x, __half* y, int n_rows, int k,
+                              void* stream);
+int launch_rms_norm(const __half* x, const __half* gamma, __half* out, void* stream);
+int set_rope_inv_freq(const float* inv_freq64);
+int launch_rope(__half* vec, int n_heads, const uint32_t* seq_len, void* stream);
+int launch_write_kv_cache(const __half* k, const __half* v, __half* kc, __half* vc,
+                          const uint32_t* seq_len, uint32_t max_ctx, void* stream);
+int launch_attention_scores(const __half* q, const __half* kc, float* scores,
+                            const uint32_t* seq_len, uint32_t max_seq, void* stream);
+int launch_softmax(float* scores, const uint32_t* seq_len, void* stream);
+int launch_attn_weighted_sum(const float* scores, const __half* vc, __half* out,
+                             const uint32_t* seq_len, void* stream);
+int launch_residual_add(const __half* a, const __half* b, __half* out, int n, void* stream);
+int launch_swiglu(__half* gate, const __half* up, int n, void* stream);
+int launch_dequant_q4(const uint8_t* packed, const __half* scales, size_t n_weights, float* out,
+                      void* stream);
+
+// ------------------------------------------------------------ sampler ----
+// Deterministic sampler (greedy when temperature <= 0).  scratch: see
+// sampler_scratch_bytes.
+size_t sampler_scratch_bytes(int n_seq);
+int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
+                  float top_p, const uint32_t* u24, int32_t* out_ids, void* scratch,
+                  int* err, cudaStream_t st);
+
+// ------------------------------------------------------ weight helpers ----
+int launch_quantize_q4(const float* w, size_t n, uint8_t* packed, __half* scales,
+                       cudaStream_t st);
+// Fills n floats with N(0,1)*stddev + mean from (seed, stream id).
+int launch_fill_normal(float* out, size_t n, uint64_t seed, uint64_t stream_id, float mean,
+                       float stddev, cudaStream_t st);
+int launch_f32_to_f16(const float* in, __half* out, size_t n, cudaStream_t st);
+
+// Host-side helpers.
+uint64_t splitmix64(uint64_t z);
+uint32_t uniform24(uint64_t seed, uint64_t sequence, uint64_t step);
+void rope_inv_freq(float* inv_freq64);
+
+}  // namespace qwen

@@ -1,0 +1,155 @@
+"""QwenEngine: the reference's engine surface (InferenceEngine.swift:9-52) over
+libqwen_b200.so.  Token ids in, token ids out; all arithmetic runs on the GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import (QWEN_KERNELS_FUSED, QWEN_KERNELS_OPS, EngineConfig, check, lib)
+
+STOP_TOKENS = (151645, 151643)  # InferenceEngine.swift:41
+
+
+@dataclass
+class QwenConfig:
+    """QwenConfig.swift:10-22 dimensions plus the runtime options the reference
+    hard-codes (maxContextWindow, sampler defaults of InferenceEngine.swift:273)."""
+
+    hidden_dim: int = 1536
+    mlp_intermediate: int = 8960
+    num_layers: int = 28
+    num_attn_heads: int = 12
+    num_kv_heads: int = 2
+    head_dim: int = 128
+    vocab_size: int = 151936
+    actual_vocab_size: int = 151666
+    max_context_window: int = 1024
+    temperature: float = 0.7
+    top_p: float = 0.8
+    seed: int = 0
+    batch: int = 1
+    device: int = 0
+    kernels: str = "fused"   # "fused" or "ops"
+    stop_on_eos: bool = True
+
+
+class QwenEngine:
+    """QwenEngine (InferenceEngine.swift:9-369).
+
+    QwenEngine(weights_path=...) loads the reference weight directory
+    (WeightLoader.swift); QwenEngine(random_seed=...) builds a random-init model
+    on the device instead."""
+
+    def __init__(self, weights_path: str | None = None, config: QwenConfig | None = None,
+                 random_seed: int | None = None):
+        self.config = config or QwenConfig()
+        c = self.config
+        cfg = EngineConfig()
+        lib().qwen_engine_config_default(ctypes.byref(cfg))
+        cfg.device = c.device
+        cfg.max_ctx = c.max_context_window
+        cfg.batch = c.batch
+        cfg.n_layers = c.num_layers
+        cfg.kernels = {"fused": QWEN_KERNELS_FUSED, "ops": QWEN_KERNELS_OPS}[c.kernels]
+        cfg.temperature = c.temperature
+        cfg.top_p = c.top_p
+        cfg.seed = c.seed
+        cfg.stop_on_eos = 1 if c.stop_on_eos else 0
+        h = ctypes.c_void_p()
+        check(lib().qwen_engine_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self._h = h
+        if weights_path is not None:
+            check(lib().qwen_engine_load_weights(self._h, weights_path.encode()))
+        elif random_seed is not None:
+            check(lib().qwen_engine_init_random(self._h, random_seed))
+
+    # -- lifecycle -----------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qwen_engine_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- the reference surface ---------------------------------------------
+    def forward(self, token_id: int, position: int) -> int:
+        """forward(tokenID:position:) -> next token id (InferenceEngine.swift:54-271)."""
+        out = ctypes.c_int32()
+        check(lib().qwen_engine_forward(self._h, token_id, position, ctypes.byref(out)))
+        return out.value
+
+    def generate(self, prompt_ids, max_tokens: int = 64) -> list:
+        """generate(prompt:maxTokens:) on token ids (InferenceEngine.swift:29-52).
+
+        prompt_ids: [n] (batch 1) or [batch][n].  Returns the generated ids per
+        sequence (a list of lists when batch > 1)."""
+        p = np.ascontiguousarray(prompt_ids, dtype=np.int32)
+        batched = p.ndim == 2
+        if not batched:
+            p = p[None, :]
+        b, n = p.shape
+        out = np.zeros((b, max_tokens), np.int32)
+        n_out = np.zeros(b, np.int32)
+        check(lib().qwen_engine_generate(self._h, p.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                         n, max_tokens,
+                                         out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                         n_out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        res = [out[i, : n_out[i]].tolist() for i in range(b)]
+        return res if batched else res[0]
+
+    def prefill(self, prompt_ids) -> None:
+        p = np.ascontiguousarray(prompt_ids, dtype=np.int32)
+        if p.ndim == 1:
+            p = p[None, :]
+        check(lib().qwen_engine_prefill(self._h, p.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                        p.shape[1]))
+
+    def decode(self, n_steps: int, record: bool = True) -> np.ndarray | None:
+        if not record:
+            check(lib().qwen_engine_decode(self._h, n_steps, None))
+            return None
+        out = np.zeros((self.config.batch, n_steps), np.int32)
+        check(lib().qwen_engine_decode(self._h, n_steps,
+                                       out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return out
+
+    def reset(self) -> None:
+        check(lib().qwen_engine_reset(self._h))
+
+    # -- inspection ------------------------------------------------------------
+    def logits(self, seq: int = 0) -> np.ndarray:
+        out = np.zeros(self.config.vocab_size, np.uint16)
+        check(lib().qwen_engine_get_logits(self._h, seq,
+                                           out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16))))
+        return out.view(np.float16)
+
+    def kv(self, seq: int, layer: int, n_pos: int):
+        k = np.zeros((n_pos, 256), np.uint16)
+        v = np.zeros((n_pos, 256), np.uint16)
+        check(lib().qwen_engine_get_kv(self._h, seq, layer, n_pos,
+                                       k.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)),
+                                       v.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16))))
+        return k.view(np.float16), v.view(np.float16)
+
+    def position(self, seq: int = 0) -> int:
+        out = ctypes.c_int32()
+        check(lib().qwen_engine_position(self._h, seq, ctypes.byref(out)))
+        return out.value
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        check(lib().qwen_engine_stream(self._h, ctypes.byref(s)))
+        return s.value or 0
