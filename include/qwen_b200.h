@@ -196,6 +196,15 @@ int qwen_engine_get_kv(qwen_engine* e, int32_t seq, int32_t layer, int32_t n_pos
 /* Current position (tokens consumed) of sequence `seq`. */
 int qwen_engine_position(qwen_engine* e, int32_t seq, int32_t* position);
 
+/* Kernel launches one decode step makes (all of them this library's). */
+int qwen_engine_kernels_per_step(qwen_engine* e, int32_t* n);
+
+/* Runs n_steps decode steps outside the CUDA graph with CUDA events around
+ * the whole step and around the model kernels (everything between the
+ * embedding gather and the sampler); returns the average milliseconds.
+ * (The reference only times wall clock, main.swift:21-49.) */
+int qwen_engine_time_steps(qwen_engine* e, int32_t n_steps, float* ms_step, float* ms_model);
+
 /* Device and stream the engine runs on (for callers that time it). */
 int qwen_engine_stream(qwen_engine* e, void** stream);
 

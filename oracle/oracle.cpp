@@ -523,6 +523,55 @@ oracle_model* oracle_model_load(const char* dir, int n_layers) {
   return m;
 }
 
+static void fill_normal_f32(std::vector<float>& v, uint64_t seed, float mean, float sd) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)v.size(); i += 2) {
+    const uint64_t r = splitmix64(seed ^ splitmix64((uint64_t)i));
+    const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((r >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);
+    const float rad = std::sqrt(-2.0f * std::log(u1));
+    v[i] = mean + sd * rad * std::cos(6.2831853f * u2);
+    if (i + 1 < (long long)v.size()) v[i + 1] = mean + sd * rad * std::sin(6.2831853f * u2);
+  }
+}
+
+oracle_model* oracle_model_random(int n_layers, uint64_t seed) {
+  auto* m = new oracle_model();
+  m->n_layers = n_layers;
+  uint64_t sid = seed * 1000003ull;
+  auto f16 = [&](std::vector<uint16_t>& dst, size_t n, float mean, float sd) {
+    std::vector<float> tmp(n);
+    fill_normal_f32(tmp, ++sid, mean, sd);
+    dst.resize(n);
+    for (size_t i = 0; i < n; ++i) dst[i] = f2h(tmp[i]);
+  };
+  auto q4 = [&](std::vector<uint8_t>& p, std::vector<uint16_t>& s, size_t rows, size_t k) {
+    std::vector<float> tmp(rows * k);
+    fill_normal_f32(tmp, ++sid, 0.0f, 0.02f);
+    p.resize(rows * k / 2);
+    s.resize(rows * k / 32);
+    oracle_quantize_q4(tmp.data(), tmp.size(), p.data(), s.data());
+  };
+  f16(m->embed, (size_t)kVocab * kHidden, 0.0f, 0.02f);
+  f16(m->final_norm, kHidden, 1.0f, 0.02f);
+  m->layers.resize(n_layers);
+  for (auto& L : m->layers) {
+    f16(L.in_norm, kHidden, 1.0f, 0.02f);
+    f16(L.post_norm, kHidden, 1.0f, 0.02f);
+    q4(L.q, L.qs, kHidden, kHidden);
+    q4(L.k, L.ks, kKVDim, kHidden);
+    q4(L.v, L.vs, kKVDim, kHidden);
+    q4(L.o, L.os, kHidden, kHidden);
+    q4(L.gate, L.gs, kInter, kHidden);
+    q4(L.up, L.us, kInter, kHidden);
+    q4(L.down, L.ds, kHidden, kInter);
+    f16(L.qkv_bias, kHidden + 2 * kKVDim, 0.0f, 0.02f);
+    L.o_bias.assign(kHidden, 0);
+    L.down_bias.assign(kHidden, 0);
+  }
+  return m;
+}
+
 void oracle_model_free(oracle_model* m) { delete m; }
 
 oracle_state* oracle_state_create(const oracle_model* m, int max_ctx) {

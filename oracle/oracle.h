@@ -81,6 +81,9 @@ typedef struct oracle_state oracle_state;
 /* Loads the reference weight directory layout (WeightLoader.swift:49-52,
  * QwenLayer.swift:31-51, QwenModel.swift:25-27). Returns NULL on error. */
 oracle_model* oracle_model_load(const char* dir, int n_layers);
+/* Random-init model in memory (same distributions as the test fixtures, own
+ * generator) for timing the CPU baseline without writing weight files. */
+oracle_model* oracle_model_random(int n_layers, uint64_t seed);
 void oracle_model_free(oracle_model* m);
 oracle_state* oracle_state_create(const oracle_model* m, int max_ctx);
 void oracle_state_free(oracle_state* s);

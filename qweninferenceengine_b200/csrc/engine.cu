@@ -32,8 +32,9 @@ __device__ __forceinline__ uint64_t dsplitmix64(uint64_t z) {
 // embedding row (:57-60) and draw the step's uniform.
 __global__ void k_step_begin(SeqCtl* ctl, const int32_t* prompt, int prompt_stride,
                              const __half* embed, __half* x, uint32_t* u24, int max_ctx,
-                             uint64_t seed, int* err) {
+                             uint64_t seed, int* err, uint32_t* epoch) {
   const int seq = blockIdx.x;
+  if (seq == 0 && threadIdx.x == 0) *epoch += 1;  // tags the fused step's exchanges
   __shared__ int32_t tok;
   if (threadIdx.x == 0) {
     SeqCtl c = ctl[seq];
@@ -111,7 +112,19 @@ void* QwenModel::dev_alloc(size_t bytes, int* rc) {
   return p;
 }
 
+void FusedWeights::release() {
+  void* ps[] = {blob, lm_tiles, norms, qkv_bias, o_bias, down_bias, rope_cs, items, item_begin};
+  for (void* p : ps)
+    if (p) cudaFree(p);
+  blob = lm_tiles = nullptr;
+  norms = qkv_bias = o_bias = down_bias = nullptr;
+  rope_cs = nullptr;
+  items = nullptr;
+  item_begin = nullptr;
+}
+
 QwenModel::~QwenModel() {
+  fused.release();
   for (void* p : allocs_) cudaFree(p);
 }
 
@@ -262,6 +275,7 @@ int InferenceManager::allocate(int b, int nl, int mc, int mo) {
   QWEN_TRY(alloc(B * sizeof(int32_t), (void**)&sampled));
   QWEN_TRY(alloc(B * sizeof(uint32_t) + 64, (void**)&u24_));
   QWEN_TRY(alloc(sizeof(int) * 4, (void**)&err));
+  QWEN_TRY(alloc(sizeof(uint32_t) * 4, (void**)&epoch));
   attn_splits = attn_max_splits(mc, b);
   QWEN_TRY(alloc(attn_scratch_bytes(attn_splits, b), &attn_scratch));
   return QWEN_OK;
@@ -269,6 +283,7 @@ int InferenceManager::allocate(int b, int nl, int mc, int mo) {
 
 // ------------------------------------------------------------ QwenEngine --
 QwenEngine::~QwenEngine() {
+  if (pinned_) cudaFreeHost(pinned_);
   if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
   if (graph_) cudaGraphDestroy(graph_);
   if (stream_) {
@@ -299,6 +314,8 @@ int QwenEngine::init(const qwen_engine_config& cfg) {
   QWEN_CUDA(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, cfg.device),
             "cudaDeviceGetAttribute");
   QWEN_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  QWEN_CUDA(cudaHostAlloc((void**)&pinned_, sizeof(HostStaging), cudaHostAllocDefault), "cudaHostAlloc");
+  std::memset(pinned_, 0, sizeof(HostStaging));
   QWEN_TRY(ensure_rope_table());
   QWEN_TRY(model_.allocate(cfg.n_layers));
   const int max_out = cfg.max_ctx + 1;
@@ -330,14 +347,16 @@ int QwenEngine::reset() {
   return QWEN_OK;
 }
 
-int QwenEngine::enqueue_step_ops() {
+int QwenEngine::enqueue_step_ops(cudaEvent_t* ev) {
   InferenceManager& s = state_;
   QwenModel& m = model_;
   cudaStream_t st = stream_;
   void* vs = st;
   const uint32_t* sl = &s.ctl[0].seq_len;
+  if (ev) cudaEventRecord(ev[0], st);
   k_step_begin<<<s.batch, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, m.embed, s.x, s.u24_,
-                                        s.max_ctx, cfg_.seed, s.err);
+                                        s.max_ctx, cfg_.seed, s.err, s.epoch);
+  if (ev) cudaEventRecord(ev[1], st);
   for (int i = 0; i < m.n_layers; ++i) {
     QwenLayer& L = m.layers[i];
     __half* kc = s.kc + (size_t)i * s.kv_layer_stride();
@@ -363,24 +382,30 @@ int QwenEngine::enqueue_step_ops() {
   }
   launch_rms_norm(s.x, m.final_norm, s.residual, vs);
   launch_gemv_fp16_rowmajor(m.embed, s.residual, s.logits, kVocab, kHidden, vs);
+  if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
                     s.sampled, nullptr, s.err, st) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
+  if (ev) cudaEventRecord(ev[3], st);
   return launch_status("decode step (ops)");
 }
 
-int QwenEngine::enqueue_step_fused() {
+int QwenEngine::enqueue_step_fused(cudaEvent_t* ev) {
   InferenceManager& s = state_;
   cudaStream_t st = stream_;
+  if (ev) cudaEventRecord(ev[0], st);
   k_step_begin<<<s.batch, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
-                                        s.max_ctx, cfg_.seed, s.err);
+                                        s.max_ctx, cfg_.seed, s.err, s.epoch);
+  if (ev) cudaEventRecord(ev[1], st);
   FusedStepArgs a{&model_, &state_, model_.n_layers, sm_count_};
   QWEN_TRY(enqueue_fused_step(a, st));
+  if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
                     s.sampled, nullptr, s.err, st) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
+  if (ev) cudaEventRecord(ev[3], st);
   return launch_status("decode step (fused)");
 }
 
@@ -395,7 +420,7 @@ int QwenEngine::ensure_graph() {
     state_.fused_scratch_bytes = bytes;
   }
   QWEN_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "BeginCapture");
-  const int rc = cfg_.kernels == QWEN_KERNELS_OPS ? enqueue_step_ops() : enqueue_step_fused();
+  const int rc = cfg_.kernels == QWEN_KERNELS_OPS ? enqueue_step_ops(nullptr) : enqueue_step_fused(nullptr);
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamEndCapture(stream_, &g);
   if (rc != QWEN_OK) {
@@ -452,18 +477,59 @@ int QwenEngine::forward(int32_t token, int32_t position, int32_t* next) {
   QWEN_TRY(ensure_graph());
   // One step that reads `token` as a prompt token at `position`; positions
   // past max_ctx-1 reuse the last slot, as InferenceEngine.swift:55 clamps.
-  SeqCtl c{};
-  c.pos = position;
-  c.n_prompt = position + 1;
+  // Inputs and the result travel through pinned host staging.
+  HostStaging* hs = pinned_;
+  std::memset(&hs->ctl, 0, sizeof(hs->ctl));
+  hs->ctl.pos = position;
+  hs->ctl.n_prompt = position + 1;
+  hs->token = token;
   const int slot = std::min(position, state_.max_ctx - 1);
-  QWEN_CUDA(cudaMemcpyAsync(state_.prompt + slot, &token, 4, cudaMemcpyHostToDevice, stream_), "memcpy");
-  QWEN_CUDA(cudaMemcpyAsync(state_.ctl, &c, sizeof(c), cudaMemcpyHostToDevice, stream_), "memcpy");
+  QWEN_CUDA(cudaMemcpyAsync(state_.prompt + slot, &hs->token, 4, cudaMemcpyHostToDevice, stream_), "memcpy");
+  QWEN_CUDA(cudaMemcpyAsync(state_.ctl, &hs->ctl, sizeof(SeqCtl), cudaMemcpyHostToDevice, stream_), "memcpy");
   QWEN_TRY(run_steps(1));
-  int32_t h = 0;
-  QWEN_CUDA(cudaMemcpyAsync(&h, state_.sampled, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
-  QWEN_TRY(check_device_error());
-  *next = h;
+  QWEN_CUDA(cudaMemcpyAsync(&hs->result, state_.sampled, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
+  QWEN_CUDA(cudaMemcpyAsync(&hs->err, state_.err, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
+  QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
+  if (hs->err != 0) QWEN_TRY(check_device_error());
+  *next = hs->result;
   return QWEN_OK;
+}
+
+int QwenEngine::kernels_per_step(int* n) const {
+  // step begin + sampler + step end around the model kernels
+  if (cfg_.kernels == QWEN_KERNELS_OPS)
+    *n = 3 + model_.n_layers * 18 + 2;
+  else
+    *n = 3 + 1;
+  return QWEN_OK;
+}
+
+int QwenEngine::time_steps(int n, float* ms_step, float* ms_model) {
+  if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
+  if (n < 1) return set_error(QWEN_ERR_INVALID_ARGUMENT, "time_steps: n < 1");
+  QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
+  QWEN_TRY(ensure_graph());
+  std::vector<cudaEvent_t> ev(4 * n);
+  for (auto& e : ev) QWEN_CUDA(cudaEventCreate(&e), "cudaEventCreate");
+  int rc = QWEN_OK;
+  for (int i = 0; i < n && rc == QWEN_OK; ++i) {
+    cudaEvent_t* e = &ev[4 * i];
+    rc = cfg_.kernels == QWEN_KERNELS_OPS ? enqueue_step_ops(e) : enqueue_step_fused(e);
+  }
+  if (rc == QWEN_OK) rc = cuda_status(cudaStreamSynchronize(stream_), "sync");
+  double step = 0, model = 0;
+  for (int i = 0; i < n && rc == QWEN_OK; ++i) {
+    float a = 0, b = 0;
+    cudaEventElapsedTime(&a, ev[4 * i], ev[4 * i + 3]);
+    cudaEventElapsedTime(&b, ev[4 * i + 1], ev[4 * i + 2]);
+    step += a;
+    model += b;
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  QWEN_TRY(rc);
+  *ms_step = (float)(step / n);
+  *ms_model = (float)(model / n);
+  return check_device_error();
 }
 
 int QwenEngine::prefill(const int32_t* ids, int32_t n) {
@@ -491,9 +557,10 @@ int QwenEngine::decode(int32_t n_steps, int32_t* out) {
   QWEN_CUDA(cudaMemcpyAsync(c.data(), state_.ctl, sizeof(SeqCtl) * c.size(), cudaMemcpyDeviceToHost,
                             stream_), "memcpy ctl");
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
-  for (auto& x : c)
-    if (x.n_out + n_steps > state_.max_out)
-      return set_error(QWEN_ERR_INVALID_ARGUMENT, "decode: %d more tokens exceed the output buffer", n_steps);
+  if (out)
+    for (auto& x : c)
+      if (x.n_out + n_steps > state_.max_out)
+        return set_error(QWEN_ERR_INVALID_ARGUMENT, "decode: %d more tokens exceed the output buffer", n_steps);
   QWEN_TRY(run_steps(n_steps));
   QWEN_TRY(check_device_error());
   if (out) {
@@ -649,6 +716,19 @@ int qwen_engine_position(qwen_engine* e, int32_t seq, int32_t* pos) {
   ENGINE_OR_FAIL(e);
   if (!pos) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
   return e->impl.position(seq, pos);
+}
+int qwen_engine_kernels_per_step(qwen_engine* e, int32_t* n) {
+  ENGINE_OR_FAIL(e);
+  if (!n) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
+  int v = 0;
+  const int rc = e->impl.kernels_per_step(&v);
+  *n = v;
+  return rc;
+}
+int qwen_engine_time_steps(qwen_engine* e, int32_t n_steps, float* ms_step, float* ms_model) {
+  ENGINE_OR_FAIL(e);
+  if (!ms_step || !ms_model) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
+  return e->impl.time_steps(n_steps, ms_step, ms_model);
 }
 int qwen_engine_stream(qwen_engine* e, void** stream) {
   ENGINE_OR_FAIL(e);

@@ -59,14 +59,21 @@ struct QwenLayer {
 
 // Weights in the layouts the fused decode kernels stream (built from the
 // reference layout on the device; see layout.cu).
+struct FusedItem;
 struct FusedWeights {
-  uint8_t* blob = nullptr;       // all layers' Q4 tiles, phase order
+  uint8_t* blob = nullptr;          // Q4 tiles of every layer, fragment order (fused.h)
   size_t blob_bytes = 0;
-  std::vector<size_t> qkv_off, o_off, gu_off, down_off;  // per layer byte offsets into blob
-  __half* qkv_bias_perm = nullptr;  // [layers][2048] in tile row order
-  __half* lm_tiles = nullptr;       // fp16 LM head in mma tile order
-  float* rope_cs = nullptr;         // [max_ctx][64][2] cos, sin
+  uint8_t* lm_tiles = nullptr;      // fp16 LM head in mma tile order
+  __half* norms = nullptr;          // [layer][2][1536] + final [1536]
+  __half* qkv_bias = nullptr;       // [layer][2048]
+  __half* o_bias = nullptr;         // [layer][1536]
+  __half* down_bias = nullptr;      // [layer][1536]
+  float* rope_cs = nullptr;         // [rope_ctx][64][2] cos, sin
   int rope_ctx = 0;
+  FusedItem* items = nullptr;       // per-CTA work lists
+  uint32_t* item_begin = nullptr;   // [grid + 1]
+  int grid = 0;
+  void release();
 };
 
 // QwenModel.swift:11-35.
@@ -122,6 +129,7 @@ class InferenceManager {
   int32_t* sampled = nullptr;    // [batch]
   uint32_t* u24_ = nullptr;      // [batch] uniforms of the running step
   int* err = nullptr;            // device error word
+  uint32_t* epoch = nullptr;     // step counter (tags of the fused step's exchanges)
   void* attn_scratch = nullptr;
   int attn_splits = 0;
   void* fused_scratch = nullptr;
@@ -150,14 +158,18 @@ class QwenEngine {
   int get_logits(int32_t seq, uint16_t* host);
   int get_kv(int32_t seq, int32_t layer, int32_t n_pos, uint16_t* hk, uint16_t* hv);
   int position(int32_t seq, int32_t* pos);
+  int kernels_per_step(int* n) const;
+  int time_steps(int n, float* ms_step, float* ms_model);
   cudaStream_t stream() const { return stream_; }
 
  private:
   int ensure_graph();
   int run_steps(int n);
   int check_device_error();
-  int enqueue_step_ops();
-  int enqueue_step_fused();
+  // ev (optional, outside capture): events recorded at step start, model
+  // start, model end, step end.
+  int enqueue_step_ops(cudaEvent_t* ev);
+  int enqueue_step_fused(cudaEvent_t* ev);
   int upload_prompt(const int32_t* prompt_ids, int32_t n_prompt, int32_t start_pos);
 
   qwen_engine_config cfg_{};
@@ -168,6 +180,13 @@ class QwenEngine {
   cudaGraph_t graph_ = nullptr;
   bool initialised_ = false;
   int sm_count_ = 0;
+  struct HostStaging {
+    int32_t token;
+    SeqCtl ctl;
+    int32_t result;
+    int32_t err;
+  };
+  HostStaging* pinned_ = nullptr;  // pinned host buffers for forward()
 };
 
 // Fused decode step (decode_fused.cu).

@@ -1,0 +1,253 @@
+// layout.cu -- builds the fused decode step's weight layouts on the device
+// (Q4 fragment-order tiles, fp16 LM-head tiles), the RoPE cos/sin table and
+// the per-CTA work schedule.  See fused.h for the byte layouts.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "engine.h"
+#include "fused.h"
+#include "qwen_common.cuh"
+#include "status.h"
+
+namespace qwen {
+
+#define QWEN_TRY(expr)                  \
+  do {                                  \
+    int _rc = (expr);                   \
+    if (_rc != QWEN_OK) return _rc;     \
+  } while (0)
+#define QWEN_CUDA(expr, what) QWEN_TRY(cuda_status((expr), (what)))
+
+enum RowMap : int { kMapPlain = 0, kMapRopePairs = 1, kMapGateUp = 2 };
+
+// Up to three reference-layout matrices with the same K, concatenated by rows.
+struct Q4Sources {
+  const uint8_t* packed[3];
+  const __half* scales[3];
+  int rows[3];
+};
+
+// Row (in the concatenated row space) of row r (0..15) of tile `tile`.
+//   RopePairs: tile = head*8 + j holds dims 8j..8j+7 (r < 8) and
+//              64+8j..64+8j+7 (r >= 8) of head `head`, so the lane that owns
+//              rows g and g+8 owns a rotate-half pair (rope.metal:21-22).
+//   GateUp:    tile t holds gate rows 8t..8t+7 and up rows 8t..8t+7
+//              (activations.metal:9-27 combines them element-wise).
+__device__ __forceinline__ int tile_row(int map, int tile, int r) {
+  if (map == kMapRopePairs) {
+    const int head = tile >> 3, j = tile & 7;
+    return head * 128 + (r < 8 ? 8 * j + r : 64 + 8 * j + (r - 8));
+  }
+  if (map == kMapGateUp) return r < 8 ? 8 * tile + r : kInter + 8 * tile + (r - 8);
+  return 16 * tile + r;
+}
+
+__device__ __forceinline__ void locate(const Q4Sources& s, int row, int& m, int& local) {
+  m = 0;
+  local = row;
+  while (m < 2 && local >= s.rows[m]) {
+    local -= s.rows[m];
+    ++m;
+  }
+}
+
+__global__ void k_repack_q4(Q4Sources src, int k, int n_tiles, int map, uint8_t* __restrict__ dst) {
+  const int P = k / 64;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)n_tiles * P * 32) return;
+  const int lane = (int)(idx & 31);
+  const long long tp = idx >> 5;
+  const int p = (int)(tp % P), tile = (int)(tp / P);
+  const int g = lane >> 2, t = lane & 3;
+  int mg, lg, mg8, lg8;
+  locate(src, tile_row(map, tile, g), mg, lg);
+  locate(src, tile_row(map, tile, g + 8), mg8, lg8);
+  const size_t rb = (size_t)k / 2;
+  const uint8_t* rowg = src.packed[mg] + (size_t)lg * rb + 4 * t;
+  const uint8_t* rowg8 = src.packed[mg8] + (size_t)lg8 * rb + 4 * t;
+  uint4 w;
+  w.x = *reinterpret_cast<const uint32_t*>(rowg + 16 * (2 * p));
+  w.y = *reinterpret_cast<const uint32_t*>(rowg8 + 16 * (2 * p));
+  w.z = *reinterpret_cast<const uint32_t*>(rowg + 16 * (2 * p + 1));
+  w.w = *reinterpret_cast<const uint32_t*>(rowg8 + 16 * (2 * p + 1));
+  uint8_t* out = dst + ((size_t)tile * P + p) * kBpBytes;
+  reinterpret_cast<uint4*>(out)[lane] = w;
+  if (t == 0) {
+    const int nb = k / 32;
+    const __half* sg = src.scales[mg] + (size_t)lg * nb;
+    const __half* sg8 = src.scales[mg8] + (size_t)lg8 * nb;
+    __half s4[4] = {sg[2 * p], sg8[2 * p], sg[2 * p + 1], sg8[2 * p + 1]};
+    *reinterpret_cast<uint2*>(out + 512 + 8 * g) = *reinterpret_cast<uint2*>(s4);
+  }
+}
+
+__global__ void k_repack_lm(const __half* __restrict__ w, uint8_t* __restrict__ dst) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)kLMTiles * 96 * 32;
+  if (idx >= total) return;
+  const int lane = (int)(idx & 31);
+  const long long ts = idx >> 5;
+  const int s = (int)(ts % 96), tile = (int)(ts / 96);
+  const int g = lane >> 2, t = lane & 3;
+  const uint2 a = *reinterpret_cast<const uint2*>(w + (size_t)(16 * tile + g) * kHidden + 16 * s + 4 * t);
+  const uint2 b = *reinterpret_cast<const uint2*>(w + (size_t)(16 * tile + g + 8) * kHidden + 16 * s + 4 * t);
+  reinterpret_cast<uint4*>(dst + ((size_t)tile * 96 + s) * kLMStepBytes)[lane] = make_uint4(a.x, a.y, b.x, b.y);
+}
+
+static int repack(const Q4Sources& s, int k, int n_tiles, int map, uint8_t* dst, cudaStream_t st) {
+  const long long n = (long long)n_tiles * (k / 64) * 32;
+  k_repack_q4<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s, k, n_tiles, map, dst);
+  return launch_status("repack_q4");
+}
+
+// ------------------------------------------------------------ schedule ----
+// Greedy assignment of every streamed tile of a step to CTAs, balancing the
+// bytes each CTA streams over the whole step.  Phase order per layer:
+// QKV, (attention: no weights), O, gate/up, down; then the LM head.
+static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items,
+                           std::vector<uint32_t>& begin) {
+  std::vector<std::vector<FusedItem>> per(grid);
+  std::vector<double> load(grid, 0.0);
+  auto least = [&](int lo, int hi) {
+    int best = lo;
+    for (int c = lo + 1; c < hi; ++c)
+      if (load[c] < load[best]) best = c;
+    return best;
+  };
+  auto add_tile = [&](int cta, uint16_t phase, int tile, size_t base, int n_k, int chunk_k,
+                      int unit_bytes) {
+    const uint16_t seq = (uint16_t)std::count_if(per[cta].begin(), per[cta].end(), [&](const FusedItem& it) {
+      return it.phase == phase && it.k0 == 0;
+    });
+    for (int k0 = 0; k0 < n_k; k0 += chunk_k) {
+      const int nk = std::min(chunk_k, n_k - k0);
+      FusedItem it{};
+      it.src = base + (size_t)k0 * unit_bytes;
+      it.bytes = (uint32_t)(nk * unit_bytes);
+      it.phase = phase;
+      it.tile = (uint16_t)tile;
+      it.k0 = (uint16_t)k0;
+      it.nk = (uint16_t)nk;
+      it.last = (uint16_t)(k0 + nk >= n_k);
+      it.seq = seq;
+      per[cta].push_back(it);
+      load[cta] += it.bytes;
+    }
+  };
+  for (int l = 0; l < n_layers; ++l) {
+    const size_t lb = (size_t)l * kLayerBlobBytes;
+    const uint16_t ph = (uint16_t)(l * kPhasesPerLayer);
+    // QKV: the first 128 CTAs, one tile each (attention units use the last CTAs).
+    for (int t = 0; t < kQKVTiles; ++t)
+      add_tile(t % grid, ph + kPhQKV, t, lb + kLayerQKVOff + (size_t)t * kTile1536Bytes, kBp1536,
+               kBp1536, kBpBytes);
+    for (int t = 0; t < kOTiles; ++t)
+      add_tile(least(0, grid), ph + kPhO, t, lb + kLayerOOff + (size_t)t * kTile1536Bytes,
+               kBp1536, kBp1536, kBpBytes);
+    for (int t = 0; t < kGUTiles; ++t)
+      add_tile(least(0, grid), ph + kPhGU, t, lb + kLayerGUOff + (size_t)t * kTile1536Bytes,
+               kBp1536, kBp1536, kBpBytes);
+    for (int t = 0; t < kDownTiles; ++t)
+      add_tile(least(0, grid), ph + kPhDown, t, lb + kLayerDownOff + (size_t)t * kTile8960Bytes,
+               kBp8960, kDownChunkBp, kBpBytes);
+  }
+  const uint16_t lm_phase = (uint16_t)(n_layers * kPhasesPerLayer);
+  for (int t = 0; t < kLMTiles; ++t)
+    add_tile(least(0, grid), lm_phase, t, (size_t)t * kLMTileBytes, 96, kLMChunkSteps, kLMStepBytes);
+  items.clear();
+  begin.assign(grid + 1, 0);
+  for (int c = 0; c < grid; ++c) {
+    begin[c] = (uint32_t)items.size();
+    items.insert(items.end(), per[c].begin(), per[c].end());
+  }
+  begin[grid] = (uint32_t)items.size();
+}
+
+int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
+  FusedWeights& f = m.fused;
+  auto alloc = [&](void** p, size_t bytes) { return cuda_status(cudaMalloc(p, bytes), "cudaMalloc(fused)"); };
+  if (!f.blob) {
+    f.blob_bytes = (size_t)m.n_layers * kLayerBlobBytes;
+    QWEN_TRY(alloc((void**)&f.blob, f.blob_bytes));
+    QWEN_TRY(alloc((void**)&f.lm_tiles, (size_t)kLMTiles * kLMTileBytes));
+    QWEN_TRY(alloc((void**)&f.norms, ((size_t)m.n_layers * 2 + 1) * kHidden * 2));
+    QWEN_TRY(alloc((void**)&f.qkv_bias, (size_t)m.n_layers * kQKVRows * 2));
+    QWEN_TRY(alloc((void**)&f.o_bias, (size_t)m.n_layers * kHidden * 2));
+    QWEN_TRY(alloc((void**)&f.down_bias, (size_t)m.n_layers * kHidden * 2));
+  }
+  for (int l = 0; l < m.n_layers; ++l) {
+    const QwenLayer& L = m.layers[l];
+    uint8_t* lb = f.blob + (size_t)l * kLayerBlobBytes;
+    Q4Sources qkv{{L.q.packed, L.k.packed, L.v.packed}, {L.q.scales, L.k.scales, L.v.scales},
+                  {kHidden, kKVDim, kKVDim}};
+    QWEN_TRY(repack(qkv, kHidden, kQKVTiles, kMapRopePairs, lb + kLayerQKVOff, st));
+    Q4Sources o{{L.o.packed, nullptr, nullptr}, {L.o.scales, nullptr, nullptr}, {kHidden, 0, 0}};
+    QWEN_TRY(repack(o, kHidden, kOTiles, kMapPlain, lb + kLayerOOff, st));
+    Q4Sources gu{{L.gate.packed, L.up.packed, nullptr}, {L.gate.scales, L.up.scales, nullptr},
+                 {kInter, kInter, 0}};
+    QWEN_TRY(repack(gu, kHidden, kGUTiles, kMapGateUp, lb + kLayerGUOff, st));
+    Q4Sources dn{{L.down.packed, nullptr, nullptr}, {L.down.scales, nullptr, nullptr}, {kHidden, 0, 0}};
+    QWEN_TRY(repack(dn, kInter, kDownTiles, kMapPlain, lb + kLayerDownOff, st));
+    QWEN_CUDA(cudaMemcpyAsync(f.norms + (size_t)(2 * l) * kHidden, L.input_norm, kHidden * 2,
+                              cudaMemcpyDeviceToDevice, st), "memcpy");
+    QWEN_CUDA(cudaMemcpyAsync(f.norms + (size_t)(2 * l + 1) * kHidden, L.post_attn_norm, kHidden * 2,
+                              cudaMemcpyDeviceToDevice, st), "memcpy");
+    QWEN_CUDA(cudaMemcpyAsync(f.qkv_bias + (size_t)l * kQKVRows, L.qkv_bias, kQKVRows * 2,
+                              cudaMemcpyDeviceToDevice, st), "memcpy");
+    QWEN_CUDA(cudaMemcpyAsync(f.o_bias + (size_t)l * kHidden, L.o_bias, kHidden * 2,
+                              cudaMemcpyDeviceToDevice, st), "memcpy");
+    QWEN_CUDA(cudaMemcpyAsync(f.down_bias + (size_t)l * kHidden, L.down_bias, kHidden * 2,
+                              cudaMemcpyDeviceToDevice, st), "memcpy");
+  }
+  QWEN_CUDA(cudaMemcpyAsync(f.norms + (size_t)(2 * m.n_layers) * kHidden, m.final_norm, kHidden * 2,
+                            cudaMemcpyDeviceToDevice, st), "memcpy");
+  {
+    const long long n = (long long)kLMTiles * 96 * 32;
+    k_repack_lm<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(m.embed, f.lm_tiles);
+    QWEN_TRY(launch_status("repack_lm"));
+  }
+  // RoPE cos/sin per position: theta = pos * 1e6^(-2i/128) in fp32 with libm,
+  // exactly as rope.metal:25-32 evaluates it.
+  if (f.rope_ctx < max_ctx) {
+    if (f.rope_cs) cudaFree(f.rope_cs);
+    f.rope_cs = nullptr;
+    QWEN_TRY(alloc((void**)&f.rope_cs, (size_t)max_ctx * 128 * sizeof(float)));
+    f.rope_ctx = max_ctx;
+  }
+  {
+    float inv[64];
+    rope_inv_freq(inv);
+    std::vector<float> cs((size_t)max_ctx * 128);
+    for (int pos = 0; pos < max_ctx; ++pos)
+      for (int i = 0; i < 64; ++i) {
+        const float theta = (float)pos * inv[i];
+        cs[(size_t)pos * 128 + 2 * i] = std::cos(theta);
+        cs[(size_t)pos * 128 + 2 * i + 1] = std::sin(theta);
+      }
+    QWEN_CUDA(cudaMemcpyAsync(f.rope_cs, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice, st),
+              "memcpy rope");
+    QWEN_CUDA(cudaStreamSynchronize(st), "sync");
+  }
+  // Work schedule for the current device's SM count.
+  int dev = 0, sms = 0;
+  QWEN_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  QWEN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "attr");
+  std::vector<FusedItem> items;
+  std::vector<uint32_t> begin;
+  build_schedule(m.n_layers, sms, items, begin);
+  if (f.items) cudaFree(f.items);
+  if (f.item_begin) cudaFree(f.item_begin);
+  f.items = nullptr;
+  f.item_begin = nullptr;
+  QWEN_TRY(alloc((void**)&f.items, items.size() * sizeof(FusedItem)));
+  QWEN_TRY(alloc((void**)&f.item_begin, begin.size() * sizeof(uint32_t)));
+  QWEN_CUDA(cudaMemcpy(f.items, items.data(), items.size() * sizeof(FusedItem), cudaMemcpyHostToDevice), "memcpy");
+  QWEN_CUDA(cudaMemcpy(f.item_begin, begin.data(), begin.size() * sizeof(uint32_t), cudaMemcpyHostToDevice), "memcpy");
+  f.grid = sms;
+  QWEN_CUDA(cudaStreamSynchronize(st), "sync");
+  return QWEN_OK;
+}
+
+}  // namespace qwen

@@ -149,6 +149,17 @@ class QwenEngine:
         check(lib().qwen_engine_position(self._h, seq, ctypes.byref(out)))
         return out.value
 
+    def kernels_per_step(self) -> int:
+        out = ctypes.c_int32()
+        check(lib().qwen_engine_kernels_per_step(self._h, ctypes.byref(out)))
+        return out.value
+
+    def time_steps(self, n_steps: int):
+        """(ms per step, ms in the model kernels) averaged over n_steps, CUDA events."""
+        a, b = ctypes.c_float(), ctypes.c_float()
+        check(lib().qwen_engine_time_steps(self._h, n_steps, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
+
     def stream(self) -> int:
         s = ctypes.c_void_p()
         check(lib().qwen_engine_stream(self._h, ctypes.byref(s)))

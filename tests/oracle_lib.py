@@ -146,6 +146,8 @@ class Oracle(_Kernels):
         L.oracle_model_load.argtypes = [ctypes.c_char_p, ctypes.c_int]
         L.oracle_model_load.restype = ctypes.c_void_p
         L.oracle_model_free.argtypes = [ctypes.c_void_p]
+        L.oracle_model_random.argtypes = [ctypes.c_int, ctypes.c_uint64]
+        L.oracle_model_random.restype = ctypes.c_void_p
         L.oracle_state_create.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.oracle_state_create.restype = ctypes.c_void_p
         L.oracle_state_free.argtypes = [ctypes.c_void_p]
@@ -199,10 +201,14 @@ class Oracle(_Kernels):
 class OracleModel:
     """Whole-model oracle over a reference-layout weight directory."""
 
-    def __init__(self, oracle: Oracle, weights_dir: str, n_layers: int, max_ctx: int):
+    def __init__(self, oracle: Oracle, weights_dir: str | None, n_layers: int, max_ctx: int,
+                 random_seed: int = 0):
         self.o = oracle
         self.n_layers = n_layers
-        self.m = oracle.lib.oracle_model_load(weights_dir.encode(), n_layers)
+        if weights_dir is None:
+            self.m = oracle.lib.oracle_model_random(n_layers, random_seed)
+        else:
+            self.m = oracle.lib.oracle_model_load(weights_dir.encode(), n_layers)
         if not self.m:
             raise FileNotFoundError(f"oracle could not load {weights_dir}")
         self.s = oracle.lib.oracle_state_create(self.m, max_ctx)
