@@ -278,17 +278,24 @@ int attn_max_splits(int max_ctx, int n_seq) {
   return s < cap ? s : cap;
 }
 
+// Scratch layout: the merge tickets first, at a fixed offset, so that calls
+// with different split counts find them where the last call left them (zero);
+// then the per-split (m, l) pairs and the per-split partial outputs.
+static size_t attn_ticket_bytes(int n_seq) {
+  return ((size_t)n_seq * kKVHeads * sizeof(uint32_t) + 255) / 256 * 256;
+}
+
 size_t attn_scratch_bytes(int max_splits, int n_seq) {
   const size_t units = (size_t)n_seq * kKVHeads;
-  return units * max_splits * (6 * kHeadDim + 12) * sizeof(float) + units * sizeof(uint32_t);
+  return attn_ticket_bytes(n_seq) + units * max_splits * (6 * kHeadDim + 12) * sizeof(float);
 }
 
 void attn_bind_scratch(AttnParams& p, void* scratch, int max_splits, int n_seq) {
   const size_t units = (size_t)n_seq * kKVHeads;
-  float* f = reinterpret_cast<float*>(scratch);
-  p.part_o = f;
-  p.part_ml = f + units * max_splits * (6 * kHeadDim);
-  p.counters = reinterpret_cast<uint32_t*>(p.part_ml + units * max_splits * 12);
+  uint8_t* base = reinterpret_cast<uint8_t*>(scratch);
+  p.counters = reinterpret_cast<uint32_t*>(base);
+  p.part_ml = reinterpret_cast<float*>(base + attn_ticket_bytes(n_seq));
+  p.part_o = p.part_ml + units * max_splits * 12;
 }
 
 void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st) {

@@ -12,6 +12,5 @@ int fused_scratch_bytes(int, int, int, size_t* bytes) {
 int enqueue_fused_step(const FusedStepArgs&, cudaStream_t) {
   return set_error(QWEN_ERR_STATE, "fused decode path not built in this library");
 }
-int build_fused_weights(QwenModel&, int, cudaStream_t) { return QWEN_OK; }
 
 }  // namespace qwen
