@@ -95,6 +95,21 @@ int qwen_attention_decode(const uint16_t* q, const uint16_t* k_cache, const uint
                           uint16_t* out, const uint32_t* seq_len, uint32_t max_ctx,
                           void* stream);
 
+/* qwen_attention_decode without any device allocation.  No counterpart in the
+ * reference (it has no allocation-free entry points): this is for callers that
+ * may not call cudaMalloc -- code running while another component holds a
+ * stream in global capture mode, latency-critical threads that must stay out
+ * of the CUDA allocator, plugins in hosts that own the whole memory pool.
+ * Same arguments and results as qwen_attention_decode.  Its scratch is a fixed
+ * 1 MiB device array inside this library (held on every GPU that loads it until
+ * exit); requests needing more are rejected with QWEN_ERR_INVALID_ARGUMENT.
+ * All calls on a device share that array: calls that overlap on the GPU race,
+ * so serialise them.  The first call on a device resolves the array's address
+ * and should come before any stream capture. */
+int qwen_attention_decode_noalloc(const uint16_t* q, const uint16_t* k_cache,
+                                  const uint16_t* v_cache, uint16_t* out,
+                                  const uint32_t* seq_len, uint32_t max_ctx, void* stream);
+
 /* (q-8)*scale for n_weights weights, low nibble first (matmul.metal:37-42). */
 int qwen_dequant_q4(const uint8_t* packed, const uint16_t* scales, size_t n_weights,
                     float* out, void* stream);
