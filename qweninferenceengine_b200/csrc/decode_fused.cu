@@ -1,16 +1,922 @@
-// decode_fused.cu -- the fused decode step (placeholder until the persistent
-// kernel lands): reports that the fused path is unavailable.
+// decode_fused.cu -- the whole decode step (28 layers + final norm + LM head)
+// as one persistent kernel, one CTA per SM.
+//
+// Replaces the 506 dispatches of InferenceEngine.swift:103-264 per token.
+//
+// Roles inside a CTA (288 threads):
+//   warp 8      producer: streams this CTA's share of every weight byte of the
+//               step, in consumption order, into a ring of shared-memory slots
+//               with TMA bulk copies (cp.async.bulk + mbarrier transaction
+//               counts).  Weights do not depend on activations, so streaming
+//               runs ahead across the dependency waits of the consumers.
+//   warps 0..7  consumers: Q4 dequant + m16n8k16 MMA GEMVs on the slots, with
+//               fused prologues (RMSNorm) and epilogues (bias, RoPE, KV-cache
+//               write, SwiGLU, residual add), and the split-K attention.
+//
+// Cross-CTA data (x, q, new k/v, attention partials and output, the SwiGLU
+// output h) travels as tagged words: a 32-bit word holds the fp16 value and a
+// 16-bit tag of (step, write instance); a reader polls until every word it
+// needs carries the expected tag.  Value and tag share one single-copy-atomic
+// store, so no fences or grid barriers are needed and each dependency costs
+// one L2 round trip.  Every wait is bounded; on timeout the kernel records
+// QWEN_ERR_DEVICE_TIMEOUT, skips the remaining work (keeping every named
+// barrier in step) and drains its in-flight copies before exiting.
+//
+// Rounding points follow the reference: q/k/v, o, gate/up, down outputs and
+// logits are rounded to fp16 (matmul.metal:71,111), RoPE re-rounds q/k
+// (rope.metal:37-38), the residual adds are fp16 adds (attention.metal:64),
+// RMSNorm rounds twice (rmsnorm.metal:44), SwiGLU rounds once
+// (activations.metal:26) and the attention output once (attention.metal:55).
+#include <algorithm>
+#include <cstring>
+
 #include "engine.h"
+#include "fused.h"
+#include "qwen_common.cuh"
 #include "status.h"
 
 namespace qwen {
 
-int fused_scratch_bytes(int, int, int, size_t* bytes) {
-  *bytes = 0;
-  return set_error(QWEN_ERR_STATE, "fused decode path not built in this library");
+namespace {
+
+constexpr int kNS = 14;                    // ring slots
+constexpr int kUnionBytes = 20480;         // x fragments (<= 17920 B) / attention buffers
+constexpr uint64_t kWaitNs = 2000000000ull;  // a wait gives up after 2 s
+
+constexpr int kOffUnion = kNS * kSlotBytes;
+constexpr int kOffXloc = kOffUnion + kUnionBytes;
+constexpr int kOffXn = kOffXloc + kHidden * 2;
+constexpr int kOffRed = kOffXn + kHidden * 2;
+constexpr int kOffRed2 = kOffRed + kConsumerWarps * 16 * 4;
+constexpr int kOffBars = kOffRed2 + 64;
+constexpr int kOffMisc = kOffBars + 2 * kNS * 8;
+constexpr int kSmemBytes = kOffMisc + 64 + 64;
+
+// attention buffers inside the union region
+constexpr int kAVs = 0;                                   // [4][16][272] V rows
+constexpr int kAPt = kAVs + kAttnWarpsFused * 16 * 272;   // [4][2][16*8] P^T hi/lo
+constexpr int kAWm = kAPt + kAttnWarpsFused * 2 * 128 * 2;
+constexpr int kAWl = kAWm + kAttnWarpsFused * 8 * 4;
+constexpr int kAKnew = kAWl + kAttnWarpsFused * 8 * 4;    // [128] fp16 new k
+constexpr int kAVnew = kAKnew + 256;                      // [128] fp16 new v
+static_assert(kAVnew + 256 <= kUnionBytes, "attention buffers exceed the union region");
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kAttnWarpsFused * 6 * 128 * 4 <= kAPt, "warp merge buffer aliases the V rows");
+
+struct Misc {
+  int abort;
+  int issued;
+  float scale;
+  int cphase;           // phase the consumers are in (diagnostics)
+  int last_rel[8];      // last item index each consumer warp released (diagnostics)
+};
+
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void abar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t cnt) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(cnt)
+               : "memory");
 }
-int enqueue_fused_step(const FusedStepArgs&, cudaStream_t) {
-  return set_error(QWEN_ERR_STATE, "fused decode path not built in this library");
+
+// ---------------------------------------------------------- tagged words --
+__device__ __forceinline__ void st_tag16(uint32_t* p, uint16_t tag, __half v) {
+  const uint32_t w = ((uint32_t)tag << 16) | (uint32_t)hbits(v);
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+}
+__device__ __forceinline__ uint4 ld_tag4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_tag32(unsigned long long* p, uint16_t tag, float v) {
+  const unsigned long long w =
+      ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tag64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool tags_ok(const uint4& v, uint32_t tag) {
+  return (v.x >> 16) == tag && (v.y >> 16) == tag && (v.z >> 16) == tag && (v.w >> 16) == tag;
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool aborted(volatile Misc* m, const int* err) {
+  return m->abort != 0 || *((volatile const int*)err) != 0;
+}
+// Records the timeout and where it happened: err[1] = site, err[2] = CTA,
+// err[3] = thread (the first failure wins).
+__device__ __forceinline__ void fail(volatile Misc* m, int* err, int site) {
+  m->abort = 1;
+  if (err && atomicCAS(err, 0, kDevWaitTimeout) == 0) {
+    err[1] = site;
+    err[2] = blockIdx.x;
+    err[3] = threadIdx.x;
+  }
+}
+// Wait sites (x 100 + layer) reported by fail().
+enum WaitSite : int {
+  kSiteEmpty = 1, kSiteFull = 2, kSiteXIn = 3, kSiteQ = 4, kSiteKV = 5, kSiteCombine = 6,
+  kSiteAttnOut = 7, kSiteXMid = 8, kSiteH = 9, kSiteXFinal = 10
+};
+
+// Polls units of 8 consecutive tagged fp16 words: unit u covers words
+// [8u, 8u+8).  Thread `tid` of `nthr` owns units tid, tid+nthr, ... (at most
+// MAXU).  f(u, v[8]) receives each unit once all its tags match.
+template <int MAXU, class F>
+__device__ __forceinline__ void poll_units(const uint32_t* src, int n_units, int tid, int nthr,
+                                           uint32_t tag, volatile Misc* m, int* err, int site, F f) {
+  uint32_t pending = 0;
+  uint64_t t0 = 0;
+#pragma unroll
+  for (int j = 0; j < MAXU; ++j)
+    if (tid + j * nthr < n_units) pending |= 1u << j;
+  for (uint32_t it = 0; pending; ++it) {
+    uint4 a[MAXU], b[MAXU];
+#pragma unroll
+    for (int j = 0; j < MAXU; ++j)
+      if (pending & (1u << j)) {
+        const uint32_t* p = src + 8 * (tid + j * nthr);
+        a[j] = ld_tag4(p);
+        b[j] = ld_tag4(p + 4);
+      }
+#pragma unroll
+    for (int j = 0; j < MAXU; ++j)
+      if ((pending & (1u << j)) && tags_ok(a[j], tag) && tags_ok(b[j], tag)) {
+        __half v[8];
+        const uint32_t w[8] = {a[j].x, a[j].y, a[j].z, a[j].w, b[j].x, b[j].y, b[j].z, b[j].w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = __ushort_as_half((unsigned short)(w[q] & 0xFFFFu));
+        f(tid + j * nthr, v);
+        pending &= ~(1u << j);
+      }
+    if (!pending) break;
+    if ((it & 63) == 0) {
+      if (aborted(m, err)) return;
+      const uint64_t now = globaltimer();
+      if (it == 0) t0 = now;
+      else if (now - t0 > kWaitNs) {
+        fail(m, err, site);
+        return;
+      }
+    }
+    __nanosleep(it < 32 ? 20 : 200);
+  }
+}
+
+__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volatile Misc* m,
+                                          int* err, int site) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (aborted(m, err)) return false;
+      const uint64_t now = globaltimer();
+      if (it == 0) t0 = now;
+      else if (now - t0 > kWaitNs) {
+        fail(m, err, site);
+        return false;
+      }
+    }
+  }
+}
+
+// Waits for item i of this CTA's list to land in its ring slot.  A slot's
+// mbarrier only tells the current phase from the previous one, so a warp
+// that runs ahead (one that owns every 8th tile) first waits until the
+// producer has issued item i -- from then on the slot's current phase is
+// item i's and the parity wait is exact.
+__device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile Misc* m, int* err,
+                                          int site) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0; m->issued <= i; ++it) {
+    if ((it & 63) == 0) {
+      if (aborted(m, err)) return false;
+      const uint64_t now = globaltimer();
+      if (it == 0) t0 = now;
+      else if (now - t0 > kWaitNs) {
+        fail(m, err, site);
+        return false;
+      }
+    }
+    __nanosleep(32);
+  }
+  return slot_wait(&full[i % kNS], (i / kNS) & 1, m, err, site);
+}
+
+__device__ __forceinline__ int it_phase_of(const FusedItem* items, int i) { return items[i].phase; }
+
+__device__ __forceinline__ float silu_ref(float x) {
+  if (x > 15.0f) return x;
+  if (x < -15.0f) return 0.0f;
+  return x / (1.0f + expf(-x));
+}
+
+// RMSNorm of xloc (rmsnorm.metal:9-46): out = half(half(x * s) * gamma).
+// Writes Q4 x fragments (frags) and/or plain fp16 (plain).  256 consumer threads.
+__device__ void rmsnorm_out(const __half* xloc, const __half* __restrict__ gamma, float* red2,
+                            volatile Misc* misc, uint4* frags, __half* plain, int ct) {
+  float ss = 0.f;
+  for (int i = ct; i < kHidden; i += 256) {
+    const float v = h2f(xloc[i]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((ct & 31) == 0) red2[ct >> 5] = ss;
+  cbar();
+  if (ct == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) tot += red2[w];
+    misc->scale = 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
+  }
+  cbar();
+  const float s = misc->scale;
+  for (int u = ct; u < kHidden / 8; u += 256) {
+    __half v[8];
+    const uint4 raw = reinterpret_cast<const uint4*>(xloc)[u];
+    const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gamma) + u);
+    const __half* xv = reinterpret_cast<const __half*>(&raw);
+    const __half* gv = reinterpret_cast<const __half*>(&graw);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = __hmul(f2h(h2f(xv[q]) * s), gv[q]);
+    if (frags) frags[u] = make_xfrag(v);
+    if (plain) reinterpret_cast<uint4*>(plain)[u] = *reinterpret_cast<uint4*>(v);
+  }
+  cbar();
+}
+
+// Block pairs b = b_begin, b_begin + b_step, ... < b_end of a Q4 slot whose
+// first block pair is k0 of its tile, for the lane's rows g and g+8.
+__device__ __forceinline__ void q4_chunk(const uint8_t* slot, int k0, int b_begin, int b_end,
+                                         int b_step, const uint4* xf, int lane, float& acc_g,
+                                         float& acc_g8) {
+  const int g = lane >> 2, t = lane & 3;
+  for (int b = b_begin; b < b_end; b += b_step) {
+    const uint8_t* bp = slot + b * kBpBytes;
+    const uint4 wv = *reinterpret_cast<const uint4*>(bp + lane * 16);
+    const uint2 sv = *reinterpret_cast<const uint2*>(bp + 512 + g * 8);
+    const int gp = k0 + b;
+    const uint4 x0 = xf[(2 * gp) * 4 + t];
+    const uint4 x1 = xf[(2 * gp + 1) * 4 + t];
+    float d[4];
+    q4_block_mma(wv.x, wv.y, x0, d);
+    const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
+    acc_g = fmaf(s0.x, d[0], acc_g);
+    acc_g8 = fmaf(s0.y, d[2], acc_g8);
+    q4_block_mma(wv.z, wv.w, x1, d);
+    const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
+    acc_g = fmaf(s1.x, d[0], acc_g);
+    acc_g8 = fmaf(s1.y, d[2], acc_g8);
+  }
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+// Split-K attention of one (kv head, split) unit by consumer warps 0..3 (the
+// arithmetic of k_attention_decode), then the combine of this unit's slice of
+// the 768 outputs of its kv head from every split's partial.
+__device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, uint32_t S_eff,
+                               uint32_t chunk, uint32_t L, uint16_t tag, uint8_t* uni, __half* qs,
+                               volatile Misc* misc, int ct) {
+  const int warp = ct >> 5, lane = ct & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t p0 = s * chunk, p1 = min(L, p0 + chunk);
+  const uint32_t last = L - 1;
+  const bool has_new = last >= p0 && last < p1;
+  __half* knew = reinterpret_cast<__half*>(uni + kAKnew);
+  __half* vnew = reinterpret_cast<__half*>(uni + kAVnew);
+  // q of the 6 heads of this kv group, and the step's new k / v rows.
+  poll_units<1>(p.q_ll + kvh * 768, 96, ct, 128, tag, misc, p.err, kSiteQ * 100 + layer, [&](int u, const __half* v) {
+    reinterpret_cast<uint4*>(qs)[u] = *reinterpret_cast<const uint4*>(v);
+  });
+  if (has_new) {
+    poll_units<1>(p.kv_ll, 64, ct, 128, tag, misc, p.err, kSiteKV * 100 + layer, [&](int u, const __half* v) {
+      const int w0 = 8 * u;  // words 0..255 = k, 256..511 = v
+      if (((w0 & 255) >> 7) != kvh) return;
+      __half* dst = (w0 < 256 ? knew : vnew) + (w0 & 127);
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(v);
+    });
+  }
+  abar();
+  const __half* kbase = p.kc + (size_t)layer * p.kv_layer_stride + kvh * kHeadDim;
+  const __half* vbase = p.vc + (size_t)layer * p.kv_layer_stride + kvh * kHeadDim;
+  uint32_t qf[16];
+  {
+    const uint4* qp = reinterpret_cast<const uint4*>(qs + (g < 6 ? g : 0) * kHeadDim + 32 * t);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = g < 6 ? qp[j] : make_uint4(0, 0, 0, 0);
+      qf[4 * j] = v.x;
+      qf[4 * j + 1] = v.y;
+      qf[4 * j + 2] = v.z;
+      qf[4 * j + 3] = v.w;
+    }
+  }
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  uint8_t* vs = uni + kAVs + warp * (16 * 272);
+  uint16_t* pth = reinterpret_cast<uint16_t*>(uni + kAPt) + warp * 256;
+  uint16_t* ptl = pth + 128;
+  for (uint32_t base = p0 + warp * 16; base < p1; base += kAttnWarpsFused * 16) {
+    {
+      const int r = lane >> 1, hs = lane & 1;
+      const uint32_t pos = base + r;
+      uint4* dst = reinterpret_cast<uint4*>(vs + r * 272 + hs * 128);
+      if (pos < p1) {
+        const uint4* src =
+            pos == last ? reinterpret_cast<const uint4*>(vnew) + hs * 8
+                        : reinterpret_cast<const uint4*>(vbase + (size_t)pos * kKVDim) + hs * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[j] = src[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const uint32_t pg = min(base + g, p1 - 1), pg8 = min(base + g + 8, p1 - 1);
+      const uint4* sg = pg == last
+                            ? reinterpret_cast<const uint4*>(knew + 32 * t)
+                            : reinterpret_cast<const uint4*>(kbase + (size_t)pg * kKVDim + 32 * t);
+      const uint4* sg8 = pg8 == last
+                             ? reinterpret_cast<const uint4*>(knew + 32 * t)
+                             : reinterpret_cast<const uint4*>(kbase + (size_t)pg8 * kKVDim + 32 * t);
+      uint32_t kg[16], kg8[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 a = sg[j], b = sg8[j];
+        kg[4 * j] = a.x; kg[4 * j + 1] = a.y; kg[4 * j + 2] = a.z; kg[4 * j + 3] = a.w;
+        kg8[4 * j] = b.x; kg8[4 * j + 1] = b.y; kg8[4 * j + 2] = b.z; kg8[4 * j + 3] = b.w;
+      }
+#pragma unroll
+      for (int st = 0; st < 8; ++st) {
+        const uint32_t a[4] = {kg[2 * st], kg8[2 * st], kg[2 * st + 1], kg8[2 * st + 1]};
+        mma_16816(sc, a, qf[2 * st], qf[2 * st + 1], sc);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[j] *= kAttnScale;
+      if (base + g >= p1) sc[0] = sc[1] = -INFINITY;
+      if (base + g + 8 >= p1) sc[2] = sc[3] = -INFINITY;
+    }
+    float pr[4];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float mx = fmaxf(sc[hh], sc[2 + hh]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m_run[hh], mx);
+      const float corr = m_run[hh] == -INFINITY ? 0.f : expf(m_run[hh] - m_new);
+      const float e0 = expf(sc[hh] - m_new), e1 = expf(sc[2 + hh] - m_new);
+      pr[hh] = e0;
+      pr[2 + hh] = e1;
+      float sum = e0 + e1;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+      l_run[hh] = l_run[hh] * corr + sum;
+      m_run[hh] = m_new;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][hh] *= corr;
+        o[i][2 + hh] *= corr;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int pos = g + (j >= 2 ? 8 : 0), head = 2 * t + (j & 1);
+      const __half h = f2h(pr[j]);
+      pth[pos * 8 + head] = hbits(h);
+      ptl[pos * 8 + head] = hbits(f2h(pr[j] - h2f(h)));
+    }
+    __syncwarp();
+    const uint32_t bh0 = (uint32_t)pth[(2 * t) * 8 + g] | ((uint32_t)pth[(2 * t + 1) * 8 + g] << 16);
+    const uint32_t bh1 = (uint32_t)pth[(2 * t + 8) * 8 + g] | ((uint32_t)pth[(2 * t + 9) * 8 + g] << 16);
+    const uint32_t bl0 = (uint32_t)ptl[(2 * t) * 8 + g] | ((uint32_t)ptl[(2 * t + 1) * 8 + g] << 16);
+    const uint32_t bl1 = (uint32_t)ptl[(2 * t + 8) * 8 + g] | ((uint32_t)ptl[(2 * t + 9) * 8 + g] << 16);
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int prow = ri + ((mi >> 1) << 3), dcol = (mi & 1) << 3;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t a[4];
+        ldmatrix_x4_trans(a, vs + prow * 272 + (16 * i + dcol) * 2);
+        mma_16816(o[i], a, bh0, bh1, o[i]);
+        mma_16816(o[i], a, bl0, bl1, o[i]);
+      }
+    }
+    __syncwarp();
+  }
+  // ---- merge the 4 warps (shared memory), write this split's partial.
+  float* wm = reinterpret_cast<float*>(uni + kAWm);
+  float* wl = reinterpret_cast<float*>(uni + kAWl);
+  if (g == 0) {
+    wm[warp * 8 + 2 * t] = m_run[0];
+    wm[warp * 8 + 2 * t + 1] = m_run[1];
+    wl[warp * 8 + 2 * t] = l_run[0];
+    wl[warp * 8 + 2 * t + 1] = l_run[1];
+  }
+  abar();  // every warp is done with its V rows: reuse them for the merge
+  float* wo = reinterpret_cast<float*>(uni + kAVs);  // [4][6][128]
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int head = 2 * t + (j & 1), d = 16 * i + g + (j >= 2 ? 8 : 0);
+      if (head < 6) wo[(warp * 6 + head) * kHeadDim + d] = o[i][j];
+    }
+  abar();
+  unsigned long long* part = p.attn_part + ((size_t)kvh * kMaxAttnSplits + s) * kAttnPartWords;
+  for (int idx = ct; idx < 6 * kHeadDim; idx += 128) {
+    const int head = idx / kHeadDim, d = idx % kHeadDim;
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarpsFused; ++w) M = fmaxf(M, wm[w * 8 + head]);
+    float Ls = 0.f, O = 0.f;
+    for (int w = 0; w < kAttnWarpsFused; ++w) {
+      const float mw = wm[w * 8 + head];
+      if (mw == -INFINITY) continue;
+      const float c = expf(mw - M);
+      Ls += wl[w * 8 + head] * c;
+      O += wo[(w * 6 + head) * kHeadDim + d] * c;
+    }
+    st_tag32(part + idx, tag, O);
+    if (d == 0) {
+      st_tag32(part + 768 + head, tag, M);
+      st_tag32(part + 774 + head, tag, Ls);
+    }
+  }
+  abar();
+  // ---- combine: this unit produces outputs [z0, z1) of its kv head.
+  const uint32_t Z = (768 + S_eff - 1) / S_eff;
+  const uint32_t z0 = min(768u, s * Z), z1 = min(768u, z0 + Z);
+  if (z0 >= z1) return;
+  const int h0 = z0 / kHeadDim, h1 = (z1 - 1) / kHeadDim;
+  const uint32_t nh = h1 - h0 + 1;
+  const uint32_t nz = z1 - z0;
+  const uint32_t per_split = nz + 2 * nh;  // o slice, m[nh], l[nh]
+  float* stage = reinterpret_cast<float*>(uni + kAVs);
+  const uint32_t n_words = S_eff * per_split;
+  for (uint32_t w0 = ct; w0 < n_words; w0 += 128 * 8) {
+    unsigned long long v[8];
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (w0 + j * 128 < n_words) pending |= 1u << j;
+    uint64_t t0 = 0;
+    for (uint32_t it = 0; pending; ++it) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (pending & (1u << j)) {
+          const uint32_t w = w0 + j * 128, sp = w / per_split, r = w % per_split;
+          uint32_t word;
+          if (r < nz) word = z0 + r;
+          else if (r < nz + nh) word = 768 + h0 + (r - nz);
+          else word = 774 + h0 + (r - nz - nh);
+          v[j] = ld_tag64(p.attn_part + ((size_t)kvh * kMaxAttnSplits + sp) * kAttnPartWords + word);
+        }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if ((pending & (1u << j)) && (uint32_t)(v[j] >> 32) == tag) {
+          stage[w0 + j * 128] = __uint_as_float((uint32_t)v[j]);
+          pending &= ~(1u << j);
+        }
+      if (!pending) break;
+      if ((it & 63) == 0) {
+        if (aborted(misc, p.err)) break;
+        const uint64_t now = globaltimer();
+        if (it == 0) t0 = now;
+        else if (now - t0 > kWaitNs) {
+          fail(misc, p.err, kSiteCombine * 100 + layer);
+          break;
+        }
+      }
+      __nanosleep(it < 32 ? 20 : 200);
+    }
+  }
+  abar();
+  for (uint32_t z = z0 + ct; z < z1; z += 128) {
+    const uint32_t hl = z / kHeadDim - h0;
+    float M = -INFINITY;
+    for (uint32_t sp = 0; sp < S_eff; ++sp) M = fmaxf(M, stage[sp * per_split + nz + hl]);
+    float Ls = 0.f, O = 0.f;
+    for (uint32_t sp = 0; sp < S_eff; ++sp) {
+      const float c = expf(stage[sp * per_split + nz + hl] - M);
+      Ls += stage[sp * per_split + nz + nh + hl] * c;
+      O += stage[sp * per_split + (z - z0)] * c;
+    }
+    st_tag16(p.attn_ll + kvh * 768 + z, tag, f2h(O / Ls));
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint8_t* uni = smem + kOffUnion;
+  __half* xloc = reinterpret_cast<__half*>(smem + kOffXloc);
+  __half* xn = reinterpret_cast<__half*>(smem + kOffXn);
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* red2 = reinterpret_cast<float*>(smem + kOffRed2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  uint64_t* empty = full + kNS;
+  volatile Misc* misc = reinterpret_cast<volatile Misc*>(smem + kOffMisc);
+  uint4* xf = reinterpret_cast<uint4*>(uni);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ib = p.item_begin[blockIdx.x];
+  const int n_items = (int)(p.item_begin[blockIdx.x + 1] - ib);
+  const FusedItem* items = p.items + ib;
+  const uint16_t lm_phase = (uint16_t)(p.n_layers * kPhasesPerLayer);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
+    misc->abort = 0;
+    misc->issued = 0;
+    misc->cphase = -1;
+    for (int w = 0; w < 8; ++w) misc->last_rel[w] = -1;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int i = 0;
+      for (; i < n_items; ++i) {
+        const int slot = i % kNS;
+        const uint32_t par = ((i / kNS) & 1) ^ 1;
+        if (!slot_wait(&empty[slot], par, misc, p.err, kSiteEmpty * 100 + (it_phase_of(items, i) % 100))) {
+          if (p.err[2] == (int)blockIdx.x && p.err[3] == (int)threadIdx.x) {
+            p.err[4] = i;
+            p.err[5] = n_items;
+            p.err[6] = misc->cphase;
+            for (int w = 0; w < 8; ++w) p.err[7 + w] = misc->last_rel[w];
+          }
+          break;
+        }
+        const FusedItem it = items[i];
+        const uint8_t* src = (it.phase == lm_phase ? p.lm : p.q4) + it.src;
+        mbar_arrive_expect_tx(&full[slot], it.bytes);
+        bulk_g2s_stream(ring + slot * kSlotBytes, src, it.bytes, &full[slot], pol);
+        misc->issued = i + 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int ct = threadIdx.x;
+    const uint32_t L = p.seq_ctl[3];       // SeqCtl.seq_len
+    const int token = (int)p.seq_ctl[4];   // SeqCtl.token
+    const uint32_t epoch = *p.epoch;
+    auto tagof = [&](uint32_t k) { return (uint32_t)((epoch << 8) + k) & 0xFFFFu; };
+    const int g = lane >> 2, t = lane & 3;
+    int cur = 0;
+    auto phase_end = [&](uint16_t ph) {
+      int e = cur;
+      while (e < n_items && items[e].phase == ph) ++e;
+      return e;
+    };
+    // K-split processing of items [cur, e): warp w takes block pairs w, w+8, ...
+    // of every chunk; the tile's 16 sums meet in shared memory at its last chunk.
+    auto ksplit = [&](int e, auto&& epilogue) {
+      float acc_g = 0.f, acc_g8 = 0.f;
+      for (int i = cur; i < e; ++i) {
+        const FusedItem it = items[i];
+        const int slot = i % kNS;
+        if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100))
+          q4_chunk(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
+                   acc_g8);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty[slot]);
+          misc->last_rel[warp] = i;
+        }
+        if (it.last) {
+          if (t == 0) {
+            red[warp * 16 + g] = acc_g;
+            red[warp * 16 + g + 8] = acc_g8;
+          }
+          acc_g = acc_g8 = 0.f;
+          cbar();
+          if (ct < 16) {
+            float sum = 0.f;
+            for (int w = 0; w < kConsumerWarps; ++w) sum += red[w * 16 + ct];
+            epilogue(it.tile, ct, sum);
+          }
+          cbar();
+        }
+      }
+      cur = e;
+    };
+    const float* rope = p.rope_cs + (size_t)(L - 1) * 128;
+
+    for (int layer = 0; layer < p.n_layers; ++layer) {
+      const uint16_t ph = (uint16_t)(layer * kPhasesPerLayer);
+      if (ct == 0) misc->cphase = ph * 1000 + cur;
+      // ---- x after the previous layer (or the embedding row, :57-60)
+      if (layer == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.embed + (size_t)token * kHidden);
+        for (int u = ct; u < kHidden / 8; u += 256) reinterpret_cast<uint4*>(xloc)[u] = src[u];
+      } else {
+        poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * layer), misc, p.err,
+                      kSiteXIn * 100 + layer, [&](int u, const __half* v) {
+                        reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
+                      });
+      }
+      cbar();
+      // ---- P1: RMSNorm -> QKV -> bias -> RoPE -> q, KV cache
+      {
+        const int e = phase_end(ph + kPhQKV);
+        if (e > cur) {
+          rmsnorm_out(xloc, p.norms + (size_t)(2 * layer) * kHidden, red2, misc, xf, nullptr, ct);
+          const uint16_t tg = (uint16_t)tagof(layer);
+          __half* kc = p.kc + (size_t)layer * p.kv_layer_stride + (size_t)(L - 1) * kKVDim;
+          __half* vc = p.vc + (size_t)layer * p.kv_layer_stride + (size_t)(L - 1) * kKVDim;
+          const __half* bias = p.qkv_bias + (size_t)layer * kQKVRows;
+          // threads 0..15 hold the tile's 16 rows; rows r and r+8 form a RoPE pair
+          ksplit(e, [&](int tile, int r, float sum) {
+            const int head = tile >> 3, j = tile & 7;
+            const int row = head * 128 + (r < 8 ? 8 * j + r : 64 + 8 * j + (r - 8));
+            red2[r] = h2f(f2h(sum + h2f(bias[row])));
+            __syncwarp(0xffffu);
+            if (r >= 8) return;
+            const float x1 = red2[r], x2 = red2[r + 8];
+            const int i = 8 * j + r;  // rotate-half pair index (rope.metal:17-22)
+            __half o1, o2;
+            if (head < 14) {
+              const float c = rope[2 * i], sn = rope[2 * i + 1];
+              o1 = f2h(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
+              o2 = f2h(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, c)));
+            } else {
+              o1 = f2h(x1);
+              o2 = f2h(x2);
+            }
+            const int d1 = 8 * j + r, d2 = 64 + 8 * j + r;
+            if (head < 12) {
+              st_tag16(p.q_ll + head * 128 + d1, tg, o1);
+              st_tag16(p.q_ll + head * 128 + d2, tg, o2);
+            } else if (head < 14) {
+              const int kh = head - 12;
+              kc[kh * 128 + d1] = o1;
+              kc[kh * 128 + d2] = o2;
+              st_tag16(p.kv_ll + kh * 128 + d1, tg, o1);
+              st_tag16(p.kv_ll + kh * 128 + d2, tg, o2);
+            } else {
+              const int vh = head - 14;
+              vc[vh * 128 + d1] = o1;
+              vc[vh * 128 + d2] = o2;
+              st_tag16(p.kv_ll + 256 + vh * 128 + d1, tg, o1);
+              st_tag16(p.kv_ll + 256 + vh * 128 + d2, tg, o2);
+            }
+          });
+        }
+      }
+      // ---- P2: attention units on the last CTAs
+      {
+        uint32_t S = (L + 127) / 128;
+        const uint32_t cap = min((uint32_t)kMaxAttnSplits, gridDim.x / 2);
+        S = max(1u, min(S, cap));
+        uint32_t chunk = (L + S - 1) / S;
+        chunk = (chunk + 15) / 16 * 16;
+        const uint32_t S_eff = (L + chunk - 1) / chunk;
+        const int u = (int)gridDim.x - 1 - (int)blockIdx.x;
+        if (u < (int)(2 * S_eff) && warp < kAttnWarpsFused)
+          attention_unit(p, layer, u & 1, u >> 1, S_eff, chunk, L, (uint16_t)tagof(layer), uni,
+                         xn, misc, ct);
+      }
+      cbar();
+      // ---- P3: O projection + bias + residual (attention.metal:58-65)
+      {
+        const int e = phase_end(ph + kPhO);
+        if (e > cur) {
+          poll_units<1>(p.attn_ll, kHidden / 8, ct, 256, tagof(layer), misc, p.err,
+                        kSiteAttnOut * 100 + layer, [&](int u, const __half* v) {
+                          __half tmp[8];
+#pragma unroll
+                          for (int q = 0; q < 8; ++q) tmp[q] = v[q];
+                          xf[u] = make_xfrag(tmp);
+                        });
+          cbar();
+          const __half* ob = p.o_bias + (size_t)layer * kHidden;
+          const uint16_t tg = (uint16_t)tagof(2 * layer + 1);
+          ksplit(e, [&](int tile, int r, float sum) {
+            const int row = 16 * tile + r;
+            const __half o = f2h(sum + h2f(ob[row]));
+            st_tag16(p.x_ll + row, tg, __hadd(xloc[row], o));
+          });
+        }
+      }
+      // ---- P4: x -> RMSNorm -> gate|up -> SwiGLU -> h (each warp owns whole tiles)
+      poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * layer + 1), misc, p.err,
+                    kSiteXMid * 100 + layer, [&](int u, const __half* v) {
+                      reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
+                    });
+      cbar();
+      {
+        const int e = phase_end(ph + kPhGU);
+        rmsnorm_out(xloc, p.norms + (size_t)(2 * layer + 1) * kHidden, red2, misc, xf, nullptr, ct);
+        const uint16_t tg = (uint16_t)tagof(layer);
+        for (int i = cur; i < e; ++i) {
+          const FusedItem it = items[i];
+          if ((it.seq & (kConsumerWarps - 1)) != warp) continue;
+          const int slot = i % kNS;
+          float acc_g = 0.f, acc_g8 = 0.f;
+          if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100))
+            q4_chunk(ring + slot * kSlotBytes, it.k0, 0, it.nk, 1, xf, lane, acc_g, acc_g8);
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_cnt(&empty[slot], kConsumerWarps);
+            misc->last_rel[warp] = i;
+          }
+          if (t == 0) {
+            // gate and up with the zero bias of InferenceEngine.swift:82-85, then
+            // half(silu(gate) * up) (activations.metal:14-26)
+            const __half gate = f2h(acc_g + 0.0f), up = f2h(acc_g8 + 0.0f);
+            st_tag16(p.h_ll + 8 * it.tile + g, tg, f2h(silu_ref(h2f(gate)) * h2f(up)));
+          }
+        }
+        cur = e;
+      }
+      cbar();
+      // ---- P5: h -> down -> bias -> residual
+      {
+        const int e = phase_end(ph + kPhDown);
+        if (e > cur) {
+          poll_units<5>(p.h_ll, kInter / 8, ct, 256, tagof(layer), misc, p.err,
+                        kSiteH * 100 + layer, [&](int u, const __half* v) {
+                          __half tmp[8];
+#pragma unroll
+                          for (int q = 0; q < 8; ++q) tmp[q] = v[q];
+                          xf[u] = make_xfrag(tmp);
+                        });
+          cbar();
+          const __half* db = p.down_bias + (size_t)layer * kHidden;
+          const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
+          ksplit(e, [&](int tile, int r, float sum) {
+            const int row = 16 * tile + r;
+            const __half d = f2h(sum + h2f(db[row]));
+            st_tag16(p.x_ll + row, tg, __hadd(xloc[row], d));
+          });
+        }
+      }
+      cbar();
+    }
+    // ---- final RMSNorm + LM head (each warp owns whole 16-row tiles)
+    if (ct == 0) misc->cphase = lm_phase * 1000 + cur;
+    poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * p.n_layers), misc, p.err,
+                  kSiteXFinal * 100, [&](int u, const __half* v) {
+                    reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
+                  });
+    cbar();
+    rmsnorm_out(xloc, p.norms + (size_t)(2 * p.n_layers) * kHidden, red2, misc, nullptr, xn, ct);
+    {
+      const int e = phase_end(lm_phase);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int i = cur; i < e; ++i) {
+        const FusedItem it = items[i];
+        if ((it.seq & (kConsumerWarps - 1)) != warp) continue;
+        const int slot = i % kNS;
+        if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100)) {
+          const uint8_t* sb = ring + slot * kSlotBytes;
+          for (int s = 0; s < it.nk; ++s) {
+            const uint4 w = *reinterpret_cast<const uint4*>(sb + s * kLMStepBytes + lane * 16);
+            const uint2 b = *reinterpret_cast<const uint2*>(xn + 16 * (it.k0 + s) + 4 * t);
+            const uint32_t a[4] = {w.x, w.z, w.y, w.w};
+            mma_16816(d, a, b.x, b.y, d);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_cnt(&empty[slot], kConsumerWarps);
+          misc->last_rel[warp] = i;
+        }
+        if (it.last) {
+          if (t == 0) {
+            p.logits[16 * it.tile + g] = f2h(d[0]);
+            p.logits[16 * it.tile + g + 8] = f2h(d[2]);
+          }
+          d[0] = d[1] = d[2] = d[3] = 0.f;
+        }
+      }
+      cur = e;
+    }
+  }
+  __syncthreads();
+  // Drain: every copy this CTA issued has landed before its shared memory goes away.
+  if (threadIdx.x == 0) {
+    const int issued = misc->issued;
+    const uint64_t t0 = globaltimer();
+    for (int i = max(0, issued - kNS); i < issued; ++i)
+      while (!mbar_try_wait(&full[i % kNS], (i / kNS) & 1))
+        if (globaltimer() - t0 > kWaitNs) break;
+  }
+}
+
+// ------------------------------------------------------------------ host --
+namespace {
+struct FusedScratchLayout {
+  size_t x_ll, q_ll, kv_ll, attn_part, attn_ll, h_ll, total;
+};
+FusedScratchLayout fused_layout() {
+  FusedScratchLayout l{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += (bytes + 255) / 256 * 256;
+    return at;
+  };
+  l.x_ll = take(kHidden * 4);
+  l.q_ll = take(kHidden * 4);
+  l.kv_ll = take(512 * 4);
+  l.attn_part = take((size_t)2 * kMaxAttnSplits * kAttnPartWords * 8);
+  l.attn_ll = take(kHidden * 4);
+  l.h_ll = take(kInter * 4);
+  l.total = o;
+  return l;
+}
+}  // namespace
+
+int fused_scratch_bytes(int batch, int, int, size_t* bytes) {
+  if (batch != 1)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "the fused decode step decodes one sequence");
+  *bytes = fused_layout().total;
+  return QWEN_OK;
+}
+
+int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
+  const QwenModel& m = *a.model;
+  InferenceManager& s = *a.state;
+  const FusedWeights& f = m.fused;
+  if (!f.blob || !f.items) return set_error(QWEN_ERR_STATE, "fused weights not built");
+  if (s.batch != 1)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "the fused decode step decodes one sequence");
+  if (f.rope_ctx < s.max_ctx) return set_error(QWEN_ERR_STATE, "RoPE table shorter than max_ctx");
+  static_assert(sizeof(SeqCtl) == 32, "SeqCtl layout read by the fused kernel");
+  const FusedScratchLayout lay = fused_layout();
+  uint8_t* sc = reinterpret_cast<uint8_t*>(s.fused_scratch);
+  FusedParams p{};
+  p.q4 = f.blob;
+  p.lm = f.lm_tiles;
+  p.embed = m.embed;
+  p.norms = f.norms;
+  p.qkv_bias = f.qkv_bias;
+  p.o_bias = f.o_bias;
+  p.down_bias = f.down_bias;
+  p.rope_cs = f.rope_cs;
+  p.items = f.items;
+  p.item_begin = f.item_begin;
+  p.seq_ctl = reinterpret_cast<const uint32_t*>(s.ctl);
+  p.epoch = s.epoch;
+  p.kc = s.kc;
+  p.vc = s.vc;
+  p.x_ll = reinterpret_cast<uint32_t*>(sc + lay.x_ll);
+  p.q_ll = reinterpret_cast<uint32_t*>(sc + lay.q_ll);
+  p.kv_ll = reinterpret_cast<uint32_t*>(sc + lay.kv_ll);
+  p.attn_part = reinterpret_cast<unsigned long long*>(sc + lay.attn_part);
+  p.attn_ll = reinterpret_cast<uint32_t*>(sc + lay.attn_ll);
+  p.h_ll = reinterpret_cast<uint32_t*>(sc + lay.h_ll);
+  p.logits = s.logits;
+  p.err = s.err;
+  p.n_layers = m.n_layers;
+  p.max_ctx = s.max_ctx;
+  p.kv_layer_stride = (int)s.kv_layer_stride();
+  if (int rc = cuda_status(cudaFuncSetAttribute(k_decode_fused,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kSmemBytes),
+                           "cudaFuncSetAttribute(k_decode_fused)"))
+    return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(f.grid);
+  cfg.blockDim = dim3(kFusedThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k_decode_fused, p), "launch k_decode_fused");
 }
 
 }  // namespace qwen

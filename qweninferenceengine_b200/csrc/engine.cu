@@ -274,7 +274,7 @@ int InferenceManager::allocate(int b, int nl, int mc, int mo) {
   QWEN_TRY(alloc(B * mo * sizeof(int32_t), (void**)&out_tokens));
   QWEN_TRY(alloc(B * sizeof(int32_t), (void**)&sampled));
   QWEN_TRY(alloc(B * sizeof(uint32_t) + 64, (void**)&u24_));
-  QWEN_TRY(alloc(sizeof(int) * 4, (void**)&err));
+  QWEN_TRY(alloc(sizeof(int) * 32, (void**)&err));
   QWEN_TRY(alloc(sizeof(uint32_t) * 4, (void**)&epoch));
   attn_splits = attn_max_splits(mc, b);
   QWEN_TRY(alloc(attn_scratch_bytes(attn_splits, b), &attn_scratch));
@@ -434,18 +434,19 @@ int QwenEngine::ensure_graph() {
 }
 
 int QwenEngine::check_device_error() {
-  int h = 0;
-  QWEN_CUDA(cudaMemcpyAsync(&h, state_.err, sizeof(int), cudaMemcpyDeviceToHost, stream_), "memcpy err");
+  int h[16] = {0};
+  QWEN_CUDA(cudaMemcpyAsync(h, state_.err, sizeof(h), cudaMemcpyDeviceToHost, stream_), "memcpy err");
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
-  if (h == kDevWaitTimeout) {
-    cudaMemsetAsync(state_.err, 0, sizeof(int), stream_);
-    return set_error(QWEN_ERR_DEVICE_TIMEOUT, "a device-side wait timed out");
-  }
-  if (h != 0) {
-    cudaMemsetAsync(state_.err, 0, sizeof(int), stream_);
-    return set_error(QWEN_ERR_INVALID_ARGUMENT, "device reported a bad argument (token id or length)");
-  }
-  return QWEN_OK;
+  if (h[0] == 0) return QWEN_OK;
+  cudaMemsetAsync(state_.err, 0, sizeof(h), stream_);
+  cudaStreamSynchronize(stream_);
+  if (h[0] == kDevWaitTimeout)
+    return set_error(QWEN_ERR_DEVICE_TIMEOUT,
+                     "a device-side wait timed out (site %d, phase %d, CTA %d, thread %d; "
+                     "detail %d %d %d | %d %d %d %d %d %d %d %d)",
+                     h[1] / 100, h[1] % 100, h[2], h[3], h[4], h[5], h[6], h[7], h[8], h[9], h[10],
+                     h[11], h[12], h[13], h[14]);
+  return set_error(QWEN_ERR_INVALID_ARGUMENT, "device reported a bad argument (token id or length)");
 }
 
 int QwenEngine::run_steps(int n) {
@@ -490,7 +491,7 @@ int QwenEngine::forward(int32_t token, int32_t position, int32_t* next) {
   QWEN_CUDA(cudaMemcpyAsync(&hs->result, state_.sampled, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
   QWEN_CUDA(cudaMemcpyAsync(&hs->err, state_.err, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
-  if (hs->err != 0) QWEN_TRY(check_device_error());
+  if (hs->err != 0) return check_device_error();
   *next = hs->result;
   return QWEN_OK;
 }

@@ -73,7 +73,8 @@ struct FusedParams {
   const float* rope_cs;       // [max_ctx][64][2]
   const FusedItem* items;
   const uint32_t* item_begin; // [grid + 1]
-  const uint32_t* seq_ctl;    // SeqCtl of the sequence (read: pos, token, seq_len, epoch)
+  const uint32_t* seq_ctl;    // SeqCtl of the sequence (read: seq_len, token)
+  const uint32_t* epoch;      // step counter (tags of this step's exchanges)
   __half* kc;                 // [layer][max_ctx][256] (reference layout)
   __half* vc;
   uint32_t* x_ll;             // [1536]  tagged fp16 words
