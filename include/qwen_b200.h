@@ -220,6 +220,18 @@ int qwen_engine_kernels_per_step(qwen_engine* e, int32_t* n);
  * (The reference only times wall clock, main.swift:21-49.) */
 int qwen_engine_time_steps(qwen_engine* e, int32_t n_steps, float* ms_step, float* ms_model);
 
+/* Fused-step tracing (the reference has none; main.swift:21-49 prints wall
+ * clock only).  When enabled, every CTA of the fused step kernel records
+ * %globaltimer stamps: [0] producer start, [1] producer done, [2] consumer
+ * start, then 10 per layer at [3 + 10*layer + k]: k = 0 layer start, 1 x ready,
+ * 2 QKV done, 3 attention done, 4 attention output ready, 5 O done, 6 gate/up
+ * input ready, 7 gate/up done, 8 h ready, 9 down done; then LM-head start and
+ * consumer end; stride 3 + 10*n_layers + 2 per CTA.
+ * qwen_engine_get_trace copies the last step's stamps ([grid][stride]) when
+ * n >= *needed, and always reports *needed. */
+int qwen_engine_trace(qwen_engine* e, int32_t enable);
+int qwen_engine_get_trace(qwen_engine* e, uint64_t* host, size_t n, size_t* needed);
+
 /* Device and stream the engine runs on (for callers that time it). */
 int qwen_engine_stream(qwen_engine* e, void** stream);
 

@@ -78,6 +78,9 @@ SIGNATURES = {
     "qwen_engine_position": (c_int, [c_void_p, c_int32, _i32p]),
     "qwen_engine_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "qwen_engine_kernels_per_step": (c_int, [c_void_p, _i32p]),
+    "qwen_engine_trace": (c_int, [c_void_p, c_int32]),
+    "qwen_engine_get_trace": (c_int, [c_void_p, ctypes.POINTER(c_uint64), c_size_t,
+                                      ctypes.POINTER(c_size_t)]),
     "qwen_engine_time_steps": (c_int, [c_void_p, c_int32, ctypes.POINTER(c_float),
                                        ctypes.POINTER(c_float)]),
 }

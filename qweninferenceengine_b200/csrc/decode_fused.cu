@@ -40,7 +40,9 @@ namespace qwen {
 namespace {
 
 constexpr int kNS = 14;                    // ring slots
-constexpr int kUnionBytes = 20480;         // x fragments (<= 17920 B) / attention buffers
+constexpr int kUnionBytes = 20480;         // x fragments + corrections / attention buffers
+constexpr int kMaxXFrags = kInter / 8;     // 1120 fragment units (K = 8960)
+static_assert(kMaxXFrags * 16 <= kUnionBytes, "x fragments exceed the union");
 constexpr uint64_t kWaitNs = 2000000000ull;  // a wait gives up after 2 s
 
 constexpr int kOffUnion = kNS * kSlotBytes;
@@ -50,7 +52,8 @@ constexpr int kOffRed = kOffXn + kHidden * 2;
 constexpr int kOffRed2 = kOffRed + kConsumerWarps * 16 * 4;
 constexpr int kOffBars = kOffRed2 + 64;
 constexpr int kOffMisc = kOffBars + 2 * kNS * 8;
-constexpr int kSmemBytes = kOffMisc + 64 + 64;
+constexpr int kOffItems = kOffMisc + 128;
+constexpr int kSmemBytes = kOffItems + kMaxItemsPerCta * 8;
 
 // attention buffers inside the union region
 constexpr int kAVs = 0;                                   // [4][16][272] V rows
@@ -171,7 +174,7 @@ __device__ __forceinline__ void poll_units(const uint32_t* src, int n_units, int
         return;
       }
     }
-    __nanosleep(it < 32 ? 20 : 200);
+    __nanosleep(32);
   }
 }
 
@@ -215,7 +218,9 @@ __device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile Misc* 
   return slot_wait(&full[i % kNS], (i / kNS) & 1, m, err, site);
 }
 
-__device__ __forceinline__ int it_phase_of(const FusedItem* items, int i) { return items[i].phase; }
+__device__ __forceinline__ int it_phase_of(const FusedItem* items, int i) {
+  return (int)(items[i] & 0xFF);
+}
 
 __device__ __forceinline__ float silu_ref(float x) {
   if (x > 15.0f) return x;
@@ -225,7 +230,7 @@ __device__ __forceinline__ float silu_ref(float x) {
 
 // RMSNorm of xloc (rmsnorm.metal:9-46): out = half(half(x * s) * gamma).
 // Writes Q4 x fragments (frags) and/or plain fp16 (plain).  256 consumer threads.
-__device__ void rmsnorm_out(const __half* xloc, const __half* __restrict__ gamma, float* red2,
+__device__ __forceinline__ void rmsnorm_out(const __half* xloc, const __half* __restrict__ gamma, float* red2,
                             volatile Misc* misc, uint4* frags, __half* plain, int ct) {
   float ss = 0.f;
   for (int i = ct; i < kHidden; i += 256) {
@@ -257,28 +262,40 @@ __device__ void rmsnorm_out(const __half* xloc, const __half* __restrict__ gamma
 }
 
 // Block pairs b = b_begin, b_begin + b_step, ... < b_end of a Q4 slot whose
-// first block pair is k0 of its tile, for the lane's rows g and g+8.
+// first block pair is k0 of its tile, for the lane's rows g and g+8.  Two
+// block pairs per iteration keep four independent MMA chains in flight.
+__device__ __forceinline__ void q4_bp(const uint8_t* slot, int k0, int b, const uint4* xf, int lane,
+                                      float& ag, float& ag8) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* bp = slot + b * kBpBytes;
+  const uint4 wv = *reinterpret_cast<const uint4*>(bp + lane * 16);
+  const uint2 sv = *reinterpret_cast<const uint2*>(bp + 512 + g * 8);
+  const int gp = k0 + b;
+  const uint4 x0 = xf[(2 * gp) * 4 + t];
+  const uint4 x1 = xf[(2 * gp + 1) * 4 + t];
+  float d0[4], d1[4];
+  q4_block_mma(wv.x, wv.y, x0, d0);
+  q4_block_mma(wv.z, wv.w, x1, d1);
+  const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
+  const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
+  ag = fmaf(s0.x, d0[0], ag);
+  ag8 = fmaf(s0.y, d0[2], ag8);
+  ag = fmaf(s1.x, d1[0], ag);
+  ag8 = fmaf(s1.y, d1[2], ag8);
+}
+
 __device__ __forceinline__ void q4_chunk(const uint8_t* slot, int k0, int b_begin, int b_end,
                                          int b_step, const uint4* xf, int lane, float& acc_g,
                                          float& acc_g8) {
-  const int g = lane >> 2, t = lane & 3;
-  for (int b = b_begin; b < b_end; b += b_step) {
-    const uint8_t* bp = slot + b * kBpBytes;
-    const uint4 wv = *reinterpret_cast<const uint4*>(bp + lane * 16);
-    const uint2 sv = *reinterpret_cast<const uint2*>(bp + 512 + g * 8);
-    const int gp = k0 + b;
-    const uint4 x0 = xf[(2 * gp) * 4 + t];
-    const uint4 x1 = xf[(2 * gp + 1) * 4 + t];
-    float d[4];
-    q4_block_mma(wv.x, wv.y, x0, d);
-    const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
-    acc_g = fmaf(s0.x, d[0], acc_g);
-    acc_g8 = fmaf(s0.y, d[2], acc_g8);
-    q4_block_mma(wv.z, wv.w, x1, d);
-    const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
-    acc_g = fmaf(s1.x, d[0], acc_g);
-    acc_g8 = fmaf(s1.y, d[2], acc_g8);
+  float ga = 0.f, g8a = 0.f, gb = 0.f, g8b = 0.f;
+  int b = b_begin;
+  for (; b + b_step < b_end; b += 2 * b_step) {
+    q4_bp(slot, k0, b, xf, lane, ga, g8a);
+    q4_bp(slot, k0, b + b_step, xf, lane, gb, g8b);
   }
+  if (b < b_end) q4_bp(slot, k0, b, xf, lane, ga, g8a);
+  acc_g += ga + gb;
+  acc_g8 += g8a + g8b;
 }
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
@@ -290,15 +307,63 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
 // Split-K attention of one (kv head, split) unit by consumer warps 0..3 (the
 // arithmetic of k_attention_decode), then the combine of this unit's slice of
 // the 768 outputs of its kv head from every split's partial.
-__device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, uint32_t S_eff,
+__device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, uint32_t S_eff,
                                uint32_t chunk, uint32_t L, uint16_t tag, uint8_t* uni, __half* qs,
-                               volatile Misc* misc, int ct) {
+                               volatile Misc* misc, int ct, unsigned long long* at) {
+  auto astamp = [&](int k) {
+    if (at && layer == 14 && ct == 0) at[k] = globaltimer();
+  };
+  astamp(0);
   const int warp = ct >> 5, lane = ct & 31, g = lane >> 2, t = lane & 3;
   const uint32_t p0 = s * chunk, p1 = min(L, p0 + chunk);
   const uint32_t last = L - 1;
   const bool has_new = last >= p0 && last < p1;
   __half* knew = reinterpret_cast<__half*>(uni + kAKnew);
   __half* vnew = reinterpret_cast<__half*>(uni + kAVnew);
+  const __half* kbase = p.kc + (size_t)layer * p.kv_layer_stride + kvh * kHeadDim;
+  const __half* vbase = p.vc + (size_t)layer * p.kv_layer_stride + kvh * kHeadDim;
+  uint8_t* vs = uni + kAVs + warp * (16 * 272);
+  uint16_t* pth = reinterpret_cast<uint16_t*>(uni + kAPt) + warp * 256;
+  uint16_t* ptl = pth + 128;
+  // Stages the V rows [base, base+16) into shared memory (cp.async, zero past
+  // p1) and loads the K rows of the lane's positions g, g+8 into registers.
+  // Before the step's new row has arrived, position `last` is fetched from the
+  // (stale) cache and patched afterwards.
+  uint32_t kg[16], kg8[16];
+  auto issue_kv = [&](uint32_t base, bool have_new) {
+    const int r = lane >> 1, hs = lane & 1;
+    const uint32_t pos = base + r;
+    uint8_t* dst = vs + r * 272 + hs * 128;
+    if (pos < p1) {
+      const uint8_t* src = (have_new && pos == last)
+                               ? reinterpret_cast<const uint8_t*>(vnew) + hs * 128
+                               : reinterpret_cast<const uint8_t*>(vbase + (size_t)pos * kKVDim) + hs * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + 16 * j)),
+                     "l"(src + 16 * j)
+                     : "memory");
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(dst)[j] = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t pg = min(base + g, p1 - 1), pg8 = min(base + g + 8, p1 - 1);
+    const uint4* sg = (have_new && pg == last)
+                          ? reinterpret_cast<const uint4*>(knew + 32 * t)
+                          : reinterpret_cast<const uint4*>(kbase + (size_t)pg * kKVDim + 32 * t);
+    const uint4* sg8 = (have_new && pg8 == last)
+                           ? reinterpret_cast<const uint4*>(knew + 32 * t)
+                           : reinterpret_cast<const uint4*>(kbase + (size_t)pg8 * kKVDim + 32 * t);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 a = sg[j], b = sg8[j];
+      kg[4 * j] = a.x; kg[4 * j + 1] = a.y; kg[4 * j + 2] = a.z; kg[4 * j + 3] = a.w;
+      kg8[4 * j] = b.x; kg8[4 * j + 1] = b.y; kg8[4 * j + 2] = b.z; kg8[4 * j + 3] = b.w;
+    }
+  };
+  const uint32_t first = p0 + warp * 16;
+  if (first < p1) issue_kv(first, false);
   // q of the 6 heads of this kv group, and the step's new k / v rows.
   poll_units<1>(p.q_ll + kvh * 768, 96, ct, 128, tag, misc, p.err, kSiteQ * 100 + layer, [&](int u, const __half* v) {
     reinterpret_cast<uint4*>(qs)[u] = *reinterpret_cast<const uint4*>(v);
@@ -312,8 +377,7 @@ __device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, 
     });
   }
   abar();
-  const __half* kbase = p.kc + (size_t)layer * p.kv_layer_stride + kvh * kHeadDim;
-  const __half* vbase = p.vc + (size_t)layer * p.kv_layer_stride + kvh * kHeadDim;
+  astamp(1);
   uint32_t qf[16];
   {
     const uint4* qp = reinterpret_cast<const uint4*>(qs + (g < 6 ? g : 0) * kHeadDim + 32 * t);
@@ -330,41 +394,33 @@ __device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, 
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  uint8_t* vs = uni + kAVs + warp * (16 * 272);
-  uint16_t* pth = reinterpret_cast<uint16_t*>(uni + kAPt) + warp * 256;
-  uint16_t* ptl = pth + 128;
-  for (uint32_t base = p0 + warp * 16; base < p1; base += kAttnWarpsFused * 16) {
-    {
-      const int r = lane >> 1, hs = lane & 1;
-      const uint32_t pos = base + r;
-      uint4* dst = reinterpret_cast<uint4*>(vs + r * 272 + hs * 128);
-      if (pos < p1) {
-        const uint4* src =
-            pos == last ? reinterpret_cast<const uint4*>(vnew) + hs * 8
-                        : reinterpret_cast<const uint4*>(vbase + (size_t)pos * kKVDim) + hs * 8;
+  for (uint32_t base = first; base < p1; base += kAttnWarpsFused * 16) {
+    if (base != first) {
+      issue_kv(base, true);
+    } else if (last >= base && last < base + 16) {
+      // patch the step's new row into the prefetched sub-tile
+      const uint32_t pg = min(base + g, p1 - 1), pg8 = min(base + g + 8, p1 - 1);
+      if (pg == last || pg8 == last) {
+        const uint4* nk = reinterpret_cast<const uint4*>(knew + 32 * t);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dst[j] = src[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < 4; ++j) {
+          const uint4 a = nk[j];
+          if (pg == last) { kg[4 * j] = a.x; kg[4 * j + 1] = a.y; kg[4 * j + 2] = a.z; kg[4 * j + 3] = a.w; }
+          if (pg8 == last) { kg8[4 * j] = a.x; kg8[4 * j + 1] = a.y; kg8[4 * j + 2] = a.z; kg8[4 * j + 3] = a.w; }
+        }
       }
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (base == first && last >= base && last < base + 16 && (int)(last - base) == (lane >> 1)) {
+      const int hs = lane & 1;
+      uint4* dst = reinterpret_cast<uint4*>(vs + (last - base) * 272 + hs * 128);
+      const uint4* src = reinterpret_cast<const uint4*>(vnew) + hs * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = src[j];
+    }
+    __syncwarp();
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
     {
-      const uint32_t pg = min(base + g, p1 - 1), pg8 = min(base + g + 8, p1 - 1);
-      const uint4* sg = pg == last
-                            ? reinterpret_cast<const uint4*>(knew + 32 * t)
-                            : reinterpret_cast<const uint4*>(kbase + (size_t)pg * kKVDim + 32 * t);
-      const uint4* sg8 = pg8 == last
-                             ? reinterpret_cast<const uint4*>(knew + 32 * t)
-                             : reinterpret_cast<const uint4*>(kbase + (size_t)pg8 * kKVDim + 32 * t);
-      uint32_t kg[16], kg8[16];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 a = sg[j], b = sg8[j];
-        kg[4 * j] = a.x; kg[4 * j + 1] = a.y; kg[4 * j + 2] = a.z; kg[4 * j + 3] = a.w;
-        kg8[4 * j] = b.x; kg8[4 * j + 1] = b.y; kg8[4 * j + 2] = b.z; kg8[4 * j + 3] = b.w;
-      }
 #pragma unroll
       for (int st = 0; st < 8; ++st) {
         const uint32_t a[4] = {kg[2 * st], kg8[2 * st], kg[2 * st + 1], kg8[2 * st + 1]};
@@ -424,6 +480,7 @@ __device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, 
     }
     __syncwarp();
   }
+  astamp(2);
   // ---- merge the 4 warps (shared memory), write this split's partial.
   float* wm = reinterpret_cast<float*>(uni + kAWm);
   float* wl = reinterpret_cast<float*>(uni + kAWl);
@@ -463,6 +520,7 @@ __device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, 
     }
   }
   abar();
+  astamp(3);
   // ---- combine: this unit produces outputs [z0, z1) of its kv head.
   const uint32_t Z = (768 + S_eff - 1) / S_eff;
   const uint32_t z0 = min(768u, s * Z), z1 = min(768u, z0 + Z);
@@ -507,10 +565,11 @@ __device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, 
           break;
         }
       }
-      __nanosleep(it < 32 ? 20 : 200);
+      __nanosleep(32);
     }
   }
   abar();
+  astamp(4);
   for (uint32_t z = z0 + ct; z < z1; z += 128) {
     const uint32_t hl = z / kHeadDim - h0;
     float M = -INFINITY;
@@ -527,6 +586,8 @@ __device__ void attention_unit(const FusedParams& p, int layer, int kvh, int s, 
 
 }  // namespace
 
+// 288 threads = 9 warps: one SM sub-partition holds 3 of them, so each thread
+// can have at most 16384 / 96 -> 168 registers.
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
@@ -543,8 +604,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ib = p.item_begin[blockIdx.x];
   const int n_items = (int)(p.item_begin[blockIdx.x + 1] - ib);
-  const FusedItem* items = p.items + ib;
+  FusedItem* items = reinterpret_cast<FusedItem*>(smem + kOffItems);
   const uint16_t lm_phase = (uint16_t)(p.n_layers * kPhasesPerLayer);
+  for (int i = threadIdx.x; i < n_items && i < kMaxItemsPerCta; i += blockDim.x) items[i] = p.items[ib + i];
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNS; ++i) {
@@ -559,9 +621,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   }
   __syncthreads();
 
+  unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      if (trace) trace[0] = globaltimer();
       const uint64_t pol = policy_evict_first();
       int i = 0;
       for (; i < n_items; ++i) {
@@ -576,12 +640,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           }
           break;
         }
-        const FusedItem it = items[i];
-        const uint8_t* src = (it.phase == lm_phase ? p.lm : p.q4) + it.src;
-        mbar_arrive_expect_tx(&full[slot], it.bytes);
-        bulk_g2s_stream(ring + slot * kSlotBytes, src, it.bytes, &full[slot], pol);
+        const ItemFields it = unpack_item(items[i]);
+        size_t off;
+        uint32_t bytes;
+        item_source(it, lm_phase, &off, &bytes);
+        const uint8_t* src = (it.phase == lm_phase ? p.lm : p.q4) + off;
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_g2s_stream(ring + slot * kSlotBytes, src, bytes, &full[slot], pol);
         misc->issued = i + 1;
       }
+      if (trace) trace[1] = globaltimer();
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -594,7 +662,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     int cur = 0;
     auto phase_end = [&](uint16_t ph) {
       int e = cur;
-      while (e < n_items && items[e].phase == ph) ++e;
+      while (e < n_items && (int)(items[e] & 0xFF) == ph) ++e;
       return e;
     };
     // K-split processing of items [cur, e): warp w takes block pairs w, w+8, ...
@@ -602,7 +670,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     auto ksplit = [&](int e, auto&& epilogue) {
       float acc_g = 0.f, acc_g8 = 0.f;
       for (int i = cur; i < e; ++i) {
-        const FusedItem it = items[i];
+        const ItemFields it = unpack_item(items[i]);
         const int slot = i % kNS;
         if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100))
           q4_chunk(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
@@ -630,10 +698,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       cur = e;
     };
     const float* rope = p.rope_cs + (size_t)(L - 1) * 128;
+    auto stamp = [&](int k) {
+      if (trace && ct == 0) trace[k] = globaltimer();
+    };
+    auto lstamp = [&](int layer, int k) { stamp(3 + layer * kTraceStampsPerLayer + k); };
+    stamp(2);
 
     for (int layer = 0; layer < p.n_layers; ++layer) {
       const uint16_t ph = (uint16_t)(layer * kPhasesPerLayer);
       if (ct == 0) misc->cphase = ph * 1000 + cur;
+      lstamp(layer, kTsLayerStart);
       // ---- x after the previous layer (or the embedding row, :57-60)
       if (layer == 0) {
         const uint4* src = reinterpret_cast<const uint4*>(p.embed + (size_t)token * kHidden);
@@ -645,6 +719,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
                       });
       }
       cbar();
+      lstamp(layer, kTsXReady);
       // ---- P1: RMSNorm -> QKV -> bias -> RoPE -> q, KV cache
       {
         const int e = phase_end(ph + kPhQKV);
@@ -692,9 +767,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           });
         }
       }
+      lstamp(layer, kTsQKVDone);
       // ---- P2: attention units on the last CTAs
       {
-        uint32_t S = (L + 127) / 128;
+        uint32_t S = (L + 63) / 64;
         const uint32_t cap = min((uint32_t)kMaxAttnSplits, gridDim.x / 2);
         S = max(1u, min(S, cap));
         uint32_t chunk = (L + S - 1) / S;
@@ -703,9 +779,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         const int u = (int)gridDim.x - 1 - (int)blockIdx.x;
         if (u < (int)(2 * S_eff) && warp < kAttnWarpsFused)
           attention_unit(p, layer, u & 1, u >> 1, S_eff, chunk, L, (uint16_t)tagof(layer), uni,
-                         xn, misc, ct);
+                         xn, misc, ct, nullptr);
       }
       cbar();
+      lstamp(layer, kTsAttnDone);
       // ---- P3: O projection + bias + residual (attention.metal:58-65)
       {
         const int e = phase_end(ph + kPhO);
@@ -718,6 +795,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
                           xf[u] = make_xfrag(tmp);
                         });
           cbar();
+          lstamp(layer, kTsOReady);
           const __half* ob = p.o_bias + (size_t)layer * kHidden;
           const uint16_t tg = (uint16_t)tagof(2 * layer + 1);
           ksplit(e, [&](int tile, int r, float sum) {
@@ -727,6 +805,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           });
         }
       }
+      lstamp(layer, kTsODone);
       // ---- P4: x -> RMSNorm -> gate|up -> SwiGLU -> h (each warp owns whole tiles)
       poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * layer + 1), misc, p.err,
                     kSiteXMid * 100 + layer, [&](int u, const __half* v) {
@@ -736,9 +815,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       {
         const int e = phase_end(ph + kPhGU);
         rmsnorm_out(xloc, p.norms + (size_t)(2 * layer + 1) * kHidden, red2, misc, xf, nullptr, ct);
+        lstamp(layer, kTsGUReady);
         const uint16_t tg = (uint16_t)tagof(layer);
         for (int i = cur; i < e; ++i) {
-          const FusedItem it = items[i];
+          const ItemFields it = unpack_item(items[i]);
           if ((it.seq & (kConsumerWarps - 1)) != warp) continue;
           const int slot = i % kNS;
           float acc_g = 0.f, acc_g8 = 0.f;
@@ -759,6 +839,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         cur = e;
       }
       cbar();
+      lstamp(layer, kTsGUDone);
       // ---- P5: h -> down -> bias -> residual
       {
         const int e = phase_end(ph + kPhDown);
@@ -771,6 +852,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
                           xf[u] = make_xfrag(tmp);
                         });
           cbar();
+          lstamp(layer, kTsDownReady);
           const __half* db = p.down_bias + (size_t)layer * kHidden;
           const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
           ksplit(e, [&](int tile, int r, float sum) {
@@ -781,9 +863,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         }
       }
       cbar();
+      lstamp(layer, kTsDownDone);
     }
     // ---- final RMSNorm + LM head (each warp owns whole 16-row tiles)
     if (ct == 0) misc->cphase = lm_phase * 1000 + cur;
+    stamp(3 + p.n_layers * kTraceStampsPerLayer);
     poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * p.n_layers), misc, p.err,
                   kSiteXFinal * 100, [&](int u, const __half* v) {
                     reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
@@ -792,14 +876,25 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     rmsnorm_out(xloc, p.norms + (size_t)(2 * p.n_layers) * kHidden, red2, misc, nullptr, xn, ct);
     {
       const int e = phase_end(lm_phase);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      float d[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};
       for (int i = cur; i < e; ++i) {
-        const FusedItem it = items[i];
+        const ItemFields it = unpack_item(items[i]);
         if ((it.seq & (kConsumerWarps - 1)) != warp) continue;
         const int slot = i % kNS;
         if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100)) {
           const uint8_t* sb = ring + slot * kSlotBytes;
-          for (int s = 0; s < it.nk; ++s) {
+          int s = 0;
+          for (; s + 1 < it.nk; s += 2) {
+            const uint4 w = *reinterpret_cast<const uint4*>(sb + s * kLMStepBytes + lane * 16);
+            const uint4 w2 = *reinterpret_cast<const uint4*>(sb + (s + 1) * kLMStepBytes + lane * 16);
+            const uint2 b = *reinterpret_cast<const uint2*>(xn + 16 * (it.k0 + s) + 4 * t);
+            const uint2 b2 = *reinterpret_cast<const uint2*>(xn + 16 * (it.k0 + s + 1) + 4 * t);
+            const uint32_t a[4] = {w.x, w.z, w.y, w.w};
+            const uint32_t a2[4] = {w2.x, w2.z, w2.y, w2.w};
+            mma_16816(d, a, b.x, b.y, d);
+            mma_16816(d2, a2, b2.x, b2.y, d2);
+          }
+          if (s < it.nk) {
             const uint4 w = *reinterpret_cast<const uint4*>(sb + s * kLMStepBytes + lane * 16);
             const uint2 b = *reinterpret_cast<const uint2*>(xn + 16 * (it.k0 + s) + 4 * t);
             const uint32_t a[4] = {w.x, w.z, w.y, w.w};
@@ -813,14 +908,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         }
         if (it.last) {
           if (t == 0) {
-            p.logits[16 * it.tile + g] = f2h(d[0]);
-            p.logits[16 * it.tile + g + 8] = f2h(d[2]);
+            p.logits[16 * it.tile + g] = f2h(d[0] + d2[0]);
+            p.logits[16 * it.tile + g + 8] = f2h(d[2] + d2[2]);
           }
           d[0] = d[1] = d[2] = d[3] = 0.f;
+          d2[0] = d2[1] = d2[2] = d2[3] = 0.f;
         }
       }
       cur = e;
     }
+    stamp(3 + p.n_layers * kTraceStampsPerLayer + 1);
   }
   __syncthreads();
   // Drain: every copy this CTA issued has landed before its shared memory goes away.
@@ -898,6 +995,8 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
   p.h_ll = reinterpret_cast<uint32_t*>(sc + lay.h_ll);
   p.logits = s.logits;
   p.err = s.err;
+  p.trace = s.trace;
+  p.trace_stride = trace_stride_for(m.n_layers);
   p.n_layers = m.n_layers;
   p.max_ctx = s.max_ctx;
   p.kv_layer_stride = (int)s.kv_layer_stride();
@@ -906,6 +1005,24 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
                                                 kSmemBytes),
                            "cudaFuncSetAttribute(k_decode_fused)"))
     return rc;
+  cudaFuncSetAttribute(k_decode_fused, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       (int)cudaSharedmemCarveoutMaxShared);
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_fused, kFusedThreads, kSmemBytes);
+  if (per_sm < 1) {
+    int dev = 0, smem_sm = 0, smem_optin = 0, smem_rsv = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&smem_rsv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, k_decode_fused);
+    return set_error(QWEN_ERR_CUDA,
+                     "k_decode_fused does not fit on an SM (%d B dynamic + %zu B static shared memory, "
+                     "%d threads x %d registers; SM: %d B shared, %d B per block opt-in, %d B reserved)",
+                     kSmemBytes, fa.sharedSizeBytes, kFusedThreads, fa.numRegs, smem_sm, smem_optin,
+                     smem_rsv);
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(f.grid);
   cfg.blockDim = dim3(kFusedThreads);

@@ -7,6 +7,7 @@
 #include <cstring>
 
 #include "engine.h"
+#include "fused.h"
 #include "qwen_common.cuh"
 #include "status.h"
 
@@ -239,6 +240,7 @@ int QwenModel::init_random(uint64_t seed, cudaStream_t st) {
 
 // ------------------------------------------------------- InferenceManager --
 InferenceManager::~InferenceManager() {
+  if (trace) cudaFree(trace);
   for (void* p : allocs_) cudaFree(p);
 }
 
@@ -496,6 +498,37 @@ int QwenEngine::forward(int32_t token, int32_t position, int32_t* next) {
   return QWEN_OK;
 }
 
+int QwenEngine::set_trace(int enable) {
+  if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
+  QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
+  const size_t n = (size_t)std::max(1, model_.fused.grid > 0 ? model_.fused.grid : sm_count_) *
+                       trace_stride_for(model_.n_layers);
+  if (enable && !state_.trace) {
+    QWEN_CUDA(cudaMalloc(&state_.trace, n * sizeof(unsigned long long)), "cudaMalloc(trace)");
+    QWEN_CUDA(cudaMemset(state_.trace, 0, n * sizeof(unsigned long long)), "memset");
+  } else if (!enable && state_.trace) {
+    cudaFree(state_.trace);
+    state_.trace = nullptr;
+  }
+  // the captured step graph bakes in the trace pointer: rebuild it
+  if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+  if (graph_) cudaGraphDestroy(graph_);
+  graph_exec_ = nullptr;
+  graph_ = nullptr;
+  return QWEN_OK;
+}
+
+int QwenEngine::get_trace(unsigned long long* host, size_t n, size_t* needed) {
+  const size_t total = (size_t)std::max(1, model_.fused.grid > 0 ? model_.fused.grid : sm_count_) *
+                           trace_stride_for(model_.n_layers);
+  *needed = total;
+  if (!state_.trace) return set_error(QWEN_ERR_STATE, "tracing is off");
+  if (!host || n < total) return QWEN_OK;
+  QWEN_CUDA(cudaMemcpy(host, state_.trace, total * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
+            "memcpy trace");
+  return QWEN_OK;
+}
+
 int QwenEngine::kernels_per_step(int* n) const {
   // step begin + sampler + step end around the model kernels
   if (cfg_.kernels == QWEN_KERNELS_OPS)
@@ -725,6 +758,15 @@ int qwen_engine_kernels_per_step(qwen_engine* e, int32_t* n) {
   const int rc = e->impl.kernels_per_step(&v);
   *n = v;
   return rc;
+}
+int qwen_engine_trace(qwen_engine* e, int32_t enable) {
+  ENGINE_OR_FAIL(e);
+  return e->impl.set_trace(enable);
+}
+int qwen_engine_get_trace(qwen_engine* e, uint64_t* host, size_t n, size_t* needed) {
+  ENGINE_OR_FAIL(e);
+  if (!needed) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
+  return e->impl.get_trace(reinterpret_cast<unsigned long long*>(host), n, needed);
 }
 int qwen_engine_time_steps(qwen_engine* e, int32_t n_steps, float* ms_step, float* ms_model) {
   ENGINE_OR_FAIL(e);

@@ -59,7 +59,6 @@ struct QwenLayer {
 
 // Weights in the layouts the fused decode kernels stream (built from the
 // reference layout on the device; see layout.cu).
-struct FusedItem;
 struct FusedWeights {
   uint8_t* blob = nullptr;          // Q4 tiles of every layer, fragment order (fused.h)
   size_t blob_bytes = 0;
@@ -70,7 +69,7 @@ struct FusedWeights {
   __half* down_bias = nullptr;      // [layer][1536]
   float* rope_cs = nullptr;         // [rope_ctx][64][2] cos, sin
   int rope_ctx = 0;
-  FusedItem* items = nullptr;       // per-CTA work lists
+  unsigned long long* items = nullptr;  // per-CTA work lists (packed items, fused.h)
   uint32_t* item_begin = nullptr;   // [grid + 1]
   int grid = 0;
   void release();
@@ -130,6 +129,7 @@ class InferenceManager {
   uint32_t* u24_ = nullptr;      // [batch] uniforms of the running step
   int* err = nullptr;            // device error word
   uint32_t* epoch = nullptr;     // step counter (tags of the fused step's exchanges)
+  unsigned long long* trace = nullptr;  // optional fused-step phase stamps
   void* attn_scratch = nullptr;
   int attn_splits = 0;
   void* fused_scratch = nullptr;
@@ -159,6 +159,8 @@ class QwenEngine {
   int get_kv(int32_t seq, int32_t layer, int32_t n_pos, uint16_t* hk, uint16_t* hv);
   int position(int32_t seq, int32_t* pos);
   int kernels_per_step(int* n) const;
+  int set_trace(int enable);
+  int get_trace(unsigned long long* host, size_t n, size_t* needed);
   int time_steps(int n, float* ms_step, float* ms_model);
   cudaStream_t stream() const { return stream_; }
 

@@ -49,18 +49,62 @@ constexpr int kAttnPartWords = 6 * 128 + 12;     // o[6][128], m[6], l[6]
 
 enum FusedPhase : uint16_t { kPhQKV = 0, kPhAttn = 1, kPhO = 2, kPhGU = 3, kPhDown = 4 };
 constexpr int kPhasesPerLayer = 5;
-
-// One streamed unit of weights for one CTA.
-struct FusedItem {
-  uint64_t src;     // byte offset into the Q4 blob or the LM tiles
-  uint32_t bytes;
-  uint16_t phase;   // layer * 5 + FusedPhase, or n_layers * 5 for the LM head
-  uint16_t tile;    // tile index inside its matrix
-  uint16_t k0;      // first block pair (Q4) or k16 step (LM) of the chunk
-  uint16_t nk;      // block pairs / k16 steps in the chunk
-  uint16_t last;    // 1 on the tile's last chunk
-  uint16_t seq;     // index of the tile among this CTA's tiles of the phase
+// Trace stamps per CTA: [0] producer start, [1] producer done, [2] consumer
+// start, then per layer kTraceStampsPerLayer stamps (see TraceStamp), then
+// LM start, consumer end.
+enum TraceStamp : int {
+  kTsLayerStart = 0, kTsXReady, kTsQKVDone, kTsAttnDone, kTsOReady, kTsODone, kTsGUReady,
+  kTsGUDone, kTsDownReady, kTsDownDone, kTraceStampsPerLayer
 };
+inline int trace_stride_for(int n_layers) { return 3 + n_layers * kTraceStampsPerLayer + 2; }
+
+// One streamed unit of weights for one CTA, packed in 64 bits:
+//   bits  0..7   phase  (layer * 5 + FusedPhase, or n_layers * 5 for the LM head)
+//   bits  8..21  tile   (tile index inside its matrix)
+//   bits 22..29  k0     (first block pair (Q4) or k16 step (LM) of the chunk)
+//   bits 30..37  nk     (block pairs / k16 steps in the chunk)
+//   bit  38      last   (the tile's last chunk)
+//   bits 39..46  seq    (index of the tile among this CTA's tiles of the phase)
+// The source offset and byte count follow from these fields (fused.h layouts).
+typedef unsigned long long FusedItem;
+constexpr int kMaxItemsPerCta = 768;
+
+struct ItemFields {
+  int phase, tile, k0, nk, last, seq;
+};
+__host__ __device__ inline FusedItem pack_item(int phase, int tile, int k0, int nk, int last, int seq) {
+  return (FusedItem)phase | ((FusedItem)tile << 8) | ((FusedItem)k0 << 22) |
+         ((FusedItem)nk << 30) | ((FusedItem)last << 38) | ((FusedItem)seq << 39);
+}
+__host__ __device__ inline ItemFields unpack_item(FusedItem w) {
+  ItemFields f;
+  f.phase = (int)(w & 0xFF);
+  f.tile = (int)((w >> 8) & 0x3FFF);
+  f.k0 = (int)((w >> 22) & 0xFF);
+  f.nk = (int)((w >> 30) & 0xFF);
+  f.last = (int)((w >> 38) & 1);
+  f.seq = (int)((w >> 39) & 0xFF);
+  return f;
+}
+// Byte offset (into the Q4 blob, or into the LM tiles when phase == lm_phase)
+// and byte count of an item.
+__host__ __device__ inline void item_source(const ItemFields& f, int lm_phase, size_t* off,
+                                            uint32_t* bytes) {
+  if (f.phase == lm_phase) {
+    *off = (size_t)f.tile * kLMTileBytes + (size_t)f.k0 * kLMStepBytes;
+    *bytes = (uint32_t)f.nk * kLMStepBytes;
+    return;
+  }
+  const int layer = f.phase / kPhasesPerLayer, k = f.phase % kPhasesPerLayer;
+  size_t base = (size_t)layer * kLayerBlobBytes;
+  size_t tile_bytes = kTile1536Bytes;
+  if (k == kPhQKV) base += kLayerQKVOff;
+  else if (k == kPhO) base += kLayerOOff;
+  else if (k == kPhGU) base += kLayerGUOff;
+  else { base += kLayerDownOff; tile_bytes = kTile8960Bytes; }
+  *off = base + (size_t)f.tile * tile_bytes + (size_t)f.k0 * kBpBytes;
+  *bytes = (uint32_t)f.nk * kBpBytes;
+}
 
 struct FusedParams {
   const uint8_t* q4;          // Q4 tiles, [layer][kLayerBlobBytes]
@@ -85,6 +129,8 @@ struct FusedParams {
   uint32_t* h_ll;             // [8960]
   __half* logits;             // [151936]
   int* err;
+  unsigned long long* trace;  // optional [grid][trace_stride] %globaltimer stamps
+  int trace_stride;
   int n_layers;
   int max_ctx;
   int kv_layer_stride;        // elements between layers of kc / vc

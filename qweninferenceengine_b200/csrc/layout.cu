@@ -116,24 +116,13 @@ static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items
       if (load[c] < load[best]) best = c;
     return best;
   };
-  auto add_tile = [&](int cta, uint16_t phase, int tile, size_t base, int n_k, int chunk_k,
-                      int unit_bytes) {
-    const uint16_t seq = (uint16_t)std::count_if(per[cta].begin(), per[cta].end(), [&](const FusedItem& it) {
-      return it.phase == phase && it.k0 == 0;
-    });
+  std::vector<std::vector<int>> tiles_in_phase(grid, std::vector<int>(n_layers * kPhasesPerLayer + 1, 0));
+  auto add_tile = [&](int cta, uint16_t phase, int tile, size_t, int n_k, int chunk_k, int unit_bytes) {
+    const int seq = tiles_in_phase[cta][phase]++;
     for (int k0 = 0; k0 < n_k; k0 += chunk_k) {
       const int nk = std::min(chunk_k, n_k - k0);
-      FusedItem it{};
-      it.src = base + (size_t)k0 * unit_bytes;
-      it.bytes = (uint32_t)(nk * unit_bytes);
-      it.phase = phase;
-      it.tile = (uint16_t)tile;
-      it.k0 = (uint16_t)k0;
-      it.nk = (uint16_t)nk;
-      it.last = (uint16_t)(k0 + nk >= n_k);
-      it.seq = seq;
-      per[cta].push_back(it);
-      load[cta] += it.bytes;
+      per[cta].push_back(pack_item(phase, tile, k0, nk, k0 + nk >= n_k, seq));
+      load[cta] += (double)nk * unit_bytes;
     }
   };
   for (int l = 0; l < n_layers; ++l) {
@@ -146,9 +135,15 @@ static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items
     for (int t = 0; t < kOTiles; ++t)
       add_tile(least(0, grid), ph + kPhO, t, lb + kLayerOOff + (size_t)t * kTile1536Bytes,
                kBp1536, kBp1536, kBpBytes);
-    for (int t = 0; t < kGUTiles; ++t)
-      add_tile(least(0, grid), ph + kPhGU, t, lb + kLayerGUOff + (size_t)t * kTile1536Bytes,
-               kBp1536, kBp1536, kBpBytes);
+    // gate/up: every consumer warp owns at most one tile per layer
+    const int gu_cap = (kGUTiles + grid - 1) / grid;
+    for (int t = 0; t < kGUTiles; ++t) {
+      int best = -1;
+      for (int c = 0; c < grid; ++c)
+        if (tiles_in_phase[c][ph + kPhGU] < gu_cap && (best < 0 || load[c] < load[best])) best = c;
+      add_tile(best, ph + kPhGU, t, lb + kLayerGUOff + (size_t)t * kTile1536Bytes, kBp1536,
+               kBp1536, kBpBytes);
+    }
     for (int t = 0; t < kDownTiles; ++t)
       add_tile(least(0, grid), ph + kPhDown, t, lb + kLayerDownOff + (size_t)t * kTile8960Bytes,
                kBp8960, kDownChunkBp, kBpBytes);
@@ -159,6 +154,7 @@ static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items
   items.clear();
   begin.assign(grid + 1, 0);
   for (int c = 0; c < grid; ++c) {
+    if (per[c].size() > (size_t)kMaxItemsPerCta) per[c].clear();  // reported by the caller
     begin[c] = (uint32_t)items.size();
     items.insert(items.end(), per[c].begin(), per[c].end());
   }
@@ -237,6 +233,10 @@ int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
   std::vector<FusedItem> items;
   std::vector<uint32_t> begin;
   build_schedule(m.n_layers, sms, items, begin);
+  for (int c = 0; c < sms; ++c)
+    if (begin[c + 1] == begin[c])
+      return set_error(QWEN_ERR_STATE, "fused schedule: CTA %d has no work or more than %d items", c,
+                       kMaxItemsPerCta);
   if (f.items) cudaFree(f.items);
   if (f.item_begin) cudaFree(f.item_begin);
   f.items = nullptr;

@@ -216,6 +216,57 @@ __device__ __forceinline__ uint4 make_xfrag(const __half (&v)[8]) {
   return r;
 }
 
+// Offset form of q4_block_mma for the fused kernels.  The MMA takes the raw
+// exponent-trick halves -- 1024+q for the low nibbles, 1024+16q for the high
+// nibbles -- against x for the low nibbles and x/16 for the high ones, and the
+// constant part cancels through the accumulator input:
+//   sum (q-8) x = D - c_b,  c_b = 1032 * sum_even x + 1152 * sum_odd (x/16)
+// (exact in real arithmetic; the fp32 accumulation carries the 1024 offset,
+// costing ~2^-24 * 4096 per block).  neg_c = -c_b of the block.
+__device__ __forceinline__ void raw_word(uint32_t w, uint32_t (&out)[4]) {
+  const uint32_t kLo = 0x000f000fu, kHi = 0x00f000f0u, kEx = 0x64006400u;
+  out[0] = lop3_and_or(w, kLo, kEx);
+  out[1] = lop3_and_or(w, kHi, kEx);
+  const uint32_t w8 = w >> 8;
+  out[2] = lop3_and_or(w8, kLo, kEx);
+  out[3] = lop3_and_or(w8, kHi, kEx);
+}
+__device__ __forceinline__ void q4_block_mma_off(uint32_t wg, uint32_t wg8, const uint4& xf,
+                                                 float neg_c, float (&d)[4]) {
+  uint32_t ag[4], ag8[4];
+  raw_word(wg, ag);
+  raw_word(wg8, ag8);
+  const float c[4] = {neg_c, neg_c, neg_c, neg_c};
+  const uint32_t a1[4] = {ag[0], ag8[0], ag[1], ag8[1]};
+  mma_16816(d, a1, xf.x, xf.y, c);
+  const uint32_t a2[4] = {ag[2], ag8[2], ag[3], ag8[3]};
+  mma_16816(d, a2, xf.z, xf.w, d);
+}
+// x fragment for the offset form: the high-nibble partners (odd k) are divided
+// by 16 (an exact power-of-two scaling for normal fp16 values).
+__device__ __forceinline__ uint4 make_xfrag_hi16(const __half (&v)[8]) {
+  const __half k16 = __ushort_as_half((unsigned short)0x2c00u);  // 1/16
+  __half h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = (i & 1) ? __hmul(v[i], k16) : v[i];
+  return make_xfrag(h);
+}
+// -c_b of block b from its four offset-form fragments (fixed summation order).
+__device__ __forceinline__ float block_neg_corr(const uint4* frag4) {
+  float even = 0.f, odd = 0.f;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint4 f = frag4[t];
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&f.x));  // x0, x4
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&f.y));  // x1/16, x5/16
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&f.z));  // x2, x6
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&f.w));  // x3/16, x7/16
+    even += (a.x + a.y) + (c.x + c.y);
+    odd += (b.x + b.y) + (d.x + d.y);
+  }
+  return -(1032.0f * even + 1152.0f * odd);
+}
+
 // Warp-wide sums.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

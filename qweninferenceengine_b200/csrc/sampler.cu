@@ -98,13 +98,27 @@ __device__ SelectResult radix_select(SampShared& s, cg::cluster_group& cluster, 
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     const int b = pass & 1;
-    for (int i = threadIdx.x; i < n_local; i += blockDim.x) {
-      const uint32_t e = s.e[i];
-      if ((e & mask) != prefix) continue;
-      if (restrict_kept && e <= e_star) continue;  // tie group added separately
-      const uint32_t d = (e >> shift) & 255u;
-      atomicAdd(&s.hsum[b][d], (unsigned long long)e);
-      atomicAdd(&s.hcnt[b][d], 1u);
+    // Warp-aggregated histogram: lanes holding the same digit combine their
+    // count and weight (as two 16-bit halves, exact) so that one lane per
+    // distinct digit per warp touches shared memory.  Near-flat distributions
+    // put most weights in a few digits; per-lane atomics would serialise.
+    const int n_iter = (n_local + (int)blockDim.x - 1) / (int)blockDim.x;
+    for (int k = 0; k < n_iter; ++k) {
+      const int i = k * (int)blockDim.x + (int)threadIdx.x;
+      uint32_t e = 0, d = 0xFFFFFFFFu;
+      if (i < n_local) {
+        e = s.e[i];
+        const bool member = (e & mask) == prefix && !(restrict_kept && e <= e_star);
+        if (member) d = (e >> shift) & 255u;
+      }
+      const uint32_t grp = __match_any_sync(0xffffffffu, d);
+      const uint32_t lo = __reduce_add_sync(grp, d == 0xFFFFFFFFu ? 0u : (e & 0xFFFFu));
+      const uint32_t hi = __reduce_add_sync(grp, d == 0xFFFFFFFFu ? 0u : (e >> 16));
+      const int leader = __ffs(grp) - 1;
+      if (d != 0xFFFFFFFFu && (int)(threadIdx.x & 31) == leader) {
+        atomicAdd(&s.hsum[b][d], ((unsigned long long)hi << 16) + (unsigned long long)lo);
+        atomicAdd(&s.hcnt[b][d], (uint32_t)__popc(grp));
+      }
     }
     cluster.sync();
     // Totals per digit over the cluster (every CTA computes the same).
@@ -238,8 +252,14 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
     s.cl_f[0] = m;
   }
   cluster.sync();
-  float M = -INFINITY;
-  for (int r = 0; r < kSampCluster; ++r) M = fmaxf(M, cluster.map_shared_rank(&s, r)->cl_f[0]);
+  __shared__ float s_M;
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int r = 0; r < kSampCluster; ++r) m = fmaxf(m, cluster.map_shared_rank(&s, r)->cl_f[0]);
+    s_M = m;
+  }
+  __syncthreads();
+  const float M = s_M;
   if (M == -INFINITY) {
     if (rank == 0 && threadIdx.x == 0) out_ids[seq] = kStopToken;
     cluster.sync();
@@ -256,8 +276,14 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   part = block_sum_u64(part, s);
   if (threadIdx.x == 0) s.cl_u = part;
   cluster.sync();
-  unsigned long long S = 0;
-  for (int r = 0; r < kSampCluster; ++r) S += cluster.map_shared_rank(&s, r)->cl_u;
+  __shared__ unsigned long long s_S;
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int r = 0; r < kSampCluster; ++r) t += cluster.map_shared_rank(&s, r)->cl_u;
+    s_S = t;
+  }
+  __syncthreads();
+  const unsigned long long S = s_S;
   const float pc = fminf(fmaxf(top_p, 0.0f), 1.0f);
   const uint32_t p24 = (uint32_t)__float2uint_rz(__fmul_rn(pc, 16777216.0f));
   unsigned long long thr = mul_shift24(S, p24);
@@ -295,8 +321,14 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   const uint32_t incl = scan[threadIdx.x], excl = incl - cnt;
   if (threadIdx.x == blockDim.x - 1) s.cl_cnt = incl;
   cluster.sync();
-  unsigned long long before = 0;
-  for (int r = 0; r < rank; ++r) before += cluster.map_shared_rank(&s, r)->cl_cnt;
+  __shared__ unsigned long long s_before;
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int r = 0; r < rank; ++r) t += cluster.map_shared_rank(&s, r)->cl_cnt;
+    s_before = t;
+  }
+  __syncthreads();
+  const unsigned long long before = s_before;
   if (j >= before + excl && j < before + incl) {
     unsigned long long want = j - before - excl;
     for (int i = b0; i < b1; ++i) {

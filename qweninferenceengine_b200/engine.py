@@ -160,6 +160,18 @@ class QwenEngine:
         check(lib().qwen_engine_time_steps(self._h, n_steps, ctypes.byref(a), ctypes.byref(b)))
         return a.value, b.value
 
+    def trace(self, enable: bool = True) -> None:
+        """Per-CTA phase timestamps of the fused step (see qwen_engine_trace)."""
+        check(lib().qwen_engine_trace(self._h, 1 if enable else 0))
+
+    def get_trace(self) -> np.ndarray:
+        need = ctypes.c_size_t()
+        check(lib().qwen_engine_get_trace(self._h, None, 0, ctypes.byref(need)))
+        out = np.zeros(need.value, np.uint64)
+        check(lib().qwen_engine_get_trace(self._h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+                                          out.size, ctypes.byref(need)))
+        return out
+
     def stream(self) -> int:
         s = ctypes.c_void_p()
         check(lib().qwen_engine_stream(self._h, ctypes.byref(s)))
