@@ -124,20 +124,27 @@ __device__ SelectResult radix_select(SampShared& s, cg::cluster_group& cluster, 
     // Totals per digit over the cluster (every CTA computes the same).
     __shared__ unsigned long long tot[256];
     __shared__ uint32_t totc[256];
-    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
-      unsigned long long sum = 0;
-      uint32_t c = 0;
+    if (threadIdx.x < 256) {
+      const int d = threadIdx.x;
+      unsigned long long part[kSampCluster];
+      uint32_t partc[kSampCluster];
+#pragma unroll
       for (int r = 0; r < kSampCluster; ++r) {
         SampShared* rs = cluster.map_shared_rank(&s, r);
-        sum += rs->hsum[b][d];
-        c += rs->hcnt[b][d];
+        part[r] = rs->hsum[b][d];
+        partc[r] = rs->hcnt[b][d];
       }
+      unsigned long long sum = 0;
+      uint32_t c = 0;
+#pragma unroll
+      for (int r = 0; r < kSampCluster; ++r) {
+        sum += part[r];
+        c += partc[r];
+      }
+      if (restrict_kept && (e_star & mask) == prefix && (uint32_t)d == ((e_star >> shift) & 255u))
+        sum += tie_weight;
       tot[d] = sum;
       totc[d] = c;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && restrict_kept && (e_star & mask) == prefix) {
-      tot[(e_star >> shift) & 255u] += tie_weight;
     }
     __syncthreads();
     // Zero the other buffer for the next pass (its last readers finished
@@ -146,18 +153,31 @@ __device__ SelectResult radix_select(SampShared& s, cg::cluster_group& cluster, 
       s.hsum[b ^ 1][d] = 0;
       s.hcnt[b ^ 1][d] = 0;
     }
-    // Serial scan from the top digit (256 steps, one thread, broadcast).
+    // Selected digit: the largest d with above + sum(tot[d..255]) >= target.
+    // Suffix sums by a block scan over the 256 digits (thread d holds digit 255-d).
+    __shared__ unsigned long long suf[256];
     __shared__ uint32_t sel;
     __shared__ unsigned long long sel_above;
-    if (threadIdx.x == 0) {
-      unsigned long long acc = above;
-      int dd = 255;
-      for (; dd > 0; --dd) {
-        if (acc + tot[dd] >= target) break;
-        acc += tot[dd];
+    if (threadIdx.x < 256) suf[threadIdx.x] = tot[255 - threadIdx.x];
+    __syncthreads();
+    for (int off = 1; off < 256; off <<= 1) {
+      unsigned long long v = 0;
+      if (threadIdx.x < 256 && threadIdx.x >= (unsigned)off) v = suf[threadIdx.x - off];
+      __syncthreads();
+      if (threadIdx.x < 256) suf[threadIdx.x] += v;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) sel = 0, sel_above = above;
+    __syncthreads();
+    if (threadIdx.x < 256) {
+      // suf[i] = sum of digits 255-i .. 255; digit d = 255 - i.
+      const int i = threadIdx.x, d = 255 - i;
+      const unsigned long long incl = above + suf[i];
+      const unsigned long long excl = incl - tot[d];
+      if ((incl >= target && excl < target) || (d == 0 && incl < target)) {
+        sel = (uint32_t)d;
+        sel_above = excl;
       }
-      sel = (uint32_t)dd;
-      sel_above = acc;
     }
     __syncthreads();
     prefix |= sel << shift;

@@ -1,0 +1,99 @@
+"""Profiling helpers for the decode engine.
+
+    python -m qweninferenceengine_b200.profiling case  [--layers 4] [--steps 2]
+        A small decode run (random-init model with `--layers` layers, a short
+        prompt, a few decode steps): the workload for `ncu --set full -k
+        regex:k_decode_fused -s 3 -c 1` captures, small enough to capture in
+        seconds while its 1.2 GB+ of weights still exceed the L2.
+
+    python -m qweninferenceengine_b200.profiling trace [--layers 28] [--ctx 512]
+        Per-phase critical-path summary of one fused decode step from the
+        kernel's %globaltimer stamps (qwen_engine_trace): for each traced layer,
+        min / median / max over CTAs of every stamp relative to the layer start.
+"""
+from __future__ import annotations
+
+import argparse
+
+import numpy as np
+
+from .engine import QwenConfig, QwenEngine
+
+STAMPS = ["start", "x_ready", "qkv_done", "attn_done", "o_ready", "o_done", "gu_ready",
+          "gu_done", "h_ready", "down_done"]
+
+
+def run_case(layers: int, steps: int) -> None:
+    cfg = QwenConfig(num_layers=layers, max_context_window=1024, temperature=0.0,
+                     stop_on_eos=False)
+    eng = QwenEngine(config=cfg, random_seed=5)
+    eng.prefill(np.arange(1, 5, dtype=np.int32))
+    eng.decode(steps, record=False)
+    eng.close()
+
+
+def run_trace(layers: int, ctx: int, show_layers) -> dict:
+    cfg = QwenConfig(num_layers=layers, max_context_window=max(1024, ctx + 64), temperature=0.7,
+                     top_p=0.8, stop_on_eos=False)
+    eng = QwenEngine(config=cfg, random_seed=5)
+    rng = np.random.default_rng(0)
+    eng.prefill(rng.integers(0, 151936, size=ctx - 1).astype(np.int32))
+    eng.decode(5, record=False)
+    ms_step, ms_model = eng.time_steps(10)
+    eng.trace(True)
+    eng.decode(3, record=False)
+    tr = eng.get_trace().astype(np.int64)
+    eng.trace(False)
+    eng.close()
+    k = len(STAMPS)
+    grid = tr.size // (3 + k * layers + 2)
+    tr = tr.reshape(grid, -1)
+    t0 = tr[:, 2].min()
+    rel = np.where(tr > 0, (tr - t0) / 1000.0, np.nan)
+    ph = rel[:, 3:3 + k * layers].reshape(grid, layers, k)
+    out = {"ms_step": ms_step, "ms_model": ms_model, "grid": grid,
+           "lm_start_us": float(np.nanmedian(rel[:, 3 + k * layers])),
+           "end_us": float(np.nanmax(rel[:, 4 + k * layers])), "layers": {}}
+    periods = np.diff(np.nanmedian(ph[:, :, 0], axis=0))
+    out["layer_period_us"] = float(np.median(periods)) if periods.size else None
+    for layer in show_layers:
+        if layer >= layers:
+            continue
+        base = np.nanmedian(ph[:, layer, 0])
+        rows = {}
+        for j, name in enumerate(STAMPS):
+            col = ph[:, layer, j]
+            col = col[~np.isnan(col)]
+            if col.size:
+                rows[name] = (int(col.size), float(col.min() - base), float(np.median(col) - base),
+                              float(col.max() - base))
+        out["layers"][layer] = rows
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("case")
+    c.add_argument("--layers", type=int, default=4)
+    c.add_argument("--steps", type=int, default=2)
+    t = sub.add_parser("trace")
+    t.add_argument("--layers", type=int, default=28)
+    t.add_argument("--ctx", type=int, default=512)
+    a = ap.parse_args()
+    if a.cmd == "case":
+        run_case(a.layers, a.steps)
+        print("ok")
+        return
+    r = run_trace(a.layers, a.ctx, [1, a.layers // 2, a.layers - 1])
+    print(f"step {r['ms_step']:.3f} ms, model kernels {r['ms_model']:.3f} ms, grid {r['grid']}, "
+          f"median layer period {r['layer_period_us']:.2f} us, LM head from {r['lm_start_us']:.1f} "
+          f"to {r['end_us']:.1f} us")
+    for layer, rows in r["layers"].items():
+        print(f"layer {layer} (us from the layer's median start; n = CTAs with the stamp)")
+        for name, (n, lo, med, hi) in rows.items():
+            print(f"  {name:10s} n={n:3d}  min {lo:7.2f}  med {med:7.2f}  max {hi:7.2f}")
+
+
+if __name__ == "__main__":
+    main()
