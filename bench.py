@@ -63,10 +63,14 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # Start timing only once the sampler is live (its first line is in).
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self

@@ -54,17 +54,27 @@ __device__ __forceinline__ unsigned long long mul_shift24(unsigned long long a, 
   return (a >> 24) * b + (((a & 0xFFFFFFull) * b) >> 24);
 }
 
+constexpr int kSampWarps = kSampThreads / 32;
+constexpr int kSampPerThread = (kSampMaxChunk + kSampThreads - 1) / kSampThreads;  // 19
+
 struct SampShared {
   uint32_t e[kSampMaxChunk];                 // scaled floats, then fixed-point weights
-  unsigned long long hsum[2][256];
-  uint32_t hcnt[2][256];
+  // Per-warp digit weights of the running pass as two exact halves (E & 0xFFFF,
+  // E >> 16): a warp sees at most 19 * 32 elements, so each half fits 32 bits.
+  uint32_t whist[kSampWarps][2][256];
+  unsigned long long qsum[4][256];           // quarter-block merges of whist
+  unsigned long long hsum[4][256];           // this CTA's digit weights, read by the cluster
+  unsigned long long tot[256];               // cluster totals of the running pass
   float red_f[32];
   int red_i[32];
   unsigned long long red_u[32];
+  uint32_t red_c[32];
   float cl_f[kSampCluster];                  // per-CTA partials read by the cluster
   int cl_i;
   unsigned long long cl_u;
   uint32_t cl_cnt;
+  uint32_t sel;
+  unsigned long long sel_above;
 };
 
 __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, SampShared& s) {
@@ -78,122 +88,145 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
   return t;
 }
 
-// Weighted radix select over E (descending).  Elements are the CTA's E values
-// with E > floor_excl... membership: E > e_star always, E == e_star counted with
-// total weight tie_weight (handled via the tie term), E < e_star excluded --
-// when e_star == 0 every element takes part.  Returns the selected value and
-// the weight strictly above it; *cnt_eq receives the number of equal elements.
+// Inclusive prefix sum of one value per thread over the block (thread order).
+__device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SampShared& s) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  if (lane == 31) s.red_c[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    uint32_t t = s.red_c[lane], x = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t u = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += u;
+    }
+    s.red_c[lane] = x - t;   // exclusive offsets of the warps
+  }
+  __syncthreads();
+  return v + s.red_c[w];
+}
+
+// Weighted radix select over E (descending order), 4 passes of 8-bit digits.
+// Members: every E (restrict_kept false), or E > e_star plus a virtual weight
+// tie_weight at value e_star (restrict_kept true).  Returns the value at which
+// the running weight from the top first reaches `target`, and the weight
+// strictly above that value.  `buf0` picks this select's pair of cluster
+// exchange buffers (a fresh pair per select, so no select waits for the
+// previous one's remote readers).
 struct SelectResult {
   uint32_t value;
   unsigned long long above;
-  uint32_t cnt_eq;
 };
 
 __device__ SelectResult radix_select(SampShared& s, cg::cluster_group& cluster, int n_local,
                                      unsigned long long target, bool restrict_kept,
-                                     uint32_t e_star, unsigned long long tie_weight) {
+                                     uint32_t e_star, unsigned long long tie_weight, int buf0) {
   uint32_t prefix = 0, mask = 0;
   unsigned long long above = 0;
-  uint32_t cnt_eq = 0;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    const int b = pass & 1;
-    // Warp-aggregated histogram: lanes holding the same digit combine their
-    // count and weight (as two 16-bit halves, exact) so that one lane per
-    // distinct digit per warp touches shared memory.  Near-flat distributions
-    // put most weights in a few digits; per-lane atomics would serialise.
-    const int n_iter = (n_local + (int)blockDim.x - 1) / (int)blockDim.x;
-    for (int k = 0; k < n_iter; ++k) {
-      const int i = k * (int)blockDim.x + (int)threadIdx.x;
-      uint32_t e = 0, d = 0xFFFFFFFFu;
-      if (i < n_local) {
-        e = s.e[i];
-        const bool member = (e & mask) == prefix && !(restrict_kept && e <= e_star);
-        if (member) d = (e >> shift) & 255u;
-      }
-      const uint32_t grp = __match_any_sync(0xffffffffu, d);
-      const uint32_t lo = __reduce_add_sync(grp, d == 0xFFFFFFFFu ? 0u : (e & 0xFFFFu));
-      const uint32_t hi = __reduce_add_sync(grp, d == 0xFFFFFFFFu ? 0u : (e >> 16));
-      const int leader = __ffs(grp) - 1;
-      if (d != 0xFFFFFFFFu && (int)(threadIdx.x & 31) == leader) {
-        atomicAdd(&s.hsum[b][d], ((unsigned long long)hi << 16) + (unsigned long long)lo);
-        atomicAdd(&s.hcnt[b][d], (uint32_t)__popc(grp));
+    const int buf = buf0 + (pass & 1);
+    uint32_t* hlo = s.whist[wid][0];
+    uint32_t* hhi = s.whist[wid][1];
+#pragma unroll
+    for (int d = lane; d < 256; d += 32) hlo[d] = hhi[d] = 0;
+    __syncwarp();
+    // Zero weights change no sum, so they are skipped.  When every member of a
+    // warp falls in one digit (peaked distributions put almost all weights in
+    // digit 0 of the upper passes) the warp reduces first and adds once.
+    for (int k = 0; k < kSampPerThread; ++k) {
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      const uint32_t e = i < n_local ? s.e[i] : 0u;
+      const bool member = e != 0u && (e & mask) == prefix && !(restrict_kept && e <= e_star);
+      const uint32_t d = (e >> shift) & 255u;
+      const uint32_t mm = __ballot_sync(0xffffffffu, member);
+      if (mm == 0u) continue;
+      const uint32_t d0 = __shfl_sync(0xffffffffu, d, __ffs(mm) - 1);
+      if (__all_sync(0xffffffffu, !member || d == d0)) {
+        const uint32_t lo = __reduce_add_sync(0xffffffffu, member ? (e & 0xFFFFu) : 0u);
+        const uint32_t hi = __reduce_add_sync(0xffffffffu, member ? (e >> 16) : 0u);
+        if (lane == 0) {
+          atomicAdd(&hlo[d0], lo);
+          atomicAdd(&hhi[d0], hi);
+        }
+      } else if (member) {
+        atomicAdd(&hlo[d], e & 0xFFFFu);
+        atomicAdd(&hhi[d], e >> 16);
       }
     }
+    __syncthreads();
+    {
+      const int d = threadIdx.x & 255, q = threadIdx.x >> 8;
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int w = 0; w < kSampWarps / 4; ++w) {
+        lo += s.whist[q * (kSampWarps / 4) + w][0][d];
+        hi += s.whist[q * (kSampWarps / 4) + w][1][d];
+      }
+      s.qsum[q][d] = ((unsigned long long)hi << 16) + lo;
+    }
+    __syncthreads();
+    if (threadIdx.x < 256) {
+      const int d = threadIdx.x;
+      s.hsum[buf][d] = s.qsum[0][d] + s.qsum[1][d] + s.qsum[2][d] + s.qsum[3][d];
+    }
     cluster.sync();
-    // Totals per digit over the cluster (every CTA computes the same).
-    __shared__ unsigned long long tot[256];
-    __shared__ uint32_t totc[256];
+    // Cluster totals per digit (every CTA computes the same).
     if (threadIdx.x < 256) {
       const int d = threadIdx.x;
       unsigned long long part[kSampCluster];
-      uint32_t partc[kSampCluster];
 #pragma unroll
-      for (int r = 0; r < kSampCluster; ++r) {
-        SampShared* rs = cluster.map_shared_rank(&s, r);
-        part[r] = rs->hsum[b][d];
-        partc[r] = rs->hcnt[b][d];
-      }
+      for (int r = 0; r < kSampCluster; ++r) part[r] = cluster.map_shared_rank(&s, r)->hsum[buf][d];
       unsigned long long sum = 0;
-      uint32_t c = 0;
 #pragma unroll
-      for (int r = 0; r < kSampCluster; ++r) {
-        sum += part[r];
-        c += partc[r];
-      }
+      for (int r = 0; r < kSampCluster; ++r) sum += part[r];
       if (restrict_kept && (e_star & mask) == prefix && (uint32_t)d == ((e_star >> shift) & 255u))
         sum += tie_weight;
-      tot[d] = sum;
-      totc[d] = c;
+      s.tot[d] = sum;
     }
     __syncthreads();
-    // Zero the other buffer for the next pass (its last readers finished
-    // before this pass's cluster barrier).
-    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
-      s.hsum[b ^ 1][d] = 0;
-      s.hcnt[b ^ 1][d] = 0;
-    }
-    // Selected digit: the largest d with above + sum(tot[d..255]) >= target.
-    // Suffix sums by a block scan over the 256 digits (thread d holds digit 255-d).
-    __shared__ unsigned long long suf[256];
-    __shared__ uint32_t sel;
-    __shared__ unsigned long long sel_above;
-    if (threadIdx.x < 256) suf[threadIdx.x] = tot[255 - threadIdx.x];
-    __syncthreads();
-    for (int off = 1; off < 256; off <<= 1) {
-      unsigned long long v = 0;
-      if (threadIdx.x < 256 && threadIdx.x >= (unsigned)off) v = suf[threadIdx.x - off];
-      __syncthreads();
-      if (threadIdx.x < 256) suf[threadIdx.x] += v;
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) sel = 0, sel_above = above;
-    __syncthreads();
-    if (threadIdx.x < 256) {
-      // suf[i] = sum of digits 255-i .. 255; digit d = 255 - i.
-      const int i = threadIdx.x, d = 255 - i;
-      const unsigned long long incl = above + suf[i];
-      const unsigned long long excl = incl - tot[d];
-      if ((incl >= target && excl < target) || (d == 0 && incl < target)) {
-        sel = (uint32_t)d;
-        sel_above = excl;
+    // Selected digit: the largest d with above + sum(tot[d..255]) >= target
+    // (digit 0 when the total falls short).  One warp: lane l holds digits
+    // 255-8l .. 248-8l in descending order.
+    if (wid == 0) {
+      unsigned long long v[8], mine = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = s.tot[255 - 8 * lane - j];
+        mine += v[j];
+      }
+      unsigned long long incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const uint32_t hit = __ballot_sync(0xffffffffu, above + incl >= target);
+      const int L = hit ? __ffs(hit) - 1 : 31;
+      if (lane == L) {
+        unsigned long long run = above + incl - mine;
+        int j = 0;
+        for (; j < 7; ++j) {
+          if (run + v[j] >= target) break;
+          run += v[j];
+        }
+        s.sel = (uint32_t)(255 - 8 * lane - j);
+        s.sel_above = run;
       }
     }
     __syncthreads();
+    const uint32_t sel = s.sel;
     prefix |= sel << shift;
     mask |= 255u << shift;
-    above = sel_above;
-    cnt_eq = totc[sel];
-    __syncthreads();
+    above = s.sel_above;
   }
-  // Leave both buffers zero for a later select.
-  cluster.sync();
-  for (int d = threadIdx.x; d < 256; d += blockDim.x) {
-    s.hsum[0][d] = s.hsum[1][d] = 0;
-    s.hcnt[0][d] = s.hcnt[1][d] = 0;
-  }
-  __syncthreads();
-  return SelectResult{prefix, above, cnt_eq};
+  return SelectResult{prefix, above};
 }
 
 __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThreads)
@@ -210,20 +243,19 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   const int lo = rank * chunk;
   const int n_local = max(0, min(vocab, lo + chunk) - lo);
 
-  for (int d = threadIdx.x; d < 256; d += blockDim.x) {
-    s.hsum[0][d] = s.hsum[1][d] = 0;
-    s.hcnt[0][d] = s.hcnt[1][d] = 0;
-  }
-
   // ---- greedy ---------------------------------------------------------
   if (!(temperature > 0.0f)) {
+    float v[kSampPerThread];
+#pragma unroll
+    for (int k = 0; k < kSampPerThread; ++k) {
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      v[k] = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
+    }
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n_local; i += blockDim.x) {
-      const float v = h2f(lg[lo + i]);
-      if (isnan(v)) continue;
-      if (v > best) { best = v; idx = lo + i; }   // increasing i: first max kept
-    }
+#pragma unroll
+    for (int k = 0; k < kSampPerThread; ++k)   // increasing id: the first maximum is kept
+      if (!isnan(v[k]) && v[k] > best) { best = v[k]; idx = lo + k * kSampThreads + (int)threadIdx.x; }
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best, o);
       const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
@@ -252,16 +284,21 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   }
 
   // ---- scale + max ---------------------------------------------------
-  float* sc = reinterpret_cast<float*>(s.e);
+  float sc[kSampPerThread];
   float mx = -INFINITY;
-  for (int i = threadIdx.x; i < n_local; i += blockDim.x) {
-    const float v = h2f(lg[lo + i]);
+#pragma unroll
+  for (int k = 0; k < kSampPerThread; ++k) {
+    const int i = k * kSampThreads + (int)threadIdx.x;
+    sc[k] = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
+  }
+#pragma unroll
+  for (int k = 0; k < kSampPerThread; ++k) {
     float x = 0.0f;
-    if (!isnan(v)) {
-      x = __fdiv_rn(v, temperature);
+    if (!isnan(sc[k])) {     // NaN logits keep 0.0 and stay out of the maximum
+      x = __fdiv_rn(sc[k], temperature);
       mx = fmaxf(mx, x);
     }
-    sc[i] = x;
+    sc[k] = x;
   }
   mx = warp_max(mx);
   if ((threadIdx.x & 31) == 0) s.red_f[threadIdx.x >> 5] = mx;
@@ -287,11 +324,15 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   }
   // ---- fixed-point weights + sum ---------------------------------------
   unsigned long long part = 0;
-  for (int i = threadIdx.x; i < n_local; i += blockDim.x) {
-    const float e = sampler_exp(__fsub_rn(sc[i], M));
-    const uint32_t E = __float2uint_rz(__fmul_rn(e, 2147483648.0f));
-    s.e[i] = E;
-    part += E;
+#pragma unroll
+  for (int k = 0; k < kSampPerThread; ++k) {
+    const int i = k * kSampThreads + (int)threadIdx.x;
+    if (i < n_local) {
+      const float e = sampler_exp(__fsub_rn(sc[k], M));
+      const uint32_t E = __float2uint_rz(__fmul_rn(e, 2147483648.0f));
+      s.e[i] = E;
+      part += E;
+    }
   }
   part = block_sum_u64(part, s);
   if (threadIdx.x == 0) s.cl_u = part;
@@ -310,7 +351,7 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   if (thr == 0) thr = 1;
 
   // ---- nucleus cutoff ----------------------------------------------------
-  const SelectResult c1 = radix_select(s, cluster, n_local, thr, false, 0, 0);
+  const SelectResult c1 = radix_select(s, cluster, n_local, thr, false, 0, 0, 0);
   const uint32_t e_star = c1.value;
   const unsigned long long need = thr - c1.above;
   const unsigned long long k_tie = (need + e_star - 1) / e_star;  // e_star >= 1
@@ -318,7 +359,7 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
 
   // ---- draw ----------------------------------------------------------------
   const unsigned long long R = mul_shift24(kept, u24[seq] & 0xFFFFFFu);
-  const SelectResult c2 = radix_select(s, cluster, n_local, R + 1, true, e_star, k_tie * e_star);
+  const SelectResult c2 = radix_select(s, cluster, n_local, R + 1, true, e_star, k_tie * e_star, 2);
   const uint32_t e2 = c2.value;
   const unsigned long long j = (R - c2.above) / e2;   // index inside the tie group (id order)
 
@@ -328,17 +369,7 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   const int b0 = threadIdx.x * per, b1 = min(n_local, b0 + per);
   uint32_t cnt = 0;
   for (int i = b0; i < b1; ++i) cnt += (s.e[i] == e2);
-  // block exclusive scan of cnt
-  __shared__ uint32_t scan[kSampThreads];
-  scan[threadIdx.x] = cnt;
-  __syncthreads();
-  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
-    const uint32_t v = threadIdx.x >= (unsigned)off ? scan[threadIdx.x - off] : 0u;
-    __syncthreads();
-    scan[threadIdx.x] += v;
-    __syncthreads();
-  }
-  const uint32_t incl = scan[threadIdx.x], excl = incl - cnt;
+  const uint32_t incl = block_incl_scan_u32(cnt, s), excl = incl - cnt;
   if (threadIdx.x == blockDim.x - 1) s.cl_cnt = incl;
   cluster.sync();
   __shared__ unsigned long long s_before;
