@@ -110,6 +110,21 @@ int qwen_attention_decode_noalloc(const uint16_t* q, const uint16_t* k_cache,
                                   const uint16_t* v_cache, uint16_t* out,
                                   const uint32_t* seq_len, uint32_t max_ctx, void* stream);
 
+/* gemv_q4_0 (matmul.metal:9-73) for n_batch activation rows at once, on the
+ * tcgen05 tensor cores: y[b][r] = half(sum_k ((q-8)*s) x[b][k] + bias[r]) for
+ * b < n_batch (1..256); x is [n_batch][k], y is [n_batch][n_rows].  The weight
+ * product (q-8)*s is rounded once to fp16 before the fp32-accumulating MMA.
+ * n_rows a multiple of 128, k a multiple of 64.  Uses temporary device
+ * memory (stream-ordered allocations) for the repacked weights. */
+int qwen_gemm_q4_0_batched(const uint8_t* packed, const uint16_t* scales, const uint16_t* x,
+                           uint16_t* y, uint32_t k, const uint16_t* bias, uint32_t n_rows,
+                           uint32_t n_batch, void* stream);
+
+/* gemv_fp16 (matmul.metal:75-113) for n_batch rows at once on tcgen05:
+ * y[b][r] = half(sum_k w[r][k] x[b][k]).  Same shape rules as above. */
+int qwen_gemm_fp16_batched(const uint16_t* w, const uint16_t* x, uint16_t* y, uint32_t k,
+                           uint32_t n_rows, uint32_t n_batch, void* stream);
+
 /* (q-8)*scale for n_weights weights, low nibble first (matmul.metal:37-42). */
 int qwen_dequant_q4(const uint8_t* packed, const uint16_t* scales, size_t n_weights,
                     float* out, void* stream);

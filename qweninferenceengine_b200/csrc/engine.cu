@@ -13,13 +13,6 @@
 
 namespace qwen {
 
-#define QWEN_TRY(expr)        \
-  do {                        \
-    int _rc = (expr);         \
-    if (_rc != QWEN_OK) return _rc; \
-  } while (0)
-#define QWEN_CUDA(expr, what) QWEN_TRY(cuda_status((expr), (what)))
-
 // ------------------------------------------------------------ step kernels --
 __device__ __forceinline__ uint64_t dsplitmix64(uint64_t z) {
   z += 0x9E3779B97F4A7C15ull;

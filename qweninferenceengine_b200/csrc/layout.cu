@@ -13,13 +13,6 @@
 
 namespace qwen {
 
-#define QWEN_TRY(expr)                  \
-  do {                                  \
-    int _rc = (expr);                   \
-    if (_rc != QWEN_OK) return _rc;     \
-  } while (0)
-#define QWEN_CUDA(expr, what) QWEN_TRY(cuda_status((expr), (what)))
-
 enum RowMap : int { kMapPlain = 0, kMapRopePairs = 1, kMapGateUp = 2 };
 
 // Up to three reference-layout matrices with the same K, concatenated by rows.

@@ -12,3 +12,11 @@ int launch_status(const char* what);
 // Uploads the RoPE frequency table to the current device once.
 int ensure_rope_table();
 }  // namespace qwen
+
+// Early return of a non-OK status (QWEN_OK is 0).
+#define QWEN_TRY(expr)                \
+  do {                                \
+    int _rc = (expr);                 \
+    if (_rc != 0) return _rc;         \
+  } while (0)
+#define QWEN_CUDA(expr, what) QWEN_TRY(::qwen::cuda_status((expr), (what)))

@@ -46,6 +46,27 @@ def gemv_fp16(w: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None)
     return y
 
 
+def gemm_q4_0_batched(packed: torch.Tensor, scales: torch.Tensor, x: torch.Tensor,
+                      bias: torch.Tensor | None = None) -> torch.Tensor:
+    """gemv_q4_0 (matmul.metal:9-73) for every row of x [n_batch][k] at once on
+    the tcgen05 tensor cores: y [n_batch][n_rows]."""
+    nb, k = x.shape
+    n = scales.numel() * 32 // k
+    y = torch.empty((nb, n), dtype=torch.float16, device=x.device)
+    check(lib().qwen_gemm_q4_0_batched(_ptr(packed), _ptr(scales), _ptr(x), _ptr(y), k, _ptr(bias),
+                                       n, nb, _stream()))
+    return y
+
+
+def gemm_fp16_batched(w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """gemv_fp16 (matmul.metal:75-113) for every row of x [n_batch][k] at once."""
+    n, k = w.shape
+    nb = x.shape[0]
+    y = torch.empty((nb, n), dtype=torch.float16, device=x.device)
+    check(lib().qwen_gemm_fp16_batched(_ptr(w), _ptr(x), _ptr(y), k, n, nb, _stream()))
+    return y
+
+
 def rms_norm_q4(x: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
     """rms_norm_q4 (rmsnorm.metal:9-46)."""
     out = torch.empty_like(x)
