@@ -158,13 +158,14 @@ typedef struct qwen_engine qwen_engine;
 
 #define QWEN_KERNELS_FUSED 0 /* fused decode step (default) */
 #define QWEN_KERNELS_OPS 1   /* the reference dispatch order, one kernel per op */
+#define QWEN_KERNELS_TC 2    /* batched step: every projection one tcgen05 GEMM over the batch */
 
 typedef struct qwen_engine_config {
   int device;          /* CUDA device ordinal */
   int max_ctx;         /* KV slots per sequence (QwenConfig.maxContextWindow = 1024) */
   int batch;           /* independent sequences decoded together */
   int n_layers;        /* decoder layers (28; fewer only for tests) */
-  int kernels;         /* QWEN_KERNELS_FUSED or QWEN_KERNELS_OPS */
+  int kernels;         /* QWEN_KERNELS_FUSED, QWEN_KERNELS_OPS or QWEN_KERNELS_TC */
   float temperature;   /* extractNextTokenID default 0.7 (:273); <= 0 -> greedy */
   float top_p;         /* default 0.8 (:273) */
   uint64_t seed;       /* uniform stream seed (the reference's RNG is unseeded) */

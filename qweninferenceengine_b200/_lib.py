@@ -23,6 +23,7 @@ QWEN_ERR_STATE = 8
 
 QWEN_KERNELS_FUSED = 0
 QWEN_KERNELS_OPS = 1
+QWEN_KERNELS_TC = 2
 
 c_void_p, c_int, c_uint32, c_int32, c_uint64, c_size_t, c_float = (
     ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint64,

@@ -1,0 +1,301 @@
+// batched.cu -- the decode step for a batch of independent sequences on the
+// tcgen05 tensor cores (QWEN_KERNELS_TC): the reference's forward
+// (InferenceEngine.swift:54-271) for every sequence at once, each projection
+// one tensor-core GEMM over all sequences (tc_gemm.cu), attention per
+// sequence with its own length (attention.cu), fp16 rounding points as in
+// the reference.
+//
+// Per layer (B sequences, nb = B padded to 16 activation rows):
+//   act_h <- rmsnorm(x)                     (previous layer's finish kernel)
+//   part  <- W_qkv . act_h                  tensor cores, K split
+//   q, K/V cache <- rope(half(part + b))    k_qkv_finish (rope.metal:12-39,
+//                                           attention.metal:67-84)
+//   attn  <- attention(q, cache)            split-K GQA decode attention
+//   act_h <- attn                           k_pack_act
+//   part  <- W_o . act_h
+//   x     <- half(x + half(part + b_o)); act_h <- rmsnorm(x)   k_resid_norm_finish
+//   part  <- W_gu . act_h                   gate rows then up rows
+//   act_i <- half(silu(g) * u)              k_swiglu_finish (activations.metal:9-27)
+//   part  <- W_down . act_i
+//   x     <- half(x + half(part + b_down)); act_h <- rmsnorm_next(x)
+// then logits = LM . act_h (fp16 out, no split).
+#include <cmath>
+#include <vector>
+
+#include "engine.h"
+#include "qwen_common.cuh"
+#include "status.h"
+#include "tc_gemm.h"
+
+namespace qwen {
+
+namespace {
+
+constexpr int kQKVTiles = kQKVRows / kTcM;          // 16
+constexpr int kOTiles = kHidden / kTcM;             // 12
+constexpr int kGUTiles = 2 * kInter / kTcM;         // 140
+constexpr int kDownTiles = kHidden / kTcM;          // 12
+constexpr int kChunks1536 = kHidden / kTcChunkK;    // 24
+constexpr int kChunks8960 = kInter / kTcChunkK;     // 140
+constexpr size_t kTcQKVBytes = (size_t)kQKVTiles * kChunks1536 * kQ4TcChunkBytes;
+constexpr size_t kTcOBytes = (size_t)kOTiles * kChunks1536 * kQ4TcChunkBytes;
+constexpr size_t kTcGUBytes = (size_t)kGUTiles * kChunks1536 * kQ4TcChunkBytes;
+constexpr size_t kTcDownBytes = (size_t)kDownTiles * kChunks8960 * kQ4TcChunkBytes;
+constexpr size_t kTcLayerBytes = kTcQKVBytes + kTcOBytes + kTcGUBytes + kTcDownBytes;
+
+// Byte offset of element i of activation row b in the tile layout of nb rows.
+__device__ __forceinline__ size_t act_off(int b, int i, int nb) {
+  const int c = i >> 6, j = (i >> 3) & 7;
+  return ((size_t)c * nb + b) * 128 + (((uint32_t)j ^ (uint32_t)(b & 7)) << 4) + (i & 7) * 2;
+}
+
+// 1/sqrt(mean(x^2) + eps) of one 1536 row, 256 threads, the summation order
+// of k_rms_norm (rmsnorm.metal:9-46).  vals: this thread's 6 elements i = t + 256 j.
+__device__ __forceinline__ float rms_scale_row(const float (&vals)[6], float* red) {
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 6; ++j) acc += vals[j] * vals[j];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += red[w];
+  return 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
+}
+
+// act row b <- half(half(x * s) * gamma).
+__global__ void __launch_bounds__(256) k_rms_to_act(const __half* __restrict__ x,
+                                                    const __half* __restrict__ gamma,
+                                                    uint8_t* __restrict__ act, int nb) {
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  const __half* xr = x + (size_t)b * kHidden;
+  float v[6];
+#pragma unroll
+  for (int j = 0; j < 6; ++j) v[j] = h2f(xr[threadIdx.x + 256 * j]);
+  const float s = rms_scale_row(v, red);
+#pragma unroll
+  for (int j = 0; j < 6; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v[j] * s), gamma[i]);
+  }
+}
+
+__device__ __forceinline__ float sum_splits(const float* __restrict__ part, int splits, int nbv,
+                                            int n, int b, int i) {
+  float s = 0.f;
+  for (int sp = 0; sp < splits; ++sp) s += part[((size_t)sp * nbv + b) * n + i];
+  return s;
+}
+
+// QKV epilogue of one sequence: biases, fp16 rounding, RoPE at position
+// seq_len - 1 on q (12 heads) and k (2 heads), K/V appended to the cache.
+__global__ void __launch_bounds__(256) k_qkv_finish(const float* __restrict__ part, int splits, int nbv,
+                                                    const __half* __restrict__ bias,
+                                                    const float* __restrict__ rope_cs,
+                                                    const SeqCtl* __restrict__ ctl, int max_ctx,
+                                                    __half* __restrict__ q, __half* __restrict__ kc,
+                                                    __half* __restrict__ vc, size_t kv_seq_stride) {
+  __shared__ __half y[kQKVRows];
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < kQKVRows; i += 256)
+    y[i] = f2h(sum_splits(part, splits, nbv, kQKVRows, b, i) + h2f(bias[i]));
+  __syncthreads();
+  const uint32_t L = ctl[b].seq_len;
+  const uint32_t pos = L - 1;
+  if (L == 0 || pos >= (uint32_t)max_ctx) return;  // step_begin clamps; never taken
+  __half* kr = kc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
+  __half* vr = vc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
+  const float* cs = rope_cs + (size_t)pos * 128;
+  for (int p = threadIdx.x; p < (kHeads + kKVHeads) * 64; p += 256) {
+    const int head = p >> 6, pair = p & 63;
+    const int i0 = head * 128 + pair;  // q heads, then the k heads at 1536
+    const float c = cs[2 * pair], s = cs[2 * pair + 1];
+    const float x1 = h2f(y[i0]), x2 = h2f(y[i0 + 64]);
+    const __half r1 = f2h(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+    const __half r2 = f2h(__fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c)));
+    if (head < kHeads) {
+      q[(size_t)b * kHidden + i0] = r1;
+      q[(size_t)b * kHidden + i0 + 64] = r2;
+    } else {
+      kr[i0 - kHidden] = r1;
+      kr[i0 - kHidden + 64] = r2;
+    }
+  }
+  for (int i = threadIdx.x; i < kKVDim; i += 256) vr[i] = y[kHidden + kKVDim + i];
+}
+
+// x <- half(x + half(sum + bias)); act_h row <- rmsnorm(x) with gamma.
+__global__ void __launch_bounds__(256) k_resid_norm_finish(const float* __restrict__ part, int splits,
+                                                           int nbv, const __half* __restrict__ bias,
+                                                           __half* __restrict__ x,
+                                                           const __half* __restrict__ gamma,
+                                                           uint8_t* __restrict__ act, int nb) {
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  __half* xr = x + (size_t)b * kHidden;
+  float v[6];
+#pragma unroll
+  for (int j = 0; j < 6; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    const __half y = f2h(sum_splits(part, splits, nbv, kHidden, b, i) + h2f(bias[i]));
+    const __half xn = __hadd(xr[i], y);
+    xr[i] = xn;
+    v[j] = h2f(xn);
+  }
+  const float s = rms_scale_row(v, red);
+#pragma unroll
+  for (int j = 0; j < 6; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v[j] * s), gamma[i]);
+  }
+}
+
+// act_i row b <- half(silu(g) * u), g and u the fp16-rounded gate/up outputs
+// (zero biases, InferenceEngine.swift:82-85).
+__global__ void __launch_bounds__(256) k_swiglu_finish(const float* __restrict__ part, int splits,
+                                                       int nbv, uint8_t* __restrict__ act, int nb) {
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  const int b = blockIdx.y;
+  if (i >= kInter) return;
+  const float g = h2f(f2h(sum_splits(part, splits, nbv, 2 * kInter, b, i) + 0.0f));
+  const float u = h2f(f2h(sum_splits(part, splits, nbv, 2 * kInter, b, kInter + i) + 0.0f));
+  *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = f2h(silu_ref(g) * u);
+}
+
+struct TcPlan {
+  int qkv, o, gu, down;  // K splits
+};
+
+TcPlan plan_for(int sm_count) {
+  return TcPlan{tc_choose_splits(kQKVTiles, kChunks1536, sm_count),
+                tc_choose_splits(kOTiles, kChunks1536, sm_count),
+                tc_choose_splits(kGUTiles, kChunks1536, sm_count),
+                tc_choose_splits(kDownTiles, kChunks8960, sm_count)};
+}
+
+int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManager& s, int n_rows,
+         int k, int splits, float* part, __half* out, long long ld_out, cudaStream_t st) {
+  TcGemmArgs a;
+  a.w = blob;
+  a.q4 = q4;
+  a.act = act;
+  a.nb = s.tc_nb;
+  a.nb_valid = s.batch;
+  a.n_rows = n_rows;
+  a.k = k;
+  a.splits = splits;
+  a.part = part;
+  a.out = out;
+  a.ld_out = ld_out;
+  a.err = s.err;
+  if (launch_tc_gemm(a, st) != 0) return launch_status("tensor-core projection");
+  return QWEN_OK;
+}
+
+}  // namespace
+
+int tc_kernels_per_step(int n_layers) { return 1 + 10 * n_layers + 1; }
+
+int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
+  TcWeights& t = m.tc;
+  t.layer_bytes = kTcLayerBytes;
+  if (!t.blob) QWEN_CUDA(cudaMalloc(&t.blob, kTcLayerBytes * m.n_layers), "cudaMalloc(tc weights)");
+  if (!t.lm) QWEN_CUDA(cudaMalloc(&t.lm, f16_tc_blob_bytes(kVocab, kHidden)), "cudaMalloc(tc lm)");
+  auto rq = [&](const Q4Linear& w, uint8_t* dst) {
+    return launch_repack_q4_tc(w.packed, w.scales, w.rows, w.k, dst, st) == 0
+               ? QWEN_OK
+               : launch_status("repack q4 (tensor-core layout)");
+  };
+  for (int l = 0; l < m.n_layers; ++l) {
+    const QwenLayer& L = m.layers[l];
+    uint8_t* base = t.blob + kTcLayerBytes * l;
+    uint8_t* qkv = base;
+    uint8_t* o = qkv + kTcQKVBytes;
+    uint8_t* gu = o + kTcOBytes;
+    uint8_t* down = gu + kTcGUBytes;
+    // Concatenating rows = concatenating whole tiles of the blob.
+    QWEN_TRY(rq(L.q, qkv));
+    QWEN_TRY(rq(L.k, qkv + (size_t)(kHidden / kTcM) * kChunks1536 * kQ4TcChunkBytes));
+    QWEN_TRY(rq(L.v, qkv + (size_t)((kHidden + kKVDim) / kTcM) * kChunks1536 * kQ4TcChunkBytes));
+    QWEN_TRY(rq(L.o, o));
+    QWEN_TRY(rq(L.gate, gu));
+    QWEN_TRY(rq(L.up, gu + (size_t)(kInter / kTcM) * kChunks1536 * kQ4TcChunkBytes));
+    QWEN_TRY(rq(L.down, down));
+  }
+  if (launch_repack_f16_tc(m.embed, kVocab, kHidden, t.lm, st) != 0)
+    return launch_status("repack lm head");
+  QWEN_TRY(upload_rope_table(&t.rope_cs, &t.rope_ctx, max_ctx, st));
+  QWEN_CUDA(cudaStreamSynchronize(st), "sync");
+  return QWEN_OK;
+}
+
+int tc_state_allocate(InferenceManager& s, int sm_count) {
+  if (s.act_h) return QWEN_OK;
+  if (s.batch > kTcMaxNb)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "tensor-core step: batch %d > %d", s.batch, kTcMaxNb);
+  s.tc_nb = act_rows(s.batch);
+  const TcPlan p = plan_for(sm_count);
+  const size_t part = std::max(std::max((size_t)p.qkv * kQKVRows, (size_t)p.o * kHidden),
+                               std::max((size_t)p.gu * 2 * kInter, (size_t)p.down * kHidden)) *
+                      s.batch;
+  QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kHidden), (void**)&s.act_h));
+  QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kInter), (void**)&s.act_i));
+  QWEN_TRY(s.alloc_tracked(part * sizeof(float), (void**)&s.tc_part));
+  return QWEN_OK;
+}
+
+int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st) {
+  const TcWeights& t = m.tc;
+  if (!t.blob || !s.act_h) return set_error(QWEN_ERR_STATE, "tensor-core step not prepared");
+  if (t.rope_ctx < s.max_ctx) return set_error(QWEN_ERR_STATE, "RoPE table shorter than max_ctx");
+  const TcPlan p = plan_for(sm_count);
+  const int B = s.batch, nb = s.tc_nb;
+  AttnParams ap{};
+  ap.q = s.q;
+  ap.q_seq_stride = kHidden;
+  ap.kv_seq_stride = (long long)s.kv_seq_stride();
+  ap.kv_pos_stride = kKVDim;
+  ap.kv_head_stride = kHeadDim;
+  ap.seq_len = &s.ctl[0].seq_len;
+  ap.seq_len_stride = (int)(sizeof(SeqCtl) / sizeof(uint32_t));
+  ap.max_ctx = (uint32_t)s.max_ctx;
+  ap.out = s.attn_out;
+  ap.out_seq_stride = kHidden;
+  ap.err = s.err;
+  attn_bind_scratch(ap, s.attn_scratch, s.attn_splits, B);
+
+  k_rms_to_act<<<B, 256, 0, st>>>(s.x, m.layers[0].input_norm, s.act_h, nb);
+  for (int l = 0; l < m.n_layers; ++l) {
+    const QwenLayer& L = m.layers[l];
+    const uint8_t* qkv = t.blob + t.layer_bytes * l;
+    const uint8_t* o = qkv + kTcQKVBytes;
+    const uint8_t* gu = o + kTcOBytes;
+    const uint8_t* down = gu + kTcGUBytes;
+    __half* kc = s.kc + (size_t)l * s.kv_layer_stride();
+    __half* vc = s.vc + (size_t)l * s.kv_layer_stride();
+
+    QWEN_TRY(gemm(qkv, true, s.act_h, s, kQKVRows, kHidden, p.qkv, s.tc_part, nullptr, 0, st));
+    k_qkv_finish<<<B, 256, 0, st>>>(s.tc_part, p.qkv, B, L.qkv_bias, t.rope_cs, s.ctl, s.max_ctx,
+                                    s.q, kc, vc, s.kv_seq_stride());
+    ap.k = kc;
+    ap.v = vc;
+    launch_attention_decode(ap, s.attn_splits, B, st);
+    if (launch_pack_act(s.attn_out, kHidden, B, kHidden, nb, s.act_h, st) != 0)
+      return launch_status("pack attention output");
+    QWEN_TRY(gemm(o, true, s.act_h, s, kHidden, kHidden, p.o, s.tc_part, nullptr, 0, st));
+    k_resid_norm_finish<<<B, 256, 0, st>>>(s.tc_part, p.o, B, L.o_bias, s.x, L.post_attn_norm,
+                                           s.act_h, nb);
+    QWEN_TRY(gemm(gu, true, s.act_h, s, 2 * kInter, kHidden, p.gu, s.tc_part, nullptr, 0, st));
+    k_swiglu_finish<<<dim3((kInter + 255) / 256, B), 256, 0, st>>>(s.tc_part, p.gu, B, s.act_i, nb);
+    QWEN_TRY(gemm(down, true, s.act_i, s, kHidden, kInter, p.down, s.tc_part, nullptr, 0, st));
+    const __half* next_norm = l + 1 < m.n_layers ? m.layers[l + 1].input_norm : m.final_norm;
+    k_resid_norm_finish<<<B, 256, 0, st>>>(s.tc_part, p.down, B, L.down_bias, s.x, next_norm,
+                                           s.act_h, nb);
+  }
+  QWEN_TRY(gemm(t.lm, false, s.act_h, s, kVocab, kHidden, 1, nullptr, s.logits, kVocab, st));
+  return launch_status("tensor-core decode step");
+}
+
+}  // namespace qwen

@@ -222,12 +222,6 @@ __device__ __forceinline__ int it_phase_of(const FusedItem* items, int i) {
   return (int)(items[i] & 0xFF);
 }
 
-__device__ __forceinline__ float silu_ref(float x) {
-  if (x > 15.0f) return x;
-  if (x < -15.0f) return 0.0f;
-  return x / (1.0f + expf(-x));
-}
-
 // RMSNorm of xloc (rmsnorm.metal:9-46): out = half(half(x * s) * gamma).
 // Writes Q4 x fragments (frags) and/or plain fp16 (plain).  256 consumer threads.
 __device__ __forceinline__ void rmsnorm_out(const __half* xloc, const __half* __restrict__ gamma, float* red2,

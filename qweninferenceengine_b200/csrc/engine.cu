@@ -117,8 +117,18 @@ void FusedWeights::release() {
   item_begin = nullptr;
 }
 
+void TcWeights::release() {
+  void* ps[] = {blob, lm, rope_cs};
+  for (void* p : ps)
+    if (p) cudaFree(p);
+  blob = lm = nullptr;
+  rope_cs = nullptr;
+  rope_ctx = 0;
+}
+
 QwenModel::~QwenModel() {
   fused.release();
+  tc.release();
   for (void* p : allocs_) cudaFree(p);
 }
 
@@ -237,6 +247,13 @@ InferenceManager::~InferenceManager() {
   for (void* p : allocs_) cudaFree(p);
 }
 
+int InferenceManager::alloc_tracked(size_t bytes, void** out) {
+  QWEN_CUDA(cudaMalloc(out, bytes), "cudaMalloc(state)");
+  allocs_.push_back(*out);
+  QWEN_CUDA(cudaMemset(*out, 0, bytes), "cudaMemset(state)");
+  return QWEN_OK;
+}
+
 int InferenceManager::allocate(int b, int nl, int mc, int mo) {
   batch = b;
   n_layers = nl;
@@ -295,7 +312,8 @@ int QwenEngine::init(const qwen_engine_config& cfg) {
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "batch=%d out of range", cfg.batch);
   if (cfg.n_layers < 1 || cfg.n_layers > kLayers)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "n_layers=%d out of range", cfg.n_layers);
-  if (cfg.kernels != QWEN_KERNELS_FUSED && cfg.kernels != QWEN_KERNELS_OPS)
+  if (cfg.kernels != QWEN_KERNELS_FUSED && cfg.kernels != QWEN_KERNELS_OPS &&
+      cfg.kernels != QWEN_KERNELS_TC)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "unknown kernels mode %d", cfg.kernels);
   if (cfg.kernels == QWEN_KERNELS_OPS && cfg.batch != 1)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "the per-op kernel path decodes one sequence");
@@ -323,7 +341,13 @@ int QwenEngine::load_weights(const std::string& dir) {
   if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_TRY(model_.load(dir, stream_));
+  QWEN_TRY(build_step_weights());
+  return QWEN_OK;
+}
+
+int QwenEngine::build_step_weights() {
   if (cfg_.kernels == QWEN_KERNELS_FUSED) QWEN_TRY(build_fused_weights(model_, cfg_.max_ctx, stream_));
+  if (cfg_.kernels == QWEN_KERNELS_TC) QWEN_TRY(build_tc_weights(model_, cfg_.max_ctx, stream_));
   return QWEN_OK;
 }
 
@@ -331,7 +355,7 @@ int QwenEngine::init_random(uint64_t seed) {
   if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_TRY(model_.init_random(seed, stream_));
-  if (cfg_.kernels == QWEN_KERNELS_FUSED) QWEN_TRY(build_fused_weights(model_, cfg_.max_ctx, stream_));
+  QWEN_TRY(build_step_weights());
   return QWEN_OK;
 }
 
@@ -404,6 +428,29 @@ int QwenEngine::enqueue_step_fused(cudaEvent_t* ev) {
   return launch_status("decode step (fused)");
 }
 
+int QwenEngine::enqueue_step_tc(cudaEvent_t* ev) {
+  InferenceManager& s = state_;
+  cudaStream_t st = stream_;
+  if (ev) cudaEventRecord(ev[0], st);
+  k_step_begin<<<s.batch, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
+                                        s.max_ctx, cfg_.seed, s.err, s.epoch);
+  if (ev) cudaEventRecord(ev[1], st);
+  QWEN_TRY(enqueue_tc_model(model_, state_, sm_count_, st));
+  if (ev) cudaEventRecord(ev[2], st);
+  if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
+                    s.sampled, nullptr, s.err, st) != 0)
+    return launch_status("sample");
+  k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
+  if (ev) cudaEventRecord(ev[3], st);
+  return launch_status("decode step (tensor cores)");
+}
+
+int QwenEngine::enqueue_step(cudaEvent_t* ev) {
+  if (cfg_.kernels == QWEN_KERNELS_OPS) return enqueue_step_ops(ev);
+  if (cfg_.kernels == QWEN_KERNELS_TC) return enqueue_step_tc(ev);
+  return enqueue_step_fused(ev);
+}
+
 int QwenEngine::ensure_graph() {
   if (graph_exec_) return QWEN_OK;
   if (!model_.loaded) return set_error(QWEN_ERR_STATE, "no weights: call load_weights or init_random");
@@ -414,8 +461,9 @@ int QwenEngine::ensure_graph() {
     QWEN_CUDA(cudaMemset(state_.fused_scratch, 0, bytes), "cudaMemset");
     state_.fused_scratch_bytes = bytes;
   }
+  if (cfg_.kernels == QWEN_KERNELS_TC) QWEN_TRY(tc_state_allocate(state_, sm_count_));
   QWEN_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "BeginCapture");
-  const int rc = cfg_.kernels == QWEN_KERNELS_OPS ? enqueue_step_ops(nullptr) : enqueue_step_fused(nullptr);
+  const int rc = enqueue_step(nullptr);
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamEndCapture(stream_, &g);
   if (rc != QWEN_OK) {
@@ -526,6 +574,8 @@ int QwenEngine::kernels_per_step(int* n) const {
   // step begin + sampler + step end around the model kernels
   if (cfg_.kernels == QWEN_KERNELS_OPS)
     *n = 3 + model_.n_layers * 18 + 2;
+  else if (cfg_.kernels == QWEN_KERNELS_TC)
+    *n = 3 + tc_kernels_per_step(model_.n_layers);
   else
     *n = 3 + 1;
   return QWEN_OK;
@@ -541,7 +591,7 @@ int QwenEngine::time_steps(int n, float* ms_step, float* ms_model) {
   int rc = QWEN_OK;
   for (int i = 0; i < n && rc == QWEN_OK; ++i) {
     cudaEvent_t* e = &ev[4 * i];
-    rc = cfg_.kernels == QWEN_KERNELS_OPS ? enqueue_step_ops(e) : enqueue_step_fused(e);
+    rc = enqueue_step(e);
   }
   if (rc == QWEN_OK) rc = cuda_status(cudaStreamSynchronize(stream_), "sync");
   double step = 0, model = 0;

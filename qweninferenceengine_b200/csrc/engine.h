@@ -75,6 +75,18 @@ struct FusedWeights {
   void release();
 };
 
+// Weights of the tensor-core batched step (tc_gemm.h blob layouts): per layer
+// the QKV (q, k, v rows concatenated: 16 tiles), O (12), gate/up (gate rows
+// then up rows: 140) and down (12) Q4 blobs back to back, and the fp16 LM head.
+struct TcWeights {
+  uint8_t* blob = nullptr;
+  size_t layer_bytes = 0;
+  uint8_t* lm = nullptr;
+  float* rope_cs = nullptr;         // [rope_ctx][64][2] cos, sin
+  int rope_ctx = 0;
+  void release();
+};
+
 // QwenModel.swift:11-35.
 class QwenModel {
  public:
@@ -90,6 +102,7 @@ class QwenModel {
   __half* final_norm = nullptr;
   __half* zero_bias = nullptr;   // the zero bias buffer of InferenceEngine.swift:82-85
   FusedWeights fused;
+  TcWeights tc;
   bool loaded = false;
 
  private:
@@ -134,6 +147,14 @@ class InferenceManager {
   int attn_splits = 0;
   void* fused_scratch = nullptr;
   size_t fused_scratch_bytes = 0;
+  // tensor-core batched step (tc_gemm.h layouts)
+  uint8_t* act_h = nullptr;      // activation tiles, k = 1536
+  uint8_t* act_i = nullptr;      // activation tiles, k = 8960
+  float* tc_part = nullptr;      // fp32 split-K partials
+  int tc_nb = 0;                 // activation rows (batch padded to 16)
+
+  // cudaMalloc + zero, freed with the state.
+  int alloc_tracked(size_t bytes, void** out);
 
   size_t kv_layer_stride() const { return (size_t)batch * max_ctx * 256; }
   size_t kv_seq_stride() const { return (size_t)max_ctx * 256; }
@@ -172,6 +193,9 @@ class QwenEngine {
   // start, model end, step end.
   int enqueue_step_ops(cudaEvent_t* ev);
   int enqueue_step_fused(cudaEvent_t* ev);
+  int enqueue_step_tc(cudaEvent_t* ev);
+  int enqueue_step(cudaEvent_t* ev);
+  int build_step_weights();
   int upload_prompt(const int32_t* prompt_ids, int32_t n_prompt, int32_t start_pos);
 
   qwen_engine_config cfg_{};
@@ -201,5 +225,13 @@ struct FusedStepArgs {
 int fused_scratch_bytes(int batch, int max_ctx, int sm_count, size_t* bytes);
 int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st);
 int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st);
+int upload_rope_table(float** cs_dev, int* ctx, int max_ctx, cudaStream_t st);
+
+// Tensor-core batched step (batched.cu): weights, state, and the model part of
+// one step for every sequence of the batch (x -> logits).
+int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st);
+int tc_state_allocate(InferenceManager& s, int sm_count);
+int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st);
+int tc_kernels_per_step(int n_layers);
 
 }  // namespace qwen

@@ -154,6 +154,31 @@ static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items
   begin[grid] = (uint32_t)items.size();
 }
 
+// RoPE cos/sin per position: theta = pos * 1e6^(-2i/128) in fp32 with libm,
+// exactly as rope.metal:25-32 evaluates it.  Table [ctx][64][2] (cos, sin).
+int upload_rope_table(float** cs_dev, int* ctx, int max_ctx, cudaStream_t st) {
+  if (*ctx < max_ctx) {
+    if (*cs_dev) cudaFree(*cs_dev);
+    *cs_dev = nullptr;
+    *ctx = 0;
+    QWEN_CUDA(cudaMalloc((void**)cs_dev, (size_t)max_ctx * 128 * sizeof(float)), "cudaMalloc(rope)");
+    *ctx = max_ctx;
+  }
+  float inv[64];
+  rope_inv_freq(inv);
+  std::vector<float> cs((size_t)max_ctx * 128);
+  for (int pos = 0; pos < max_ctx; ++pos)
+    for (int i = 0; i < 64; ++i) {
+      const float theta = (float)pos * inv[i];
+      cs[(size_t)pos * 128 + 2 * i] = std::cos(theta);
+      cs[(size_t)pos * 128 + 2 * i + 1] = std::sin(theta);
+    }
+  QWEN_CUDA(cudaMemcpyAsync(*cs_dev, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice, st),
+            "memcpy rope");
+  QWEN_CUDA(cudaStreamSynchronize(st), "sync");
+  return QWEN_OK;
+}
+
 int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
   FusedWeights& f = m.fused;
   auto alloc = [&](void** p, size_t bytes) { return cuda_status(cudaMalloc(p, bytes), "cudaMalloc(fused)"); };
@@ -197,28 +222,7 @@ int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
     k_repack_lm<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(m.embed, f.lm_tiles);
     QWEN_TRY(launch_status("repack_lm"));
   }
-  // RoPE cos/sin per position: theta = pos * 1e6^(-2i/128) in fp32 with libm,
-  // exactly as rope.metal:25-32 evaluates it.
-  if (f.rope_ctx < max_ctx) {
-    if (f.rope_cs) cudaFree(f.rope_cs);
-    f.rope_cs = nullptr;
-    QWEN_TRY(alloc((void**)&f.rope_cs, (size_t)max_ctx * 128 * sizeof(float)));
-    f.rope_ctx = max_ctx;
-  }
-  {
-    float inv[64];
-    rope_inv_freq(inv);
-    std::vector<float> cs((size_t)max_ctx * 128);
-    for (int pos = 0; pos < max_ctx; ++pos)
-      for (int i = 0; i < 64; ++i) {
-        const float theta = (float)pos * inv[i];
-        cs[(size_t)pos * 128 + 2 * i] = std::cos(theta);
-        cs[(size_t)pos * 128 + 2 * i + 1] = std::sin(theta);
-      }
-    QWEN_CUDA(cudaMemcpyAsync(f.rope_cs, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice, st),
-              "memcpy rope");
-    QWEN_CUDA(cudaStreamSynchronize(st), "sync");
-  }
+  QWEN_TRY(upload_rope_table(&f.rope_cs, &f.rope_ctx, max_ctx, st));
   // Work schedule for the current device's SM count.
   int dev = 0, sms = 0;
   QWEN_CUDA(cudaGetDevice(&dev), "cudaGetDevice");

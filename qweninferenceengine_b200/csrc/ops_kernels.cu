@@ -242,11 +242,6 @@ __global__ void k_residual_add(const __half* __restrict__ a, const __half* __res
   if (i < n) out[i] = __hadd(a[i], b[i]);
 }
 
-__device__ __forceinline__ float silu_ref(float x) {
-  if (x > 15.0f) return x;
-  if (x < -15.0f) return 0.0f;
-  return x / (1.0f + expf(-x));
-}
 
 __global__ void k_swiglu(__half* __restrict__ gate, const __half* __restrict__ up, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;

@@ -38,6 +38,13 @@ __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
 __device__ __forceinline__ __half f2h(float f) { return __float2half_rn(f); }
 __device__ __forceinline__ uint16_t hbits(__half h) { return __half_as_ushort(h); }
 
+// SiLU with the reference's clamps (activations.metal:9-27).
+__device__ __forceinline__ float silu_ref(float x) {
+  if (x > 15.0f) return x;
+  if (x < -15.0f) return 0.0f;
+  return x / (1.0f + expf(-x));
+}
+
 // --------------------------------------------------------------- errors ---
 __device__ __forceinline__ void raise_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);

@@ -8,7 +8,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (QWEN_KERNELS_FUSED, QWEN_KERNELS_OPS, EngineConfig, check, lib)
+from ._lib import (QWEN_KERNELS_FUSED, QWEN_KERNELS_OPS, QWEN_KERNELS_TC, EngineConfig, check,
+                   lib)
 
 STOP_TOKENS = (151645, 151643)  # InferenceEngine.swift:41
 
@@ -32,7 +33,7 @@ class QwenConfig:
     seed: int = 0
     batch: int = 1
     device: int = 0
-    kernels: str = "fused"   # "fused" or "ops"
+    kernels: str = "fused"   # "fused", "ops" or "tc" (tensor-core batched step)
     stop_on_eos: bool = True
 
 
@@ -53,7 +54,8 @@ class QwenEngine:
         cfg.max_ctx = c.max_context_window
         cfg.batch = c.batch
         cfg.n_layers = c.num_layers
-        cfg.kernels = {"fused": QWEN_KERNELS_FUSED, "ops": QWEN_KERNELS_OPS}[c.kernels]
+        cfg.kernels = {"fused": QWEN_KERNELS_FUSED, "ops": QWEN_KERNELS_OPS,
+                       "tc": QWEN_KERNELS_TC}[c.kernels]
         cfg.temperature = c.temperature
         cfg.top_p = c.top_p
         cfg.seed = c.seed

@@ -36,7 +36,7 @@ def small_model(oracle):
     return make_weight_dir(oracle, 2, 11)
 
 
-@pytest.mark.parametrize("kernels", ["ops", "fused"])
+@pytest.mark.parametrize("kernels", ["ops", "fused", "tc"])
 def test_engine_steps_match_oracle(cuda, oracle, small_model, kernels):
     cfg = QwenConfig(num_layers=2, max_context_window=64, temperature=0.0, kernels=kernels,
                      stop_on_eos=False)
@@ -61,7 +61,7 @@ def test_engine_steps_match_oracle(cuda, oracle, small_model, kernels):
     om.close()
 
 
-@pytest.mark.parametrize("kernels", ["ops", "fused"])
+@pytest.mark.parametrize("kernels", ["ops", "fused", "tc"])
 def test_engine_generate_greedy(cuda, oracle, small_model, kernels):
     cfg = QwenConfig(num_layers=2, max_context_window=64, temperature=0.0, kernels=kernels,
                      stop_on_eos=False)

@@ -1,0 +1,80 @@
+"""Batched decode on the tensor cores (kernels="tc"): every sequence of a batch
+against the CPU oracle stepping that sequence alone (InferenceEngine.swift:54-271
+per sequence; the batch shares nothing but the weights).
+
+Same tolerances as the batch-1 engine tests: logits max-abs <= 2e-2 and <= 1e-2
+of the logit range; greedy ids may part from the oracle only where its top-2
+margin is below the logit tolerance.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from qweninferenceengine_b200 import QwenConfig, QwenEngine  # noqa: E402
+from model_fixture import make_weight_dir  # noqa: E402
+from oracle_lib import OracleModel  # noqa: E402
+from test_gpu_engine import LOGIT_ABS, check_logits, top2_margin  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def small_model(oracle):
+    return make_weight_dir(oracle, 2, 11)
+
+
+def test_tc_batch_logits_match_oracle(cuda, oracle, small_model):
+    B, n = 3, 20
+    checks = (1, 7, 20)
+    prompts = np.random.default_rng(21).integers(0, 151936, size=(B, n)).astype(np.int32)
+    refs = {}
+    for b in range(B):
+        om = OracleModel(oracle, small_model, 2, 64)
+        for pos in range(n):
+            want = (pos + 1) in checks
+            lg = om.forward(int(prompts[b, pos]), pos, want_logits=want)
+            if want:
+                refs[(b, pos + 1)] = lg
+        om.close()
+    cfg = QwenConfig(num_layers=2, max_context_window=64, temperature=0.0, kernels="tc", batch=B,
+                     stop_on_eos=False)
+    eng = QwenEngine(small_model, cfg)
+    for m in checks:
+        eng.prefill(prompts[:, :m])   # positions 0 .. m-1 of every sequence
+        for b in range(B):
+            check_logits(eng.logits(b), refs[(b, m)])
+    k, v = eng.kv(2, 1, n)
+    om = OracleModel(oracle, small_model, 2, 64)
+    for pos in range(n):
+        om.forward(int(prompts[2, pos]), pos, want_logits=False)
+    assert np.abs(k.astype(np.float32) - om.k_cache(1)[:n].astype(np.float32)).max() < 2e-2
+    assert np.abs(v.astype(np.float32) - om.v_cache(1)[:n].astype(np.float32)).max() < 2e-2
+    om.close()
+    eng.close()
+
+
+def test_tc_batch_generate_greedy(cuda, oracle, small_model):
+    B, n, gen = 4, 9, 8
+    prompts = np.random.default_rng(22).integers(0, 151936, size=(B, n)).astype(np.int32)
+    cfg = QwenConfig(num_layers=2, max_context_window=64, temperature=0.0, kernels="tc", batch=B,
+                     stop_on_eos=False)
+    eng = QwenEngine(small_model, cfg)
+    outs = eng.generate(prompts, max_tokens=gen)
+    eng.close()
+    assert len(outs) == B
+    for b in range(B):
+        om = OracleModel(oracle, small_model, 2, 64)
+        for i in range(n - 1):
+            om.forward(int(prompts[b, i]), i, want_logits=False)
+        lg = om.forward(int(prompts[b, -1]), n - 1)
+        ref, margins = [], []
+        for j in range(gen):
+            cur = oracle.sample_greedy(lg)
+            ref.append(cur)
+            margins.append(top2_margin(lg))
+            if j + 1 < gen:
+                lg = om.forward(cur, n + j)
+        om.close()
+        assert len(outs[b]) == gen
+        diff = [j for j in range(gen) if outs[b][j] != ref[j]]
+        if diff:
+            assert margins[diff[0]] < LOGIT_ABS, f"seq {b} parts at step {diff[0]}"
