@@ -88,6 +88,7 @@ SIGNATURES = {
                                       ctypes.POINTER(c_size_t)]),
     "qwen_engine_time_steps": (c_int, [c_void_p, c_int32, ctypes.POINTER(c_float),
                                        ctypes.POINTER(c_float)]),
+    "qwen_engine_profile_step": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
 }
 
 _lib = None

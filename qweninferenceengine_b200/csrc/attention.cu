@@ -27,11 +27,27 @@ namespace {
 
 constexpr int kAttnWarps = 4;
 constexpr int kSub = 16;  // positions per warp sub-tile
+constexpr int kMinSplitLen = kAttnWarps * kSub;  // 64 positions: one sub-tile per warp
+constexpr int kMaxSplits = 32;                   // bounds the merge of one (sequence, kv head)
+constexpr int kAttnCtaTarget = 148 * 8;          // ~8 resident CTAs per SM
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(smem_u32(p)));
+}
+
+// Output element (seq, col): row-major out, or the activation tile layout
+// ([col/64][row][128 B], 16-byte chunk j of row r at (j ^ (r & 7))).
+__device__ __forceinline__ void store_out(const AttnParams& p, int seq, int col, float v) {
+  if (p.act_out) {
+    const int c = col >> 6, j = (col >> 3) & 7;
+    const size_t off = ((size_t)c * p.act_nb + seq) * 128 + (((uint32_t)j ^ (uint32_t)(seq & 7)) << 4) +
+                       (col & 7) * 2;
+    *reinterpret_cast<__half*>(p.act_out + off) = f2h(v);
+  } else {
+    p.out[(size_t)seq * p.out_seq_stride + col] = f2h(v);
+  }
 }
 
 }  // namespace
@@ -47,15 +63,20 @@ __global__ void __launch_bounds__(128) k_attention_decode(AttnParams p) {
   __shared__ float wo[kAttnWarps][6][kHeadDim];
   __shared__ uint32_t s_ticket;
 
+  // As a programmatic dependent: let the next kernel launch, then wait for the
+  // previous one (no-ops in a plain launch).
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
   const uint32_t L = p.seq_len[(size_t)seq * p.seq_len_stride];
   if (L == 0 || L > p.max_ctx) {
     if (threadIdx.x == 0 && split == 0 && kvh == 0) raise_error(p.err, kDevBadArgument);
     return;
   }
-  // Chunking: S = min(gridDim.x, ceil(L/16)) splits of a 16-multiple length.
+  // Chunking: S = min(gridDim.x, ceil(L/64)) splits of a 16-multiple length
+  // (at least one 16-position sub-tile per warp).
   const uint32_t max_s = gridDim.x;
-  uint32_t S = (L + kSub - 1) / kSub;
+  uint32_t S = (L + kMinSplitLen - 1) / kMinSplitLen;
   if (S > max_s) S = max_s;
   uint32_t chunk = (L + S - 1) / S;
   chunk = (chunk + kSub - 1) / kSub * kSub;
@@ -234,7 +255,7 @@ __global__ void __launch_bounds__(128) k_attention_decode(AttnParams p) {
       O += wo[w][head][d] * c;
     }
     if (S_eff == 1) {
-      p.out[(size_t)seq * p.out_seq_stride + (6 * kvh + head) * kHeadDim + d] = f2h(O / Lsum);
+      store_out(p, seq, (6 * kvh + head) * kHeadDim + d, O / Lsum);
     } else {
       part_o[idx] = O;
       if (d == 0) {
@@ -254,27 +275,45 @@ __global__ void __launch_bounds__(128) k_attention_decode(AttnParams p) {
   __threadfence();
   const float* all_o = p.part_o + unit * max_s * (6 * kHeadDim);
   const float* all_ml = p.part_ml + unit * max_s * 12;
-  for (int idx = threadIdx.x; idx < 6 * kHeadDim; idx += blockDim.x) {
-    const int head = idx / kHeadDim;
+  // Per head: the maximum over splits, each split's rescale factor and the
+  // total weight, staged once in shared memory (wo/wm are free by now).
+  float* sc = &wo[0][0][0];             // [S_eff][6] factors
+  float* hsum = &wo[1][0][0];           // [6] totals
+  if (threadIdx.x < 6) {
+    const int head = threadIdx.x;
     float M = -INFINITY;
     for (uint32_t sp = 0; sp < S_eff; ++sp) M = fmaxf(M, __ldcg(all_ml + sp * 12 + 2 * head));
-    float Lsum = 0.f, O = 0.f;
+    float Lsum = 0.f;
     for (uint32_t sp = 0; sp < S_eff; ++sp) {
       const float m = __ldcg(all_ml + sp * 12 + 2 * head);
-      if (m == -INFINITY) continue;
-      const float c = expf(m - M);
+      const float c = m == -INFINITY ? 0.f : expf(m - M);
+      sc[sp * 6 + head] = c;
       Lsum += __ldcg(all_ml + sp * 12 + 2 * head + 1) * c;
-      O += __ldcg(all_o + sp * (6 * kHeadDim) + idx) * c;
     }
-    p.out[(size_t)seq * p.out_seq_stride + (6 * kvh) * kHeadDim + idx] = f2h(O / Lsum);
+    hsum[head] = Lsum;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 6 * kHeadDim; idx += blockDim.x) {
+    const int head = idx / kHeadDim;
+    float part[kMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp)
+      part[sp] = (uint32_t)sp < S_eff ? __ldcg(all_o + sp * (6 * kHeadDim) + idx) : 0.f;
+    float O = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp)
+      if ((uint32_t)sp < S_eff) O += part[sp] * sc[sp * 6 + head];
+    store_out(p, seq, (6 * kvh) * kHeadDim + idx, O / hsum[head]);
   }
   if (threadIdx.x == 0) p.counters[unit] = 0;  // re-arm for the next launch
 }
 
+// Splits for a launch: enough CTAs for ~8 per SM over the batch, at least 64
+// positions per split, at most 32 splits (the merge reads them all).
 int attn_max_splits(int max_ctx, int n_seq) {
-  int s = (max_ctx + kSub - 1) / kSub;
-  const int target = (2 * 148) / (2 * (n_seq > 0 ? n_seq : 1));
-  const int cap = target < 1 ? 1 : target;
+  int s = (max_ctx + kMinSplitLen - 1) / kMinSplitLen;
+  const int target = kAttnCtaTarget / (kKVHeads * (n_seq > 0 ? n_seq : 1));
+  const int cap = target < 1 ? 1 : (target > kMaxSplits ? kMaxSplits : target);
   return s < cap ? s : cap;
 }
 
@@ -298,9 +337,18 @@ void attn_bind_scratch(AttnParams& p, void* scratch, int max_splits, int n_seq) 
   p.part_o = p.part_ml + units * max_splits * 12;
 }
 
-void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st) {
-  dim3 grid(max_splits, kKVHeads, n_seq);
-  k_attention_decode<<<grid, 128, 0, st>>>(p);
+void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st,
+                             bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(max_splits, kKVHeads, n_seq);
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k_attention_decode, p);
 }
 
 }  // namespace qwen

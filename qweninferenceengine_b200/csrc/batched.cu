@@ -10,8 +10,8 @@
 //   part  <- W_qkv . act_h                  tensor cores, K split
 //   q, K/V cache <- rope(half(part + b))    k_qkv_finish (rope.metal:12-39,
 //                                           attention.metal:67-84)
-//   attn  <- attention(q, cache)            split-K GQA decode attention
-//   act_h <- attn                           k_pack_act
+//   act_h <- attention(q, cache)            split-K GQA decode attention, written
+//                                           straight into the activation tiles
 //   part  <- W_o . act_h
 //   x     <- half(x + half(part + b_o)); act_h <- rmsnorm(x)   k_resid_norm_finish
 //   part  <- W_gu . act_h                   gate rows then up rows
@@ -49,105 +49,143 @@ __device__ __forceinline__ size_t act_off(int b, int i, int nb) {
   return ((size_t)c * nb + b) * 128 + (((uint32_t)j ^ (uint32_t)(b & 7)) << 4) + (i & 7) * 2;
 }
 
-// 1/sqrt(mean(x^2) + eps) of one 1536 row, 256 threads, the summation order
-// of k_rms_norm (rmsnorm.metal:9-46).  vals: this thread's 6 elements i = t + 256 j.
-__device__ __forceinline__ float rms_scale_row(const float (&vals)[6], float* red) {
+// Programmatic dependent launch: let the next kernel of the step launch (its
+// prologue overlaps this kernel), then wait until the previous kernel has
+// completed and its writes are visible.
+__device__ __forceinline__ void pdl_prologue() {
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), "launch");
+}
+
+constexpr int kTcMaxSplits = 24;  // split counts the plan may pick (checked on the host)
+
+// 1/sqrt(mean(x^2) + eps) of one 1536 row held by NT threads, PER values each
+// (rmsnorm.metal:9-46; fp32 sum of squares).
+template <int NT, int PER>
+__device__ __forceinline__ float rms_scale_row(const float (&vals)[PER], float* red) {
   float acc = 0.f;
 #pragma unroll
-  for (int j = 0; j < 6; ++j) acc += vals[j] * vals[j];
+  for (int j = 0; j < PER; ++j) acc += vals[j] * vals[j];
   acc = warp_sum(acc);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
   float tot = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) tot += red[w];
+  for (int w = 0; w < NT / 32; ++w) tot += red[w];
   return 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
 }
 
 // act row b <- half(half(x * s) * gamma).
-__global__ void __launch_bounds__(256) k_rms_to_act(const __half* __restrict__ x,
+__global__ void __launch_bounds__(512) k_rms_to_act(const __half* __restrict__ x,
                                                     const __half* __restrict__ gamma,
                                                     uint8_t* __restrict__ act, int nb) {
-  __shared__ float red[8];
+  pdl_prologue();
+  __shared__ float red[16];
   const int b = blockIdx.x;
   const __half* xr = x + (size_t)b * kHidden;
-  float v[6];
+  float v[3];
 #pragma unroll
-  for (int j = 0; j < 6; ++j) v[j] = h2f(xr[threadIdx.x + 256 * j]);
-  const float s = rms_scale_row(v, red);
+  for (int j = 0; j < 3; ++j) v[j] = h2f(xr[threadIdx.x + 512 * j]);
+  const float s = rms_scale_row<512, 3>(v, red);
 #pragma unroll
-  for (int j = 0; j < 6; ++j) {
-    const int i = threadIdx.x + 256 * j;
+  for (int j = 0; j < 3; ++j) {
+    const int i = threadIdx.x + 512 * j;
     *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v[j] * s), gamma[i]);
   }
 }
 
+// sum_sp part[sp][b][i] in split order; every load issued before the sum.
 __device__ __forceinline__ float sum_splits(const float* __restrict__ part, int splits, int nbv,
                                             int n, int b, int i) {
+  const size_t stride = (size_t)nbv * n, idx = (size_t)b * n + i;
+  float v[kTcMaxSplits];
+#pragma unroll
+  for (int sp = 0; sp < kTcMaxSplits; ++sp) v[sp] = sp < splits ? __ldcg(part + sp * stride + idx) : 0.f;
   float s = 0.f;
-  for (int sp = 0; sp < splits; ++sp) s += part[((size_t)sp * nbv + b) * n + i];
+#pragma unroll
+  for (int sp = 0; sp < kTcMaxSplits; ++sp)
+    if (sp < splits) s += v[sp];
   return s;
 }
 
-// QKV epilogue of one sequence: biases, fp16 rounding, RoPE at position
-// seq_len - 1 on q (12 heads) and k (2 heads), K/V appended to the cache.
-__global__ void __launch_bounds__(256) k_qkv_finish(const float* __restrict__ part, int splits, int nbv,
-                                                    const __half* __restrict__ bias,
-                                                    const float* __restrict__ rope_cs,
-                                                    const SeqCtl* __restrict__ ctl, int max_ctx,
-                                                    __half* __restrict__ q, __half* __restrict__ kc,
-                                                    __half* __restrict__ vc, size_t kv_seq_stride) {
-  __shared__ __half y[kQKVRows];
-  const int b = blockIdx.x;
-  for (int i = threadIdx.x; i < kQKVRows; i += 256)
-    y[i] = f2h(sum_splits(part, splits, nbv, kQKVRows, b, i) + h2f(bias[i]));
-  __syncthreads();
+// QKV epilogue, one CTA per (sequence, head): biases, fp16 rounding, RoPE at
+// position seq_len - 1 on the 12 q heads and 2 k heads (blockIdx.y < 14), K/V
+// appended to the cache (blockIdx.y 12..14).
+__global__ void __launch_bounds__(64) k_qkv_finish(const float* __restrict__ part, int splits, int nbv,
+                                                   const __half* __restrict__ bias,
+                                                   const float* __restrict__ rope_cs,
+                                                   const SeqCtl* __restrict__ ctl, int max_ctx,
+                                                   __half* __restrict__ q, __half* __restrict__ kc,
+                                                   __half* __restrict__ vc, size_t kv_seq_stride) {
+  pdl_prologue();
+  const int b = blockIdx.x, head = blockIdx.y, t = threadIdx.x;
   const uint32_t L = ctl[b].seq_len;
   const uint32_t pos = L - 1;
   if (L == 0 || pos >= (uint32_t)max_ctx) return;  // step_begin clamps; never taken
-  __half* kr = kc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
-  __half* vr = vc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
-  const float* cs = rope_cs + (size_t)pos * 128;
-  for (int p = threadIdx.x; p < (kHeads + kKVHeads) * 64; p += 256) {
-    const int head = p >> 6, pair = p & 63;
-    const int i0 = head * 128 + pair;  // q heads, then the k heads at 1536
-    const float c = cs[2 * pair], s = cs[2 * pair + 1];
-    const float x1 = h2f(y[i0]), x2 = h2f(y[i0 + 64]);
+  if (head < kHeads + kKVHeads) {
+    const int i0 = head * 128 + t;  // q heads, then the k heads at 1536
+    const float x1 = h2f(f2h(sum_splits(part, splits, nbv, kQKVRows, b, i0) + h2f(bias[i0])));
+    const float x2 =
+        h2f(f2h(sum_splits(part, splits, nbv, kQKVRows, b, i0 + 64) + h2f(bias[i0 + 64])));
+    const float* cs = rope_cs + (size_t)pos * 128;
+    const float c = cs[2 * t], s = cs[2 * t + 1];
     const __half r1 = f2h(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
     const __half r2 = f2h(__fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c)));
     if (head < kHeads) {
       q[(size_t)b * kHidden + i0] = r1;
       q[(size_t)b * kHidden + i0 + 64] = r2;
     } else {
+      __half* kr = kc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
       kr[i0 - kHidden] = r1;
       kr[i0 - kHidden + 64] = r2;
     }
+  } else {
+    __half* vr = vc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = kHidden + kKVDim + t + 64 * e;
+      vr[i - kHidden - kKVDim] = f2h(sum_splits(part, splits, nbv, kQKVRows, b, i) + h2f(bias[i]));
+    }
   }
-  for (int i = threadIdx.x; i < kKVDim; i += 256) vr[i] = y[kHidden + kKVDim + i];
 }
 
 // x <- half(x + half(sum + bias)); act_h row <- rmsnorm(x) with gamma.
-__global__ void __launch_bounds__(256) k_resid_norm_finish(const float* __restrict__ part, int splits,
+__global__ void __launch_bounds__(512) k_resid_norm_finish(const float* __restrict__ part, int splits,
                                                            int nbv, const __half* __restrict__ bias,
                                                            __half* __restrict__ x,
                                                            const __half* __restrict__ gamma,
                                                            uint8_t* __restrict__ act, int nb) {
-  __shared__ float red[8];
+  pdl_prologue();
+  __shared__ float red[16];
   const int b = blockIdx.x;
   __half* xr = x + (size_t)b * kHidden;
-  float v[6];
+  float v[3];
 #pragma unroll
-  for (int j = 0; j < 6; ++j) {
-    const int i = threadIdx.x + 256 * j;
+  for (int j = 0; j < 3; ++j) {
+    const int i = threadIdx.x + 512 * j;
     const __half y = f2h(sum_splits(part, splits, nbv, kHidden, b, i) + h2f(bias[i]));
     const __half xn = __hadd(xr[i], y);
     xr[i] = xn;
     v[j] = h2f(xn);
   }
-  const float s = rms_scale_row(v, red);
+  const float s = rms_scale_row<512, 3>(v, red);
 #pragma unroll
-  for (int j = 0; j < 6; ++j) {
-    const int i = threadIdx.x + 256 * j;
+  for (int j = 0; j < 3; ++j) {
+    const int i = threadIdx.x + 512 * j;
     *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v[j] * s), gamma[i]);
   }
 }
@@ -156,6 +194,7 @@ __global__ void __launch_bounds__(256) k_resid_norm_finish(const float* __restri
 // (zero biases, InferenceEngine.swift:82-85).
 __global__ void __launch_bounds__(256) k_swiglu_finish(const float* __restrict__ part, int splits,
                                                        int nbv, uint8_t* __restrict__ act, int nb) {
+  pdl_prologue();
   const int i = blockIdx.x * 256 + threadIdx.x;
   const int b = blockIdx.y;
   if (i >= kInter) return;
@@ -190,13 +229,14 @@ int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManage
   a.out = out;
   a.ld_out = ld_out;
   a.err = s.err;
+  a.pdl = true;
   if (launch_tc_gemm(a, st) != 0) return launch_status("tensor-core projection");
   return QWEN_OK;
 }
 
 }  // namespace
 
-int tc_kernels_per_step(int n_layers) { return 1 + 10 * n_layers + 1; }
+int tc_kernels_per_step(int n_layers) { return 1 + 9 * n_layers + 1; }
 
 int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
   TcWeights& t = m.tc;
@@ -246,11 +286,18 @@ int tc_state_allocate(InferenceManager& s, int sm_count) {
   return QWEN_OK;
 }
 
-int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st) {
+int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st,
+                     cudaEvent_t* marks, int* n_marks) {
+  // Optional per-launch timeline: an event after every kernel.
+  auto mark = [&]() {
+    if (marks) cudaEventRecord(marks[(*n_marks)++], st);
+  };
   const TcWeights& t = m.tc;
   if (!t.blob || !s.act_h) return set_error(QWEN_ERR_STATE, "tensor-core step not prepared");
   if (t.rope_ctx < s.max_ctx) return set_error(QWEN_ERR_STATE, "RoPE table shorter than max_ctx");
   const TcPlan p = plan_for(sm_count);
+  if (std::max(std::max(p.qkv, p.o), std::max(p.gu, p.down)) > kTcMaxSplits)
+    return set_error(QWEN_ERR_STATE, "tensor-core step: split plan exceeds %d", kTcMaxSplits);
   const int B = s.batch, nb = s.tc_nb;
   AttnParams ap{};
   ap.q = s.q;
@@ -263,10 +310,13 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
   ap.max_ctx = (uint32_t)s.max_ctx;
   ap.out = s.attn_out;
   ap.out_seq_stride = kHidden;
+  ap.act_out = s.act_h;  // the O projection's input tiles, written directly
+  ap.act_nb = nb;
   ap.err = s.err;
   attn_bind_scratch(ap, s.attn_scratch, s.attn_splits, B);
 
-  k_rms_to_act<<<B, 256, 0, st>>>(s.x, m.layers[0].input_norm, s.act_h, nb);
+  QWEN_TRY(launch_pdl(k_rms_to_act, dim3(B), dim3(512), st, s.x, m.layers[0].input_norm, s.act_h, nb));
+  mark();
   for (int l = 0; l < m.n_layers; ++l) {
     const QwenLayer& L = m.layers[l];
     const uint8_t* qkv = t.blob + t.layer_bytes * l;
@@ -277,24 +327,34 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
     __half* vc = s.vc + (size_t)l * s.kv_layer_stride();
 
     QWEN_TRY(gemm(qkv, true, s.act_h, s, kQKVRows, kHidden, p.qkv, s.tc_part, nullptr, 0, st));
-    k_qkv_finish<<<B, 256, 0, st>>>(s.tc_part, p.qkv, B, L.qkv_bias, t.rope_cs, s.ctl, s.max_ctx,
-                                    s.q, kc, vc, s.kv_seq_stride());
+    mark();
+    QWEN_TRY(launch_pdl(k_qkv_finish, dim3(B, kHeads + kKVHeads + 1), dim3(64), st, s.tc_part,
+                        p.qkv, B, L.qkv_bias, t.rope_cs, s.ctl, s.max_ctx, s.q, kc, vc,
+                        s.kv_seq_stride()));
+    mark();
     ap.k = kc;
     ap.v = vc;
-    launch_attention_decode(ap, s.attn_splits, B, st);
-    if (launch_pack_act(s.attn_out, kHidden, B, kHidden, nb, s.act_h, st) != 0)
-      return launch_status("pack attention output");
+    launch_attention_decode(ap, s.attn_splits, B, st, true);
+    mark();
     QWEN_TRY(gemm(o, true, s.act_h, s, kHidden, kHidden, p.o, s.tc_part, nullptr, 0, st));
-    k_resid_norm_finish<<<B, 256, 0, st>>>(s.tc_part, p.o, B, L.o_bias, s.x, L.post_attn_norm,
-                                           s.act_h, nb);
+    mark();
+    QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.o, B, L.o_bias,
+                        s.x, L.post_attn_norm, s.act_h, nb));
+    mark();
     QWEN_TRY(gemm(gu, true, s.act_h, s, 2 * kInter, kHidden, p.gu, s.tc_part, nullptr, 0, st));
-    k_swiglu_finish<<<dim3((kInter + 255) / 256, B), 256, 0, st>>>(s.tc_part, p.gu, B, s.act_i, nb);
+    mark();
+    QWEN_TRY(launch_pdl(k_swiglu_finish, dim3((kInter + 255) / 256, B), dim3(256), st, s.tc_part,
+                        p.gu, B, s.act_i, nb));
+    mark();
     QWEN_TRY(gemm(down, true, s.act_i, s, kHidden, kInter, p.down, s.tc_part, nullptr, 0, st));
+    mark();
     const __half* next_norm = l + 1 < m.n_layers ? m.layers[l + 1].input_norm : m.final_norm;
-    k_resid_norm_finish<<<B, 256, 0, st>>>(s.tc_part, p.down, B, L.down_bias, s.x, next_norm,
-                                           s.act_h, nb);
+    QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.down, B,
+                        L.down_bias, s.x, next_norm, s.act_h, nb));
+    mark();
   }
   QWEN_TRY(gemm(t.lm, false, s.act_h, s, kVocab, kHidden, 1, nullptr, s.logits, kVocab, st));
+  mark();
   return launch_status("tensor-core decode step");
 }
 

@@ -609,6 +609,42 @@ int QwenEngine::time_steps(int n, float* ms_step, float* ms_model) {
   return check_device_error();
 }
 
+// One eagerly launched step of the tensor-core path with an event after every
+// model kernel: ms[i] = device time from the previous launch's end to launch
+// i's end, in launch order (one entry per model kernel).
+int QwenEngine::profile_step(float* ms, int cap, int* n) {
+  if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
+  if (cfg_.kernels != QWEN_KERNELS_TC)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "per-launch profile: tensor-core step only");
+  QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
+  QWEN_TRY(ensure_graph());
+  const int need = tc_kernels_per_step(model_.n_layers);
+  *n = need;
+  if (!ms || cap < need) return QWEN_OK;
+  std::vector<cudaEvent_t> ev(need + 1);
+  for (auto& e : ev) QWEN_CUDA(cudaEventCreate(&e), "cudaEventCreate");
+  InferenceManager& s = state_;
+  cudaStream_t st = stream_;
+  k_step_begin<<<s.batch, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
+                                        s.max_ctx, cfg_.seed, s.err, s.epoch);
+  cudaEventRecord(ev[0], st);
+  int marks = 0;
+  int rc = enqueue_tc_model(model_, state_, sm_count_, st, ev.data() + 1, &marks);
+  if (rc == QWEN_OK && launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature,
+                                     cfg_.top_p, s.u24_, s.sampled, nullptr, s.err, st) != 0)
+    rc = launch_status("sample");
+  if (rc == QWEN_OK)
+    k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
+  if (rc == QWEN_OK) rc = cuda_status(cudaStreamSynchronize(st), "sync");
+  for (int i = 0; i < need && rc == QWEN_OK; ++i) {
+    if (i >= marks) { ms[i] = 0.f; continue; }
+    cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]);
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  QWEN_TRY(rc);
+  return check_device_error();
+}
+
 int QwenEngine::prefill(const int32_t* ids, int32_t n) {
   if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
   if (n < 1) return set_error(QWEN_ERR_INVALID_ARGUMENT, "empty prompt");
@@ -815,6 +851,14 @@ int qwen_engine_time_steps(qwen_engine* e, int32_t n_steps, float* ms_step, floa
   ENGINE_OR_FAIL(e);
   if (!ms_step || !ms_model) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
   return e->impl.time_steps(n_steps, ms_step, ms_model);
+}
+int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n) {
+  ENGINE_OR_FAIL(e);
+  if (!n) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
+  int v = 0;
+  const int rc = e->impl.profile_step(ms, cap, &v);
+  *n = v;
+  return rc;
 }
 int qwen_engine_stream(qwen_engine* e, void** stream) {
   ENGINE_OR_FAIL(e);

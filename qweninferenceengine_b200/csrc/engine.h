@@ -183,6 +183,7 @@ class QwenEngine {
   int set_trace(int enable);
   int get_trace(unsigned long long* host, size_t n, size_t* needed);
   int time_steps(int n, float* ms_step, float* ms_model);
+  int profile_step(float* ms, int cap, int* n);
   cudaStream_t stream() const { return stream_; }
 
  private:
@@ -231,7 +232,9 @@ int upload_rope_table(float** cs_dev, int* ctx, int max_ctx, cudaStream_t st);
 // one step for every sequence of the batch (x -> logits).
 int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st);
 int tc_state_allocate(InferenceManager& s, int sm_count);
-int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st);
+// marks (optional): an event is recorded after every launch, (*n_marks)++.
+int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st,
+                     cudaEvent_t* marks = nullptr, int* n_marks = nullptr);
 int tc_kernels_per_step(int n_layers);
 
 }  // namespace qwen

@@ -21,6 +21,8 @@ struct AttnParams {
   uint32_t max_ctx;         // L must be in [1, max_ctx]
   __half* out;              // [n_seq][1536]
   long long out_seq_stride;
+  uint8_t* act_out;         // if set: the output goes here instead, in the
+  int act_nb;               //   tensor-core activation tile layout of act_nb rows
   float* part_o;            // scratch: [n_seq][2][max_splits][6][128]
   float* part_ml;           // scratch: [n_seq][2][max_splits][6][2]
   uint32_t* counters;       // scratch: [n_seq][2], zero between launches
@@ -29,7 +31,9 @@ struct AttnParams {
 int attn_max_splits(int max_ctx, int n_seq);
 size_t attn_scratch_bytes(int max_splits, int n_seq);
 void attn_bind_scratch(AttnParams& p, void* scratch, int max_splits, int n_seq);
-void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st);
+// pdl: launch as a programmatic dependent of the previous kernel in the stream.
+void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st,
+                             bool pdl = false);
 
 // ------------------------------------------------------- op launchers ----
 int launch_gemv_q4_rowmajor(const uint8_t* packed, const __half* scales, const __half* x,

@@ -2,8 +2,11 @@
 //
 // CTA = 128 output rows x nb activation rows, K split over grid.y.  Six warps:
 //   warp 4      producer: one lane issues the 1-D bulk copies of each K chunk
-//               (weight blob chunk + activation chunk) into a 4-stage ring,
-//               completion as transaction bytes on full[s]
+//               into a 4-stage ring: the weight blob chunk (completion on
+//               wfull[s]) and the activation chunk (xfull[s]).  Launched as a
+//               programmatic dependent, the first stages' weights are fetched
+//               before griddepcontrol.wait, i.e. while the previous kernel of
+//               the stream still runs; activations only after it.
 //   warps 0..3  Q4: thread r dequantises row r of the chunk (16 nibble pairs
 //               -> fp16 via the 0x6400 exponent trick, (q - 8) exact, one
 //               rounding for the product with the block scale) into the
@@ -155,11 +158,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   const uint32_t xbytes = (uint32_t)nb * 128u;
   uint8_t* sR = sX + kTcStages * xbytes;                   // [S][4608] (Q4)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sR + (a.q4 ? kTcStages * kQ4TcChunkBytes : 0));
-  uint64_t* full = bars;
-  uint64_t* deq = bars + kTcStages;
-  uint64_t* empty = bars + 2 * kTcStages;
-  uint64_t* accum = bars + 3 * kTcStages;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * kTcStages + 1);
+  uint64_t* wfull = bars;
+  uint64_t* xfull = bars + kTcStages;
+  uint64_t* deq = bars + 2 * kTcStages;
+  uint64_t* empty = bars + 3 * kTcStages;
+  uint64_t* accum = bars + 4 * kTcStages;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4 * kTcStages + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -171,7 +175,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(full + s, 1);
+      mbar_init(wfull + s, 1);
+      mbar_init(xfull + s, 1);
       mbar_init(deq + s, kDeqThreads);
       mbar_init(empty + s, 1);
     }
@@ -188,24 +193,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
+  if (threadIdx.x == 0) pdl_launch_dependents();
   if (warp == 4) {
     // ---------------------------------------------------------- producer --
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       const uint32_t wbytes = a.q4 ? kQ4TcChunkBytes : kF16TcChunkBytes;
-      int i = 0;
+      auto load_w = [&](int i) {
+        const int s = i % kTcStages;
+        mbar_arrive_expect_tx(wfull + s, wbytes);
+        uint8_t* wdst = a.q4 ? sR + s * kQ4TcChunkBytes : sA + s * kF16TcChunkBytes;
+        bulk_g2s_stream(wdst, a.w + ((size_t)tile * n_chunks + c0 + i) * wbytes, wbytes, wfull + s,
+                        pol);
+      };
+      auto load_x = [&](int i) {
+        const int s = i % kTcStages;
+        mbar_arrive_expect_tx(xfull + s, xbytes);
+        bulk_g2s(sX + s * xbytes, a.act + (size_t)(c0 + i) * xbytes, xbytes, xfull + s);
+      };
+      const int pre = cps < kTcStages ? cps : kTcStages;
+      for (int i = 0; i < pre; ++i) load_w(i);  // weights do not depend on earlier kernels
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_x(i);
+      int i = pre;
       for (; i < cps; ++i) {
         const int s = i % kTcStages;
-        if (i >= kTcStages && !tc_wait(empty + s, ((i / kTcStages) - 1) & 1, abort, a.err)) break;
-        mbar_arrive_expect_tx(full + s, wbytes + xbytes);
-        const size_t c = (size_t)c0 + i;
-        uint8_t* wdst = a.q4 ? sR + s * kQ4TcChunkBytes : sA + s * kF16TcChunkBytes;
-        bulk_g2s_stream(wdst, a.w + ((size_t)tile * n_chunks + c) * wbytes, wbytes, full + s, pol);
-        bulk_g2s(sX + s * xbytes, a.act + c * xbytes, xbytes, full + s);
+        if (!tc_wait(empty + s, ((i / kTcStages) - 1) & 1, abort, a.err)) break;
+        load_w(i);
+        load_x(i);
       }
       // Every issued copy lands before the CTA may exit.
-      for (int j = i > kTcStages ? i - kTcStages : 0; j < i; ++j)
-        tc_wait(full + j % kTcStages, (j / kTcStages) & 1, abort, a.err, false);
+      for (int j = i > kTcStages ? i - kTcStages : 0; j < i; ++j) {
+        tc_wait(wfull + j % kTcStages, (j / kTcStages) & 1, abort, a.err, false);
+        tc_wait(xfull + j % kTcStages, (j / kTcStages) & 1, abort, a.err, false);
+      }
     }
     __syncwarp();
   } else if (warp == 5) {
@@ -214,7 +235,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
       const uint32_t idesc = f16_idesc(kTcM, nb);
       for (int i = 0; i < cps; ++i) {
         const int s = i % kTcStages;
-        if (!tc_wait(a.q4 ? deq + s : full + s, (i / kTcStages) & 1, abort, a.err)) break;
+        if (!tc_wait(a.q4 ? deq + s : wfull + s, (i / kTcStages) & 1, abort, a.err)) break;
+        if (!tc_wait(xfull + s, (i / kTcStages) & 1, abort, a.err)) break;
         tc_fence_after();
         const uint64_t ad = sw128_kmajor_desc(smem_u32(sA + s * kF16TcChunkBytes));
         const uint64_t bd = sw128_kmajor_desc(smem_u32(sX + s * xbytes));
@@ -232,7 +254,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     if (a.q4) {
       for (int i = 0; i < cps; ++i) {
         const int s = i % kTcStages;
-        if (!tc_wait(full + s, (i / kTcStages) & 1, abort, a.err)) break;
+        if (!tc_wait(wfull + s, (i / kTcStages) & 1, abort, a.err)) break;
         const uint8_t* raw = sR + s * kQ4TcChunkBytes;
         const uint4 p0 = *reinterpret_cast<const uint4*>(raw + r * 16);
         const uint4 p1 = *reinterpret_cast<const uint4*>(raw + 2048 + r * 16);
@@ -253,6 +275,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
       }
     }
     // ---------------------------------------------------------- epilogue --
+    pdl_wait();  // outputs are written only after the previous kernel completed
     const bool landed = tc_wait(accum, 0, abort, a.err, false);
     tc_fence_after();
     // tcgen05.ld is warp-collective: the decision is the warp's, not the lane's.
@@ -360,7 +383,7 @@ inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threa
 
 size_t tc_gemm_smem_bytes(int nb, bool q4) {
   return 1024 + (size_t)kTcStages * kF16TcChunkBytes + (size_t)kTcStages * nb * 128 +
-         (q4 ? (size_t)kTcStages * kQ4TcChunkBytes : 0) + (3 * kTcStages + 1) * 8 + 16;
+         (q4 ? (size_t)kTcStages * kQ4TcChunkBytes : 0) + (4 * kTcStages + 1) * 8 + 16;
 }
 
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
@@ -373,8 +396,17 @@ int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
   if (cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return -1;
-  k_tc_gemm<<<dim3(a.n_rows / kTcM, a.splits), kTcThreads, smem, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_rows / kTcM, a.splits);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_tc_gemm, a) == cudaSuccess ? 0 : -1;
 }
 
 int launch_repack_q4_tc(const uint8_t* packed, const __half* scales, int n_rows, int k,

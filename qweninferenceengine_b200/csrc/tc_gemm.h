@@ -56,6 +56,7 @@ struct TcGemmArgs {
   __half* out = nullptr;       //   fp16 results out[b * ld_out + n] (splits == 1)
   long long ld_out = 0;
   int* err = nullptr;
+  bool pdl = false;            // launch as a programmatic dependent of the previous kernel
 };
 
 // K splits for a launch: the largest divisor d of the chunk count with

@@ -162,6 +162,19 @@ class QwenEngine:
         check(lib().qwen_engine_time_steps(self._h, n_steps, ctypes.byref(a), ctypes.byref(b)))
         return a.value, b.value
 
+    def profile_step(self) -> list:
+        """Tensor-core step only: [(kernel, ms)] for one eagerly launched step, a
+        CUDA event after every model kernel (advances every sequence one step)."""
+        n = ctypes.c_int32()
+        check(lib().qwen_engine_profile_step(self._h, None, 0, ctypes.byref(n)))
+        ms = np.zeros(n.value, np.float32)
+        check(lib().qwen_engine_profile_step(self._h, ms.ctypes.data_as(ctypes.c_void_p), n.value,
+                                             ctypes.byref(n)))
+        per_layer = ["qkv_gemm", "qkv_finish", "attention", "o_gemm", "o_finish", "gu_gemm",
+                     "swiglu_finish", "down_gemm", "down_finish"]
+        names = ["rmsnorm"] + per_layer * ((n.value - 2) // len(per_layer)) + ["lm_gemm"]
+        return list(zip(names, ms.tolist()))
+
     def trace(self, enable: bool = True) -> None:
         """Per-CTA phase timestamps of the fused step (see qwen_engine_trace)."""
         check(lib().qwen_engine_trace(self._h, 1 if enable else 0))
