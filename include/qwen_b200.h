@@ -95,6 +95,16 @@ int qwen_attention_decode(const uint16_t* q, const uint16_t* k_cache, const uint
                           uint16_t* out, const uint32_t* seq_len, uint32_t max_ctx,
                           void* stream);
 
+/* qwen_attention_decode for n_seq independent sequences in one launch (the
+ * tensor-core batched step's attention): q [n_seq][1536]; caches
+ * [n_seq][max_ctx][256] (reference row layout per sequence); seq_len[n_seq]
+ * device lengths in [1, max_ctx]; out [n_seq][1536].  Scratch from
+ * stream-ordered allocations. */
+int qwen_attention_decode_batched(const uint16_t* q, const uint16_t* k_cache,
+                                  const uint16_t* v_cache, uint16_t* out,
+                                  const uint32_t* seq_len, uint32_t n_seq, uint32_t max_ctx,
+                                  void* stream);
+
 /* qwen_attention_decode without any device allocation.  No counterpart in the
  * reference (it has no allocation-free entry points): this is for callers that
  * may not call cudaMalloc -- code running while another component holds a

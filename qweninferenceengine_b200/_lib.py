@@ -49,6 +49,8 @@ SIGNATURES = {
     "qwen_gemv_fp16": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p]),
     "qwen_gemm_q4_0_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_uint32, c_void_p,
                                        c_uint32, c_uint32, c_void_p]),
+    "qwen_attention_decode_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                              c_uint32, c_uint32, c_void_p]),
     "qwen_gemm_fp16_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32,
                                        c_void_p]),
     "qwen_rms_norm_q4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -1,23 +1,35 @@
 // attention.cu -- split-K GQA decode attention (flash-decoding) for 12 query
-// heads over 2 KV heads, head_dim 128, FP16 KV cache.
+// heads over 2 KV heads, head_dim 128, FP16 KV cache, any number of sequences.
 //
 // Replaces attention_scores -> softmax -> attn_weighted_sum
 // (attention.metal:9-56, activations.metal:29-55; InferenceEngine.swift:162-182):
 //   s_t = 0.088388 * q_h . K_t,   p_t = exp(s_t - max) / sum,   o_h = sum_t p_t V_t
 // evaluated as an online softmax over position chunks.
 //
-// Grid (splits, 2 kv heads, sequences).  A CTA owns one chunk of positions of
-// one (sequence, kv head) and serves all 6 query heads of that group from a
-// single read of K and V.  Each of its 4 warps walks 16-position sub-tiles:
-//   S^T[16 pos x 8 heads] = K[16 x 128] . q^T   (8 m16n8k16 MMAs, K straight
-//                                                from global, q in registers)
-//   o^T[128 x 8]        += V^T[128 x 16] . P^T  (V staged in shared memory and
-//                                                read with ldmatrix.trans; P is
-//                                                split into fp16 hi + lo parts so
-//                                                the product keeps ~22 bits)
-// Warps merge in shared memory; chunks merge in a fixed order by the last CTA
-// of the (sequence, kv head) to finish (an atomic ticket -- nothing waits), so
-// results do not depend on scheduling.
+// Persistent grid (one CTA per SM) over work units = (sequence, split): a
+// split is a run of 64-position tiles of one sequence, covering both kv heads.
+//   warp 8      producer: per tile, one lane issues 8 TMA tile loads from 2-D
+//               tensor maps over the K and V caches (rows = positions, 256
+//               fp16 per row): boxes of 64 positions x 64 elements with the
+//               128-byte swizzle, so the K fragment loads and the V
+//               ldmatrix.trans reads hit distinct banks; a 3-stage ring
+//               (192 KB in flight per SM);
+//               the ring runs on across units, so loads of the next unit
+//               overlap the merge of this one
+//   warps 0..7  warp w serves kv head w/4 (query heads 6h..6h+5) on positions
+//               16(w%4) .. +16 of every tile:
+//                 S^T[16 pos x 8 heads] = K[16 x 128] . q^T   (8 m16n8k16 MMAs)
+//                 o^T[128 x 8]        += V^T[128 x 16] . P^T  (V by
+//                     ldmatrix.trans; P split into fp16 hi + lo parts so the
+//                     product keeps ~22 bits)
+// The 4 warps of a head merge in shared memory; splits merge in a fixed order
+// by the last CTA of the sequence to finish (an atomic ticket -- nothing
+// waits), so results do not depend on scheduling.  Waits are bounded (2 s).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "qwen_common.cuh"
 #include "qwen_internal.h"
 
@@ -25,16 +37,75 @@ namespace qwen {
 
 namespace {
 
-constexpr int kAttnWarps = 4;
-constexpr int kSub = 16;  // positions per warp sub-tile
-constexpr int kMinSplitLen = kAttnWarps * kSub;  // 64 positions: one sub-tile per warp
-constexpr int kMaxSplits = 32;                   // bounds the merge of one (sequence, kv head)
-constexpr int kAttnCtaTarget = 148 * 8;          // ~8 resident CTAs per SM
+constexpr int kTilePos = 64;                        // positions per ring stage
+constexpr int kSub = 16;                            // positions per warp sub-tile
+constexpr int kConsumerWarps = 8;
+constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 3;
+constexpr int kBoxBytes = kTilePos * 128;          // 64 positions x 64 fp16, swizzled
+constexpr int kBoxes = 4;                           // 256 fp16 per position: 2 heads x 2
+constexpr int kMaxSplits = 32;                      // bounds the merge of a sequence
+constexpr int kUnitsPerSm = 1;                      // work units per SM to aim for (each costs a merge)
+constexpr unsigned long long kAttnWaitNs = 2000000000ull;
+
+struct AttnSmem {
+  uint8_t k[kStages][kBoxes][kBoxBytes];            // 1024-byte aligned (swizzle atoms)
+  uint8_t v[kStages][kBoxes][kBoxBytes];
+  uint16_t pt[kConsumerWarps][2][kSub * 8];        // P^T hi/lo, [pos][head]
+  float wm[kConsumerWarps][8], wl[kConsumerWarps][8];
+  float wo[kConsumerWarps][6][kHeadDim];
+  float sc[2][kMaxSplits][8];                      // split merge factors [head group][split][head]
+  float hsum[2][8];
+  uint64_t full[kStages], empty[kStages];
+  uint32_t ticket;
+  int abort;
+  int unit_abort;   // abort as seen by the merge of the running unit (uniform)
+};
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(smem_u32(p)));
+}
+// 2-D TMA tile load (box of the tensor map at element x, row y) into shared
+// memory, completion as transaction bytes on bar.  x is a multiple of 64
+// elements (128 B).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// Byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return (uint32_t)row * 128u + ((uint32_t)(chunk ^ (row & 7)) << 4);
+}
+// Barrier of the 8 consumer warps (the producer warp does not take part).
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded parity wait; on timeout records kDevWaitTimeout and sets abort.
+__device__ bool attn_wait(uint64_t* bar, uint32_t parity, AttnSmem& s, int* err,
+                          bool honour_abort = true) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = gtime();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (honour_abort && *((volatile int*)&s.abort)) return false;
+      if (gtime() - t0 > kAttnWaitNs) {
+        *((volatile int*)&s.abort) = 1;
+        raise_error(err, kDevWaitTimeout);
+        return false;
+      }
+    }
+  }
 }
 
 // Output element (seq, col): row-major out, or the activation tile layout
@@ -42,279 +113,347 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
 __device__ __forceinline__ void store_out(const AttnParams& p, int seq, int col, float v) {
   if (p.act_out) {
     const int c = col >> 6, j = (col >> 3) & 7;
-    const size_t off = ((size_t)c * p.act_nb + seq) * 128 + (((uint32_t)j ^ (uint32_t)(seq & 7)) << 4) +
-                       (col & 7) * 2;
+    const size_t off = ((size_t)c * p.act_nb + seq) * 128 +
+                       (((uint32_t)j ^ (uint32_t)(seq & 7)) << 4) + (col & 7) * 2;
     *reinterpret_cast<__half*>(p.act_out + off) = f2h(v);
   } else {
     p.out[(size_t)seq * p.out_seq_stride + col] = f2h(v);
   }
 }
 
+struct Unit {
+  int seq, split;
+  uint32_t p0, p1, s_eff;
+};
+// Unit u = (sequence u / max_s, split u % max_s): n_tiles = ceil(L/64) tiles
+// in S = min(max_s, n_tiles) near-equal runs; false if the split is empty.
+__device__ __forceinline__ bool unit_of(const AttnParams& p, int u, int max_s, Unit& w) {
+  w.seq = u / max_s;
+  w.split = u % max_s;
+  const uint32_t L = p.seq_len[(size_t)w.seq * p.seq_len_stride];
+  if (L == 0 || L > p.max_ctx) return false;
+  const uint32_t n_tiles = (L + kTilePos - 1) / kTilePos;
+  const uint32_t S = n_tiles < (uint32_t)max_s ? n_tiles : (uint32_t)max_s;
+  const uint32_t tps = (n_tiles + S - 1) / S;
+  w.s_eff = (n_tiles + tps - 1) / tps;
+  if ((uint32_t)w.split >= w.s_eff) return false;
+  w.p0 = (uint32_t)w.split * tps * kTilePos;
+  w.p1 = min(L, w.p0 + tps * kTilePos);
+  return true;
+}
+
 }  // namespace
 
-// V sub-tile rows are padded to 272 B so the 8 row addresses of each
-// ldmatrix phase fall in distinct banks.
-constexpr int kVRowBytes = 272;
-
-__global__ void __launch_bounds__(128) k_attention_decode(AttnParams p) {
-  __shared__ __align__(16) uint8_t vs[kAttnWarps][kSub * kVRowBytes];
-  __shared__ __align__(16) uint16_t pt[kAttnWarps][2][kSub * 8];  // P^T hi/lo, [pos][head]
-  __shared__ float wm[kAttnWarps][8], wl[kAttnWarps][8];
-  __shared__ float wo[kAttnWarps][6][kHeadDim];
-  __shared__ uint32_t s_ticket;
-
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    k_attention_decode(AttnParams p, int max_s, int n_units, int rows_per_seq,
+                       const __grid_constant__ CUtensorMap tmk,
+                       const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ uint8_t attn_smem_raw[];
+  AttnSmem& s = *reinterpret_cast<AttnSmem*>(
+      attn_smem_raw + ((1024u - (smem_u32(attn_smem_raw) & 1023u)) & 1023u));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], kConsumerWarps);
+    }
+    s.abort = 0;
+    fence_mbar_init();
+  }
   // As a programmatic dependent: let the next kernel launch, then wait for the
   // previous one (no-ops in a plain launch).
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
-  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
-  const uint32_t L = p.seq_len[(size_t)seq * p.seq_len_stride];
-  if (L == 0 || L > p.max_ctx) {
-    if (threadIdx.x == 0 && split == 0 && kvh == 0) raise_error(p.err, kDevBadArgument);
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer --
+    uint32_t it = 0;
+    if (lane == 0) {
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        Unit w;
+        if (!unit_of(p, u, max_s, w)) continue;
+        const int row0 = w.seq * rows_per_seq;
+        for (uint32_t base = w.p0; base < w.p1; base += kTilePos, ++it) {
+          const int st = it % kStages;
+          if (it >= kStages && !attn_wait(&s.empty[st], ((it / kStages) - 1) & 1, s, p.err))
+            continue;  // aborting: keep the tile count, issue nothing
+          mbar_arrive_expect_tx(&s.full[st], 2 * kBoxes * kBoxBytes);
+#pragma unroll
+          for (int b = 0; b < kBoxes; ++b) {
+            tma_load_2d(s.k[st][b], &tmk, 64 * b, row0 + (int)base, &s.full[st]);
+            tma_load_2d(s.v[st][b], &tmv, 64 * b, row0 + (int)base, &s.full[st]);
+          }
+        }
+      }
+      // Every issued copy lands before the CTA may exit.
+      for (uint32_t j = it > kStages ? it - kStages : 0; j < it; ++j)
+        attn_wait(&s.full[j % kStages], (j / kStages) & 1, s, p.err, false);
+    }
+    __syncwarp();
     return;
   }
-  // Chunking: S = min(gridDim.x, ceil(L/64)) splits of a 16-multiple length
-  // (at least one 16-position sub-tile per warp).
-  const uint32_t max_s = gridDim.x;
-  uint32_t S = (L + kMinSplitLen - 1) / kMinSplitLen;
-  if (S > max_s) S = max_s;
-  uint32_t chunk = (L + S - 1) / S;
-  chunk = (chunk + kSub - 1) / kSub * kSub;
-  const uint32_t S_eff = (L + chunk - 1) / chunk;
-  if ((uint32_t)split >= S_eff) return;
-  const uint32_t p0 = split * chunk;
-  const uint32_t p1 = min(L, p0 + chunk);
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const __half* kbase = p.k + (size_t)seq * p.kv_seq_stride + (size_t)kvh * p.kv_head_stride;
-  const __half* vbase = p.v + (size_t)seq * p.kv_seq_stride + (size_t)kvh * p.kv_head_stride;
-
-  // q fragments: lane (g,t) holds q[head 6*kvh + g][32t .. 32t+31] (zero for g >= 6).
-  uint32_t qf[16];
-  {
-    const bool hv = g < 6;
-    const uint4* qp = reinterpret_cast<const uint4*>(p.q + (size_t)seq * p.q_seq_stride +
-                                                     (size_t)(6 * kvh + (hv ? g : 0)) * kHeadDim +
-                                                     32 * t);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 v = hv ? qp[j] : make_uint4(0, 0, 0, 0);
-      qf[4 * j + 0] = v.x;
-      qf[4 * j + 1] = v.y;
-      qf[4 * j + 2] = v.z;
-      qf[4 * j + 3] = v.w;
+  // -------------------------------------------------------------- consumers --
+  const int h = warp >> 2, slice = warp & 3;     // kv head, 16-row slice of a tile
+  const int g = lane >> 2, t = lane & 3;
+  const int ctid = threadIdx.x;                  // 0..255
+  const int htid = ctid & 127;                   // thread within the head group
+  uint32_t it = 0;
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    Unit w;
+    if (!unit_of(p, u, max_s, w)) {
+      if (ctid == 0 && u % max_s == 0) {
+        const uint32_t L = p.seq_len[(size_t)(u / max_s) * p.seq_len_stride];
+        if (L == 0 || L > p.max_ctx) raise_error(p.err, kDevBadArgument);
+      }
+      continue;
     }
-  }
-
-  // Running state for heads 2t, 2t+1 (replicated over g).
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float o[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-  for (uint32_t base = p0 + warp * kSub; base < p1; base += kAttnWarps * kSub) {
-    // ---- stage V rows [base, base+16) into shared memory (zero past p1).
+    // q fragments: lane (g,t) holds q[head 6h + g][32t .. 32t+31] (zero for g >= 6).
+    uint32_t qf[16];
     {
-      const int r = lane >> 1, half_sel = lane & 1;
-      const uint32_t pos = base + r;
-      uint8_t* dst = vs[warp] + r * kVRowBytes + half_sel * 128;
-      if (pos < p1) {
-        const uint4* src = reinterpret_cast<const uint4*>(vbase + (size_t)pos * p.kv_pos_stride) +
-                           half_sel * 8;
+      const bool hv = g < 6;
+      const uint4* qp = reinterpret_cast<const uint4*>(
+          p.q + (size_t)w.seq * p.q_seq_stride + (size_t)(6 * h + (hv ? g : 0)) * kHeadDim + 32 * t);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(dst)[j] = src[j];
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = hv ? qp[j] : make_uint4(0, 0, 0, 0);
+        qf[4 * j + 0] = v.x;
+        qf[4 * j + 1] = v.y;
+        qf[4 * j + 2] = v.z;
+        qf[4 * j + 3] = v.w;
+      }
+    }
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+    for (uint32_t tb = w.p0; tb < w.p1; tb += kTilePos, ++it) {
+      const int st = it % kStages;
+      bool ok = true;
+      if (lane == 0) ok = attn_wait(&s.full[st], (it / kStages) & 1, s, p.err);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      const uint32_t base = tb + 16 * slice;
+      const int r0 = 16 * slice;  // first row of this warp in the boxes
+      bool zeroed = false;
+      if (ok && base < w.p1) {
+        // ---- S^T = K q^T: lane reads K[row g][32t..32t+31] and K[row g+8][..].
+        float sv[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          uint32_t kg[16], kg8[16];
+          // d = 32t + 8j: box 2h + t/2, chunk 4(t&1) + j of rows r0+g, r0+g+8.
+          const uint8_t* kbox = s.k[st][2 * h + (t >> 1)];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 a = *reinterpret_cast<const uint4*>(kbox + swz(r0 + g, 4 * (t & 1) + j));
+            const uint4 b = *reinterpret_cast<const uint4*>(kbox + swz(r0 + g + 8, 4 * (t & 1) + j));
+            kg[4 * j] = a.x; kg[4 * j + 1] = a.y; kg[4 * j + 2] = a.z; kg[4 * j + 3] = a.w;
+            kg8[4 * j] = b.x; kg8[4 * j + 1] = b.y; kg8[4 * j + 2] = b.z; kg8[4 * j + 3] = b.w;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            // mma-k (2t,2t+1) <-> d = 32t+4q, +1 ; (2t+8, 2t+9) <-> d = 32t+4q+2, +3
+            const uint32_t a[4] = {kg[2 * q], kg8[2 * q], kg[2 * q + 1], kg8[2 * q + 1]};
+            mma_16816(sv, a, qf[2 * q], qf[2 * q + 1], sv);
+          }
+          // sv[0]: (pos g, head 2t) sv[1]: (pos g, head 2t+1)
+          // sv[2]: (pos g+8, head 2t) sv[3]: (pos g+8, head 2t+1)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sv[j] *= kAttnScale;
+          if (base + g >= w.p1) sv[0] = sv[1] = -INFINITY;
+          if (base + g + 8 >= w.p1) sv[2] = sv[3] = -INFINITY;
+        }
+        // ---- online softmax for heads 2t and 2t+1.
+        float pr[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float mx = fmaxf(sv[hh], sv[2 + hh]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float m_new = fmaxf(m_run[hh], mx);
+          const float corr = m_run[hh] == -INFINITY ? 0.f : expf(m_run[hh] - m_new);
+          const float e0 = expf(sv[hh] - m_new), e1 = expf(sv[2 + hh] - m_new);
+          pr[hh] = e0;
+          pr[2 + hh] = e1;
+          float sum = e0 + e1;
+          sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+          l_run[hh] = l_run[hh] * corr + sum;
+          m_run[hh] = m_new;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            o[i][hh] *= corr;
+            o[i][2 + hh] *= corr;
+          }
+        }
+        // ---- P^T to shared memory as fp16 hi/lo: pt[pos][head].
+        {
+          uint16_t* hi = s.pt[warp][0];
+          uint16_t* lo = s.pt[warp][1];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int pos = g + (j >= 2 ? 8 : 0), head = 2 * t + (j & 1);
+            const __half hv = f2h(pr[j]);
+            const __half lv = f2h(pr[j] - h2f(hv));
+            hi[pos * 8 + head] = hbits(hv);
+            lo[pos * 8 + head] = hbits(lv);
+          }
+        }
+        // Rows past the end hold stale data: zero this head's half (P is 0
+        // there, but 0 * NaN would not be).
+        if (base + 16 > w.p1) {
+          for (int r = (int)(w.p1 - base); r < 16; ++r)
+            if (lane < 16)  // both boxes of this head, whole 128-byte rows
+              *reinterpret_cast<uint4*>(s.v[st][2 * h + (lane >> 3)] + (r0 + r) * 128 +
+                                        (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
+          zeroed = true;
+        }
+        __syncwarp();
+        // B fragments (k = pos, n = head): lane (g,t): (pos 2t, 2t+1 ; head g), (pos 2t+8, 2t+9 ; head g)
+        uint32_t bh0, bh1, bl0, bl1;
+        {
+          const uint16_t* hi = s.pt[warp][0];
+          const uint16_t* lo = s.pt[warp][1];
+          bh0 = (uint32_t)hi[(2 * t) * 8 + g] | ((uint32_t)hi[(2 * t + 1) * 8 + g] << 16);
+          bh1 = (uint32_t)hi[(2 * t + 8) * 8 + g] | ((uint32_t)hi[(2 * t + 9) * 8 + g] << 16);
+          bl0 = (uint32_t)lo[(2 * t) * 8 + g] | ((uint32_t)lo[(2 * t + 1) * 8 + g] << 16);
+          bl1 = (uint32_t)lo[(2 * t + 8) * 8 + g] | ((uint32_t)lo[(2 * t + 9) * 8 + g] << 16);
+        }
+        // ---- o^T += V^T P^T over the 8 d-tiles: A = V^T[16 d x 16 pos] by
+        // ldmatrix.trans of V rows: matrices (pos 0-7, d 0-7), (pos 0-7, d 8-15),
+        // (pos 8-15, d 0-7), (pos 8-15, d 8-15).
+        {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int prow = ri + ((mi >> 1) << 3);
+          const int dcol = (mi & 1) << 3;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            // d = 16i + dcol: box 2h + i/4, chunk 2(i&3) + dcol/8.
+            uint32_t a[4];
+            ldmatrix_x4_trans(a, s.v[st][2 * h + (i >> 2)] + swz(r0 + prow, 2 * (i & 3) + (dcol >> 3)));
+            mma_16816(o[i], a, bh0, bh1, o[i]);
+            mma_16816(o[i], a, bl0, bl1, o[i]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        if (zeroed) fence_proxy_async();  // generic stores before the next TMA write
+        mbar_arrive(&s.empty[st]);
+      }
+    }
+
+    // ---- merge the 4 warps of each head group.  o[i][0]: (d 16i+g, head 2t)
+    // o[i][1]: (d 16i+g, head 2t+1) o[i][2]: (d 16i+g+8, head 2t) o[i][3]: (d 16i+g+8, head 2t+1)
+    if (g == 0) {
+      s.wm[warp][2 * t] = m_run[0];
+      s.wm[warp][2 * t + 1] = m_run[1];
+      s.wl[warp][2 * t] = l_run[0];
+      s.wl[warp][2 * t + 1] = l_run[1];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int head = 2 * t + (j & 1), d = 16 * i + g + (j >= 2 ? 8 : 0);
+        if (head < 6) s.wo[warp][head][d] = o[i][j];
+      }
+    // One snapshot of the abort flag, so every consumer thread takes the same
+    // barriers below.
+    if (ctid == 0) s.unit_abort = *((volatile int*)&s.abort);
+    consumers_sync();
+    const bool aborting = s.unit_abort != 0;
+    const size_t pidx = ((size_t)w.seq * max_s + w.split) * 2 + h;
+    float* part_o = p.part_o + pidx * (6 * kHeadDim);
+    float* part_ml = p.part_ml + pidx * 12;
+    for (int idx = htid; idx < 6 * kHeadDim && !aborting; idx += 128) {
+      const int head = idx / kHeadDim, d = idx % kHeadDim;
+      float M = -INFINITY;
+#pragma unroll
+      for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, s.wm[4 * h + ww][head]);
+      float Lsum = 0.f, O = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < 4; ++ww) {
+        const float m = s.wm[4 * h + ww][head];
+        if (m == -INFINITY) continue;
+        const float c = expf(m - M);
+        Lsum += s.wl[4 * h + ww][head] * c;
+        O += s.wo[4 * h + ww][head][d] * c;
+      }
+      if (w.s_eff == 1) {
+        store_out(p, w.seq, (6 * h + head) * kHeadDim + d, O / Lsum);
       } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(dst)[j] = make_uint4(0, 0, 0, 0);
+        part_o[idx] = O;
+        if (d == 0) {
+          part_ml[2 * head] = M;
+          part_ml[2 * head + 1] = Lsum;
+        }
       }
     }
-    // ---- S^T = K q^T: lane reads K[pos g][32t..32t+31] and K[pos g+8][..].
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const uint32_t pg = base + g, pg8 = base + g + 8;
-      uint32_t kg[16], kg8[16];
-      const uint4* srcg = reinterpret_cast<const uint4*>(kbase + (size_t)min(pg, p1 - 1) * p.kv_pos_stride + 32 * t);
-      const uint4* srcg8 = reinterpret_cast<const uint4*>(kbase + (size_t)min(pg8, p1 - 1) * p.kv_pos_stride + 32 * t);
+    if (w.s_eff > 1 && !aborting) {
+      // ---- ticket: the last CTA of this sequence merges its splits in order.
+      __threadfence();
+      consumers_sync();
+      if (ctid == 0) s.ticket = atomicAdd(&p.counters[w.seq], 1u);
+      consumers_sync();
+      if (s.ticket == w.s_eff - 1) {
+        __threadfence();
+        const float* all_ml = p.part_ml + (size_t)w.seq * max_s * 2 * 12;
+        const float* all_o = p.part_o + (size_t)w.seq * max_s * 2 * (6 * kHeadDim);
+        if (warp < 2) {  // warp hg: head group hg, lane = split
+          const int hg = warp;
+          const bool have = (uint32_t)lane < w.s_eff;
+          for (int head = 0; head < 6; ++head) {
+            const float m = have ? __ldcg(all_ml + ((size_t)lane * 2 + hg) * 12 + 2 * head) : -INFINITY;
+            const float l = have ? __ldcg(all_ml + ((size_t)lane * 2 + hg) * 12 + 2 * head + 1) : 0.f;
+            float M = m;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 a = srcg[j], b = srcg8[j];
-        kg[4 * j] = a.x; kg[4 * j + 1] = a.y; kg[4 * j + 2] = a.z; kg[4 * j + 3] = a.w;
-        kg8[4 * j] = b.x; kg8[4 * j + 1] = b.y; kg8[4 * j + 2] = b.z; kg8[4 * j + 3] = b.w;
-      }
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            const float c = m == -INFINITY ? 0.f : expf(m - M);
+            s.sc[hg][lane][head] = c;
+            // fixed-order tree sum over splits (lane order) for determinism
+            float L = l * c;
 #pragma unroll
-      for (int st = 0; st < 8; ++st) {
-        // mma-k (2t,2t+1) <-> d = 32t+4st, +1 ; (2t+8, 2t+9) <-> d = 32t+4st+2, +3
-        const uint32_t a[4] = {kg[2 * st], kg8[2 * st], kg[2 * st + 1], kg8[2 * st + 1]};
-        mma_16816(s, a, qf[2 * st], qf[2 * st + 1], s);
-      }
-      // s[0]: (pos g, head 2t)  s[1]: (pos g, head 2t+1)
-      // s[2]: (pos g+8, head 2t) s[3]: (pos g+8, head 2t+1)
-      const bool vg = pg < p1, vg8 = pg8 < p1;
+            for (int off = 1; off < 32; off <<= 1) {
+              const float o2 = __shfl_down_sync(0xffffffffu, L, off);
+              if ((lane & (2 * off - 1)) == 0) L += o2;
+            }
+            if (lane == 0) s.hsum[hg][head] = L;
+          }
+        }
+        consumers_sync();
+        for (int idx = ctid; idx < 2 * 6 * kHeadDim; idx += 256) {
+          const int hg = idx / (6 * kHeadDim), r = idx % (6 * kHeadDim), head = r / kHeadDim;
+          float part[kMaxSplits];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) s[j] *= kAttnScale;
-      if (!vg) s[0] = s[1] = -INFINITY;
-      if (!vg8) s[2] = s[3] = -INFINITY;
-    }
-    // ---- online softmax for heads 2t and 2t+1.
-    float pr[4];
+          for (int sp = 0; sp < kMaxSplits; ++sp)
+            part[sp] = (uint32_t)sp < w.s_eff
+                           ? __ldcg(all_o + ((size_t)sp * 2 + hg) * (6 * kHeadDim) + r)
+                           : 0.f;
+          float O = 0.f;
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float mx = fmaxf(s[hh], s[2 + hh]);
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float m_new = fmaxf(m_run[hh], mx);
-      const float corr = m_run[hh] == -INFINITY ? 0.f : expf(m_run[hh] - m_new);
-      const float e0 = expf(s[hh] - m_new), e1 = expf(s[2 + hh] - m_new);
-      pr[hh] = e0;
-      pr[2 + hh] = e1;
-      float sum = e0 + e1;
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-      l_run[hh] = l_run[hh] * corr + sum;
-      m_run[hh] = m_new;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        o[i][hh] *= corr;
-        o[i][2 + hh] *= corr;
+          for (int sp = 0; sp < kMaxSplits; ++sp)
+            if ((uint32_t)sp < w.s_eff) O += part[sp] * s.sc[hg][sp][head];
+          store_out(p, w.seq, (6 * hg) * kHeadDim + r, O / s.hsum[hg][head]);
+        }
+        if (ctid == 0) p.counters[w.seq] = 0;  // re-arm for the next launch
       }
     }
-    // ---- P^T to shared memory as fp16 hi/lo: pt[pos][head].
-    {
-      uint16_t* hi = pt[warp][0];
-      uint16_t* lo = pt[warp][1];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int pos = g + (j >= 2 ? 8 : 0), head = 2 * t + (j & 1);
-        const __half h = f2h(pr[j]);
-        const __half l = f2h(pr[j] - h2f(h));
-        hi[pos * 8 + head] = hbits(h);
-        lo[pos * 8 + head] = hbits(l);
-      }
-    }
-    __syncwarp();
-    // B fragments (k = pos, n = head): lane (g,t): (pos 2t, 2t+1 ; head g), (pos 2t+8, 2t+9 ; head g)
-    uint32_t bh0, bh1, bl0, bl1;
-    {
-      const uint16_t* hi = pt[warp][0];
-      const uint16_t* lo = pt[warp][1];
-      bh0 = (uint32_t)hi[(2 * t) * 8 + g] | ((uint32_t)hi[(2 * t + 1) * 8 + g] << 16);
-      bh1 = (uint32_t)hi[(2 * t + 8) * 8 + g] | ((uint32_t)hi[(2 * t + 9) * 8 + g] << 16);
-      bl0 = (uint32_t)lo[(2 * t) * 8 + g] | ((uint32_t)lo[(2 * t + 1) * 8 + g] << 16);
-      bl1 = (uint32_t)lo[(2 * t + 8) * 8 + g] | ((uint32_t)lo[(2 * t + 9) * 8 + g] << 16);
-    }
-    // ---- o^T += V^T P^T over the 8 d-tiles.  A = V^T[16 d x 16 pos] via
-    // ldmatrix.trans of V rows: matrices (pos 0-7, d 0-7), (pos 0-7, d 8-15),
-    // (pos 8-15, d 0-7), (pos 8-15, d 8-15) -> a0..a3 after transposition
-    // are (d g, pos 2t..), (d g+8, pos 2t..), (d g, pos 2t+8..), (d g+8, pos 2t+8..).
-    {
-      const int mi = lane >> 3, ri = lane & 7;
-      const int prow = ri + ((mi >> 1) << 3);   // position row of this address
-      const int dcol = (mi & 1) << 3;           // d offset within the tile
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t a[4];
-        ldmatrix_x4_trans(a, vs[warp] + prow * kVRowBytes + (16 * i + dcol) * 2);
-        mma_16816(o[i], a, bh0, bh1, o[i]);
-        mma_16816(o[i], a, bl0, bl1, o[i]);
-      }
-    }
-    __syncwarp();
+    consumers_sync();  // wo / wm / sc are reused by the next unit
   }
-
-  // ---- merge the 4 warps.  o[i][0]: (d 16i+g, head 2t) o[i][1]: (d 16i+g, head 2t+1)
-  //                          o[i][2]: (d 16i+g+8, head 2t) o[i][3]: (d 16i+g+8, head 2t+1)
-  if (g == 0) {
-    wm[warp][2 * t] = m_run[0];
-    wm[warp][2 * t + 1] = m_run[1];
-    wl[warp][2 * t] = l_run[0];
-    wl[warp][2 * t + 1] = l_run[1];
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int head = 2 * t + (j & 1), d = 16 * i + g + (j >= 2 ? 8 : 0);
-      if (head < 6) wo[warp][head][d] = o[i][j];
-    }
-  __syncthreads();
-
-  const size_t unit = ((size_t)seq * kKVHeads + kvh);
-  float* part_o = p.part_o + (unit * max_s + split) * (6 * kHeadDim);
-  float* part_ml = p.part_ml + (unit * max_s + split) * 12;
-  for (int idx = threadIdx.x; idx < 6 * kHeadDim; idx += blockDim.x) {
-    const int head = idx / kHeadDim, d = idx % kHeadDim;
-    float M = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][head]);
-    float Lsum = 0.f, O = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w) {
-      if (wm[w][head] == -INFINITY) continue;
-      const float c = expf(wm[w][head] - M);
-      Lsum += wl[w][head] * c;
-      O += wo[w][head][d] * c;
-    }
-    if (S_eff == 1) {
-      store_out(p, seq, (6 * kvh + head) * kHeadDim + d, O / Lsum);
-    } else {
-      part_o[idx] = O;
-      if (d == 0) {
-        part_ml[2 * head] = M;
-        part_ml[2 * head + 1] = Lsum;
-      }
-    }
-  }
-  if (S_eff == 1) return;
-
-  // ---- ticket: the last CTA of this (seq, kv head) merges all chunks in order.
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_ticket = atomicAdd(&p.counters[unit], 1u);
-  __syncthreads();
-  if (s_ticket != S_eff - 1) return;
-  __threadfence();
-  const float* all_o = p.part_o + unit * max_s * (6 * kHeadDim);
-  const float* all_ml = p.part_ml + unit * max_s * 12;
-  // Per head: the maximum over splits, each split's rescale factor and the
-  // total weight, staged once in shared memory (wo/wm are free by now).
-  float* sc = &wo[0][0][0];             // [S_eff][6] factors
-  float* hsum = &wo[1][0][0];           // [6] totals
-  if (threadIdx.x < 6) {
-    const int head = threadIdx.x;
-    float M = -INFINITY;
-    for (uint32_t sp = 0; sp < S_eff; ++sp) M = fmaxf(M, __ldcg(all_ml + sp * 12 + 2 * head));
-    float Lsum = 0.f;
-    for (uint32_t sp = 0; sp < S_eff; ++sp) {
-      const float m = __ldcg(all_ml + sp * 12 + 2 * head);
-      const float c = m == -INFINITY ? 0.f : expf(m - M);
-      sc[sp * 6 + head] = c;
-      Lsum += __ldcg(all_ml + sp * 12 + 2 * head + 1) * c;
-    }
-    hsum[head] = Lsum;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < 6 * kHeadDim; idx += blockDim.x) {
-    const int head = idx / kHeadDim;
-    float part[kMaxSplits];
-#pragma unroll
-    for (int sp = 0; sp < kMaxSplits; ++sp)
-      part[sp] = (uint32_t)sp < S_eff ? __ldcg(all_o + sp * (6 * kHeadDim) + idx) : 0.f;
-    float O = 0.f;
-#pragma unroll
-    for (int sp = 0; sp < kMaxSplits; ++sp)
-      if ((uint32_t)sp < S_eff) O += part[sp] * sc[sp * 6 + head];
-    store_out(p, seq, (6 * kvh) * kHeadDim + idx, O / hsum[head]);
-  }
-  if (threadIdx.x == 0) p.counters[unit] = 0;  // re-arm for the next launch
 }
 
-// Splits for a launch: enough CTAs for ~8 per SM over the batch, at least 64
-// positions per split, at most 32 splits (the merge reads them all).
+// Splits per sequence for a launch: ~1 work unit per SM over the batch, at
+// most one per 64-position tile, at most 32 (the merge reads them all).
 int attn_max_splits(int max_ctx, int n_seq) {
-  int s = (max_ctx + kMinSplitLen - 1) / kMinSplitLen;
-  const int target = kAttnCtaTarget / (kKVHeads * (n_seq > 0 ? n_seq : 1));
-  const int cap = target < 1 ? 1 : (target > kMaxSplits ? kMaxSplits : target);
-  return s < cap ? s : cap;
+  const int tiles = (max_ctx + kTilePos - 1) / kTilePos;
+  int target = (148 * kUnitsPerSm) / (n_seq > 0 ? n_seq : 1);
+  if (target < 1) target = 1;
+  const int s = tiles < target ? tiles : target;
+  return s < kMaxSplits ? s : kMaxSplits;
 }
 
 // Scratch layout: the merge tickets first, at a fixed offset, so that calls
@@ -337,18 +476,71 @@ void attn_bind_scratch(AttnParams& p, void* scratch, int max_splits, int n_seq) 
   p.part_o = p.part_ml + units * max_splits * 12;
 }
 
-void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st,
-                             bool pdl) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// rows x 256 fp16 (512-byte rows), boxes of 64 rows x 64 elements, 128-byte
+// swizzle, zero fill past the last row.
+bool encode_kv_map(CUtensorMap* map, const __half* base, uint64_t rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kKVDim, rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kKVDim * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kTilePos};
+  const cuuint32_t elem[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box,
+             elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st,
+                            bool pdl) {
+  // The tensor maps see each cache as rows of 256 fp16 (both kv heads of a position).
+  if (p.kv_pos_stride != kKVDim || p.kv_head_stride != kHeadDim || p.kv_seq_stride % kKVDim ||
+      max_splits < 1 || max_splits > kMaxSplits || n_seq < 1 || p.max_ctx < 1)
+    return -1;
+  const int rows_per_seq = (int)(p.kv_seq_stride / kKVDim);
+  if (n_seq > 1 && rows_per_seq < (int)p.max_ctx) return -1;
+  const uint64_t rows = (uint64_t)(n_seq - 1) * rows_per_seq + p.max_ctx;
+  CUtensorMap tmk, tmv;
+  if (!encode_kv_map(&tmk, p.k, rows) || !encode_kv_map(&tmv, p.v, rows)) return -1;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return -1;
+  const int n_units = n_seq * max_splits;
+  const size_t smem = sizeof(AttnSmem) + 1024;
+  if (cudaFuncSetAttribute(k_attention_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return -1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(max_splits, kKVHeads, n_seq);
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3(n_units < sms ? n_units : sms);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k_attention_decode, p);
+  return cudaLaunchKernelEx(&cfg, k_attention_decode, p, max_splits, n_units, rows_per_seq, tmk,
+                            tmv) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 }  // namespace qwen

@@ -12,7 +12,7 @@
 // Limits and sharing:
 //   * The array holds kNoAllocScratchBytes (1 MiB) on every GPU that loads this
 //     library, for the life of the process.  One sequence at a time needs at
-//     most 256 + 2 * 148 * 780 * 4 bytes (923,776 B), for any max_ctx up to 2^20;
+//     most 256 + 2 * 32 * 780 * 4 bytes (199,936 B), for any max_ctx up to 2^20;
 //     larger requests are rejected with QWEN_ERR_INVALID_ARGUMENT.
 //   * Every call on a device shares the same array and leaves its contents
 //     behind.  The merge tickets that must start at zero are cleared on the
@@ -99,6 +99,8 @@ extern "C" int qwen_attention_decode_noalloc(const uint16_t* q, const uint16_t* 
   if (int rc = cuda_status(cudaMemsetAsync(p.counters, 0, kKVHeads * sizeof(uint32_t), st),
                            "cudaMemsetAsync(attention tickets)"))
     return rc;
-  launch_attention_decode(p, splits, 1, st);
+  if (launch_attention_decode(p, splits, 1, st) != 0)
+    return set_error(QWEN_ERR_CUDA, "attention_decode_noalloc: launch failed (%s)",
+                     cudaGetErrorString(cudaGetLastError()));
   return launch_status("attention_decode_noalloc");
 }

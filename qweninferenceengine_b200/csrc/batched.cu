@@ -334,7 +334,8 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
     mark();
     ap.k = kc;
     ap.v = vc;
-    launch_attention_decode(ap, s.attn_splits, B, st, true);
+    if (launch_attention_decode(ap, s.attn_splits, B, st, true) != 0)
+      return set_error(QWEN_ERR_CUDA, "attention launch failed (%s)", cudaGetErrorString(cudaGetLastError()));
     mark();
     QWEN_TRY(gemm(o, true, s.act_h, s, kHidden, kHidden, p.o, s.tc_part, nullptr, 0, st));
     mark();

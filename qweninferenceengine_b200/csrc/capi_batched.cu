@@ -105,4 +105,39 @@ int qwen_gemm_fp16_batched(const uint16_t* w, const uint16_t* x, uint16_t* y, ui
                      n_batch, buf);
 }
 
+int qwen_attention_decode_batched(const uint16_t* q, const uint16_t* k_cache,
+                                  const uint16_t* v_cache, uint16_t* out,
+                                  const uint32_t* seq_len, uint32_t n_seq, uint32_t max_ctx,
+                                  void* stream) {
+  if (!q || !k_cache || !v_cache || !out || !seq_len)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "attention_decode_batched: null buffer");
+  if (max_ctx == 0 || max_ctx > (1u << 20))
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "attention_decode_batched: max_ctx=%u", max_ctx);
+  if (n_seq == 0 || n_seq > 65535)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "attention_decode_batched: n_seq=%u", n_seq);
+  StreamBuffers buf(static_cast<cudaStream_t>(stream));
+  const int splits = attn_max_splits((int)max_ctx, (int)n_seq);
+  const size_t bytes = attn_scratch_bytes(splits, (int)n_seq);
+  QWEN_CUDA(cudaMallocAsync(&buf.p[0], bytes, buf.st), "cudaMallocAsync(attention scratch)");
+  QWEN_CUDA(cudaMemsetAsync(buf.p[0], 0, bytes, buf.st), "cudaMemsetAsync");
+  AttnParams p{};
+  p.q = reinterpret_cast<const __half*>(q);
+  p.q_seq_stride = kHidden;
+  p.k = reinterpret_cast<const __half*>(k_cache);
+  p.v = reinterpret_cast<const __half*>(v_cache);
+  p.kv_seq_stride = (long long)max_ctx * kKVDim;
+  p.kv_pos_stride = kKVDim;
+  p.kv_head_stride = kHeadDim;
+  p.seq_len = seq_len;
+  p.seq_len_stride = 1;
+  p.max_ctx = max_ctx;
+  p.out = reinterpret_cast<__half*>(out);
+  p.out_seq_stride = kHidden;
+  attn_bind_scratch(p, buf.p[0], splits, (int)n_seq);
+  if (launch_attention_decode(p, splits, (int)n_seq, buf.st) != 0)
+    return set_error(QWEN_ERR_CUDA, "attention_decode_batched: launch failed (%s)",
+                     cudaGetErrorString(cudaGetLastError()));
+  return launch_status("attention_decode_batched");
+}
+
 }  // extern "C"

@@ -195,7 +195,9 @@ int qwen_attention_decode(const uint16_t* q, const uint16_t* k_cache, const uint
   p.out_seq_stride = kHidden;
   p.err = nullptr;
   attn_bind_scratch(p, scratch, splits, 1);
-  launch_attention_decode(p, splits, 1, reinterpret_cast<cudaStream_t>(stream));
+  if (launch_attention_decode(p, splits, 1, reinterpret_cast<cudaStream_t>(stream)) != 0)
+    return set_error(QWEN_ERR_CUDA, "attention_decode: launch failed (%s)",
+                     cudaGetErrorString(cudaGetLastError()));
   return launch_status("attention_decode");
 }
 

@@ -32,8 +32,9 @@ int attn_max_splits(int max_ctx, int n_seq);
 size_t attn_scratch_bytes(int max_splits, int n_seq);
 void attn_bind_scratch(AttnParams& p, void* scratch, int max_splits, int n_seq);
 // pdl: launch as a programmatic dependent of the previous kernel in the stream.
-void launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st,
-                             bool pdl = false);
+// Returns 0, or -1 for unsupported strides / split counts or a launch failure.
+int launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cudaStream_t st,
+                            bool pdl = false);
 
 // ------------------------------------------------------- op launchers ----
 int launch_gemv_q4_rowmajor(const uint8_t* packed, const __half* scales, const __half* x,

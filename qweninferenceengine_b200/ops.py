@@ -120,6 +120,16 @@ def attention_decode(q, k_cache, v_cache, seq_len, max_ctx: int) -> torch.Tensor
     return out
 
 
+def attention_decode_batched(q, k_cache, v_cache, seq_len, max_ctx: int) -> torch.Tensor:
+    """attention_decode for every sequence: q [n][1536], caches [n][max_ctx][256],
+    seq_len [n] (device uint32/int32)."""
+    n = q.shape[0]
+    out = torch.empty((n, HIDDEN), dtype=torch.float16, device=q.device)
+    check(lib().qwen_attention_decode_batched(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out),
+                                              _ptr(seq_len), n, max_ctx, _stream()))
+    return out
+
+
 def dequant_q4(packed: torch.Tensor, scales: torch.Tensor, n_weights: int) -> torch.Tensor:
     out = torch.empty(n_weights, dtype=torch.float32, device=packed.device)
     check(lib().qwen_dequant_q4(_ptr(packed), _ptr(scales), n_weights, _ptr(out), _stream()))

@@ -84,3 +84,19 @@ def test_gemm_batched_rejects_bad_shapes(cuda):
     w = torch.zeros((128, 128), dtype=torch.float16, device="cuda")
     with pytest.raises(RuntimeError):
         ops.gemm_fp16_batched(w, x)            # more than 256 rows
+
+
+def test_attention_decode_batched(cuda, oracle):
+    # ragged lengths, including a single position and a full cache
+    lens = [1, 17, 64, 65, 300, 1000]
+    max_ctx = 1000
+    rng = np.random.default_rng(31)
+    n = len(lens)
+    q = rng.standard_normal((n, 1536)).astype(np.float16)
+    kc = rng.standard_normal((n, max_ctx, 256)).astype(np.float16)
+    vc = rng.standard_normal((n, max_ctx, 256)).astype(np.float16)
+    sl = T(np.array(lens, np.int32))
+    got = N(ops.attention_decode_batched(T(q), T(kc), T(vc), sl, max_ctx))
+    for b, L in enumerate(lens):
+        ref = oracle.attention(q[b], kc[b], vc[b], L)
+        assert_within(got[b], ref, 1e-4)
