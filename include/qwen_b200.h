@@ -249,8 +249,8 @@ int qwen_engine_time_steps(qwen_engine* e, int32_t n_steps, float* ms_step, floa
 /* Per-launch device times of one eagerly launched step of the tensor-core path
  * (QWEN_KERNELS_TC; the step advances every sequence like a decode step).
  * Launch order: rmsnorm, then per layer {qkv gemm, qkv finish, attention,
- * o gemm, o finish, gate/up gemm, swiglu finish, down gemm, down finish},
- * then the LM head gemm; *n receives the count (1 + 9*layers + 1).
+ * o gemm, o finish, gate/up gemm with SwiGLU, down gemm, down finish}, then
+ * the LM head gemm; *n receives the count (1 + 8*layers + 1).
  * With ms == NULL or cap < *n only the count is returned. */
 int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n);
 

@@ -14,8 +14,9 @@
 //                                           straight into the activation tiles
 //   part  <- W_o . act_h
 //   x     <- half(x + half(part + b_o)); act_h <- rmsnorm(x)   k_resid_norm_finish
-//   part  <- W_gu . act_h                   gate rows then up rows
-//   act_i <- half(silu(g) * u)              k_swiglu_finish (activations.metal:9-27)
+//   act_i <- half(silu(g) * u)              W_gu . act_h, tiles of 64 gate + 64 up
+//                                           rows, SwiGLU in the GEMM epilogue
+//                                           (activations.metal:9-27)
 //   part  <- W_down . act_i
 //   x     <- half(x + half(part + b_down)); act_h <- rmsnorm_next(x)
 // then logits = LM . act_h (fp16 out, no split).
@@ -190,32 +191,19 @@ __global__ void __launch_bounds__(512) k_resid_norm_finish(const float* __restri
   }
 }
 
-// act_i row b <- half(silu(g) * u), g and u the fp16-rounded gate/up outputs
-// (zero biases, InferenceEngine.swift:82-85).
-__global__ void __launch_bounds__(256) k_swiglu_finish(const float* __restrict__ part, int splits,
-                                                       int nbv, uint8_t* __restrict__ act, int nb) {
-  pdl_prologue();
-  const int i = blockIdx.x * 256 + threadIdx.x;
-  const int b = blockIdx.y;
-  if (i >= kInter) return;
-  const float g = h2f(f2h(sum_splits(part, splits, nbv, 2 * kInter, b, i) + 0.0f));
-  const float u = h2f(f2h(sum_splits(part, splits, nbv, 2 * kInter, b, kInter + i) + 0.0f));
-  *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = f2h(silu_ref(g) * u);
-}
-
 struct TcPlan {
-  int qkv, o, gu, down;  // K splits
+  int qkv, o, down;  // K splits (gate/up runs unsplit: its epilogue needs whole sums)
 };
 
 TcPlan plan_for(int sm_count) {
   return TcPlan{tc_choose_splits(kQKVTiles, kChunks1536, sm_count),
                 tc_choose_splits(kOTiles, kChunks1536, sm_count),
-                tc_choose_splits(kGUTiles, kChunks1536, sm_count),
                 tc_choose_splits(kDownTiles, kChunks8960, sm_count)};
 }
 
 int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManager& s, int n_rows,
-         int k, int splits, float* part, __half* out, long long ld_out, cudaStream_t st) {
+         int k, int splits, float* part, __half* out, long long ld_out, cudaStream_t st,
+         uint8_t* swiglu_act = nullptr) {
   TcGemmArgs a;
   a.w = blob;
   a.q4 = q4;
@@ -228,6 +216,8 @@ int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManage
   a.part = part;
   a.out = out;
   a.ld_out = ld_out;
+  a.swiglu_act = swiglu_act;
+  a.swiglu_nb = s.tc_nb;
   a.err = s.err;
   a.pdl = true;
   if (launch_tc_gemm(a, st) != 0) return launch_status("tensor-core projection");
@@ -236,7 +226,7 @@ int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManage
 
 }  // namespace
 
-int tc_kernels_per_step(int n_layers) { return 1 + 9 * n_layers + 1; }
+int tc_kernels_per_step(int n_layers) { return 1 + 8 * n_layers + 1; }
 
 int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
   TcWeights& t = m.tc;
@@ -260,8 +250,10 @@ int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
     QWEN_TRY(rq(L.k, qkv + (size_t)(kHidden / kTcM) * kChunks1536 * kQ4TcChunkBytes));
     QWEN_TRY(rq(L.v, qkv + (size_t)((kHidden + kKVDim) / kTcM) * kChunks1536 * kQ4TcChunkBytes));
     QWEN_TRY(rq(L.o, o));
-    QWEN_TRY(rq(L.gate, gu));
-    QWEN_TRY(rq(L.up, gu + (size_t)(kInter / kTcM) * kChunks1536 * kQ4TcChunkBytes));
+    // Gate/up pairing: tile t = gate rows 64t .. 64t+63, then up rows 64t .. 64t+63.
+    if (launch_repack_q4_tc_rows(L.gate.packed, L.gate.scales, kInter, kHidden, gu, 64, 0, st) ||
+        launch_repack_q4_tc_rows(L.up.packed, L.up.scales, kInter, kHidden, gu, 64, 64, st))
+      return launch_status("repack gate/up (tensor-core layout)");
     QWEN_TRY(rq(L.down, down));
   }
   if (launch_repack_f16_tc(m.embed, kVocab, kHidden, t.lm, st) != 0)
@@ -277,8 +269,8 @@ int tc_state_allocate(InferenceManager& s, int sm_count) {
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "tensor-core step: batch %d > %d", s.batch, kTcMaxNb);
   s.tc_nb = act_rows(s.batch);
   const TcPlan p = plan_for(sm_count);
-  const size_t part = std::max(std::max((size_t)p.qkv * kQKVRows, (size_t)p.o * kHidden),
-                               std::max((size_t)p.gu * 2 * kInter, (size_t)p.down * kHidden)) *
+  const size_t part = std::max((size_t)p.qkv * kQKVRows,
+                               std::max((size_t)p.o * kHidden, (size_t)p.down * kHidden)) *
                       s.batch;
   QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kHidden), (void**)&s.act_h));
   QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kInter), (void**)&s.act_i));
@@ -296,7 +288,7 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
   if (!t.blob || !s.act_h) return set_error(QWEN_ERR_STATE, "tensor-core step not prepared");
   if (t.rope_ctx < s.max_ctx) return set_error(QWEN_ERR_STATE, "RoPE table shorter than max_ctx");
   const TcPlan p = plan_for(sm_count);
-  if (std::max(std::max(p.qkv, p.o), std::max(p.gu, p.down)) > kTcMaxSplits)
+  if (std::max(p.qkv, std::max(p.o, p.down)) > kTcMaxSplits)
     return set_error(QWEN_ERR_STATE, "tensor-core step: split plan exceeds %d", kTcMaxSplits);
   const int B = s.batch, nb = s.tc_nb;
   AttnParams ap{};
@@ -342,10 +334,7 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
     QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.o, B, L.o_bias,
                         s.x, L.post_attn_norm, s.act_h, nb));
     mark();
-    QWEN_TRY(gemm(gu, true, s.act_h, s, 2 * kInter, kHidden, p.gu, s.tc_part, nullptr, 0, st));
-    mark();
-    QWEN_TRY(launch_pdl(k_swiglu_finish, dim3((kInter + 255) / 256, B), dim3(256), st, s.tc_part,
-                        p.gu, B, s.act_i, nb));
+    QWEN_TRY(gemm(gu, true, s.act_h, s, 2 * kInter, kHidden, 1, nullptr, nullptr, 0, st, s.act_i));
     mark();
     QWEN_TRY(gemm(down, true, s.act_i, s, kHidden, kInter, p.down, s.tc_part, nullptr, 0, st));
     mark();

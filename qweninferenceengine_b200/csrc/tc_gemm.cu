@@ -34,7 +34,7 @@
 namespace qwen {
 namespace {
 
-constexpr int kTcStages = 4;
+constexpr int kTcMaxStages = 4;  // deeper rings measured slower (one CTA per SM instead of two)
 constexpr int kTcThreads = 192;
 constexpr int kDeqThreads = 128;
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
@@ -151,19 +151,20 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2) {
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   extern __shared__ uint8_t tc_smem[];
+  const int S = a.stages;  // ring depth (host-sized to the shared memory budget)
   const uint32_t pad = (1024u - (smem_u32(tc_smem) & 1023u)) & 1023u;
   uint8_t* sA = tc_smem + pad;                             // [S][128 rows][128 B]
-  uint8_t* sX = sA + kTcStages * kF16TcChunkBytes;         // [S][nb rows][128 B]
+  uint8_t* sX = sA + S * kF16TcChunkBytes;         // [S][nb rows][128 B]
   const int nb = a.nb;
   const uint32_t xbytes = (uint32_t)nb * 128u;
-  uint8_t* sR = sX + kTcStages * xbytes;                   // [S][4608] (Q4)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + (a.q4 ? kTcStages * kQ4TcChunkBytes : 0));
+  uint8_t* sR = sX + S * xbytes;                   // [S][4608] (Q4)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + (a.q4 ? S * kQ4TcChunkBytes : 0));
   uint64_t* wfull = bars;
-  uint64_t* xfull = bars + kTcStages;
-  uint64_t* deq = bars + 2 * kTcStages;
-  uint64_t* empty = bars + 3 * kTcStages;
-  uint64_t* accum = bars + 4 * kTcStages;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4 * kTcStages + 1);
+  uint64_t* xfull = bars + S;
+  uint64_t* deq = bars + 2 * S;
+  uint64_t* empty = bars + 3 * S;
+  uint64_t* accum = bars + 4 * S;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4 * S + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   const uint32_t ncols = nb <= 32 ? 32u : nb <= 64 ? 64u : nb <= 128 ? 128u : 256u;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(wfull + s, 1);
       mbar_init(xfull + s, 1);
       mbar_init(deq + s, kDeqThreads);
@@ -200,32 +201,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
       const uint64_t pol = policy_evict_first();
       const uint32_t wbytes = a.q4 ? kQ4TcChunkBytes : kF16TcChunkBytes;
       auto load_w = [&](int i) {
-        const int s = i % kTcStages;
+        const int s = i % S;
         mbar_arrive_expect_tx(wfull + s, wbytes);
         uint8_t* wdst = a.q4 ? sR + s * kQ4TcChunkBytes : sA + s * kF16TcChunkBytes;
         bulk_g2s_stream(wdst, a.w + ((size_t)tile * n_chunks + c0 + i) * wbytes, wbytes, wfull + s,
                         pol);
       };
       auto load_x = [&](int i) {
-        const int s = i % kTcStages;
+        const int s = i % S;
         mbar_arrive_expect_tx(xfull + s, xbytes);
         bulk_g2s(sX + s * xbytes, a.act + (size_t)(c0 + i) * xbytes, xbytes, xfull + s);
       };
-      const int pre = cps < kTcStages ? cps : kTcStages;
+      const int pre = cps < S ? cps : S;
       for (int i = 0; i < pre; ++i) load_w(i);  // weights do not depend on earlier kernels
       pdl_wait();
       for (int i = 0; i < pre; ++i) load_x(i);
       int i = pre;
       for (; i < cps; ++i) {
-        const int s = i % kTcStages;
-        if (!tc_wait(empty + s, ((i / kTcStages) - 1) & 1, abort, a.err)) break;
+        const int s = i % S;
+        if (!tc_wait(empty + s, ((i / S) - 1) & 1, abort, a.err)) break;
         load_w(i);
         load_x(i);
       }
       // Every issued copy lands before the CTA may exit.
-      for (int j = i > kTcStages ? i - kTcStages : 0; j < i; ++j) {
-        tc_wait(wfull + j % kTcStages, (j / kTcStages) & 1, abort, a.err, false);
-        tc_wait(xfull + j % kTcStages, (j / kTcStages) & 1, abort, a.err, false);
+      for (int j = i > S ? i - S : 0; j < i; ++j) {
+        tc_wait(wfull + j % S, (j / S) & 1, abort, a.err, false);
+        tc_wait(xfull + j % S, (j / S) & 1, abort, a.err, false);
       }
     }
     __syncwarp();
@@ -234,9 +235,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     if (lane == 0) {
       const uint32_t idesc = f16_idesc(kTcM, nb);
       for (int i = 0; i < cps; ++i) {
-        const int s = i % kTcStages;
-        if (!tc_wait(a.q4 ? deq + s : wfull + s, (i / kTcStages) & 1, abort, a.err)) break;
-        if (!tc_wait(xfull + s, (i / kTcStages) & 1, abort, a.err)) break;
+        const int s = i % S;
+        if (!tc_wait(a.q4 ? deq + s : wfull + s, (i / S) & 1, abort, a.err)) break;
+        if (!tc_wait(xfull + s, (i / S) & 1, abort, a.err)) break;
         tc_fence_after();
         const uint64_t ad = sw128_kmajor_desc(smem_u32(sA + s * kF16TcChunkBytes));
         const uint64_t bd = sw128_kmajor_desc(smem_u32(sX + s * xbytes));
@@ -253,8 +254,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     const int r = threadIdx.x;  // row of the tile
     if (a.q4) {
       for (int i = 0; i < cps; ++i) {
-        const int s = i % kTcStages;
-        if (!tc_wait(wfull + s, (i / kTcStages) & 1, abort, a.err)) break;
+        const int s = i % S;
+        if (!tc_wait(wfull + s, (i / S) & 1, abort, a.err)) break;
         const uint8_t* raw = sR + s * kQ4TcChunkBytes;
         const uint4 p0 = *reinterpret_cast<const uint4*>(raw + r * 16);
         const uint4 p1 = *reinterpret_cast<const uint4*>(raw + 2048 + r * 16);
@@ -279,7 +280,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     const bool landed = tc_wait(accum, 0, abort, a.err, false);
     tc_fence_after();
     // tcgen05.ld is warp-collective: the decision is the warp's, not the lane's.
-    if (__all_sync(0xffffffffu, landed && !*abort)) {
+    const bool go = __all_sync(0xffffffffu, landed && !*abort);
+    if (a.swiglu_act) {
+      // Up rows (tensor-memory lanes 64..127, warps 2-3) -> fp16 in shared
+      // memory [b][64] (the A ring is idle once the accumulator is complete),
+      // then warps 0-1 combine them with their gate rows.
+      __half* ub = reinterpret_cast<__half*>(sA);
+      const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+      if (go && warp >= 2)
+        for (int c = 0; c < nb; c += 16) {
+          float v[16];
+          tmem_ld16(lane_addr + (uint32_t)c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ub[(c + j) * 64 + (r - 64)] = f2h(v[j]);
+        }
+      asm volatile("bar.sync 2, 128;" ::: "memory");  // the four epilogue warps
+      if (go && warp < 2) {
+        const int hrow = tile * 64 + r;  // k index of the down projection's input
+        const int cc = hrow >> 6, jj = (hrow >> 3) & 7;
+        for (int c = 0; c < nb; c += 16) {
+          float v[16];
+          tmem_ld16(lane_addr + (uint32_t)c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int b = c + j;
+            if (b < a.nb_valid) {
+              const float gt = h2f(f2h(v[j])), up = h2f(ub[b * 64 + r]);
+              const size_t off = ((size_t)cc * a.swiglu_nb + b) * 128 +
+                                 (((uint32_t)jj ^ (uint32_t)(b & 7)) << 4) + (hrow & 7) * 2;
+              *reinterpret_cast<__half*>(a.swiglu_act + off) = f2h(silu_ref(gt) * up);
+            }
+          }
+        }
+      }
+    } else if (go) {
       const size_t row = (size_t)tile * kTcM + r;
       const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
       for (int c = 0; c < nb; c += 16) {
@@ -317,23 +351,26 @@ __device__ __forceinline__ uint32_t permute_nibbles(uint32_t w) {
   return o;
 }
 
+// Source row tile * R + r goes to tile row dst_off + r (R = rows per tile taken
+// from the source: 128, or 64 for the gate/up pairing).
 __global__ void k_repack_q4_tc(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
-                               int n_rows, int k, uint8_t* __restrict__ blob) {
+                               int n_rows, int k, uint8_t* __restrict__ blob, int R, int dst_off) {
   const int nc = k / kTcChunkK;
-  const size_t total = (size_t)(n_rows / kTcM) * nc * 2 * kTcM;
+  const size_t total = (size_t)(n_rows / R) * nc * 2 * R;
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
-  const int r = (int)(idx % kTcM);
-  const int h = (int)((idx / kTcM) % 2);
-  const size_t tc = idx / (2 * kTcM);  // tile * nc + chunk
+  const int r = (int)(idx % R);
+  const int h = (int)((idx / R) % 2);
+  const size_t tc = idx / (2 * (size_t)R);  // tile * nc + chunk
   const int c = (int)(tc % nc);
-  const size_t row = (tc / nc) * kTcM + r;
+  const size_t row = (tc / nc) * R + r;
+  const int rr = dst_off + r;
   const uint4 src = *reinterpret_cast<const uint4*>(packed + row * (k / 2) + (size_t)(c * 2 + h) * 16);
   const uint4 dst = make_uint4(permute_nibbles(src.x), permute_nibbles(src.y),
                                permute_nibbles(src.z), permute_nibbles(src.w));
   uint8_t* chunk = blob + tc * kQ4TcChunkBytes;
-  *reinterpret_cast<uint4*>(chunk + h * 2048 + r * 16) = dst;
-  *reinterpret_cast<__half*>(chunk + 4096 + r * 4 + h * 2) = scales[row * (k / 32) + c * 2 + h];
+  *reinterpret_cast<uint4*>(chunk + h * 2048 + rr * 16) = dst;
+  *reinterpret_cast<__half*>(chunk + 4096 + rr * 4 + h * 2) = scales[row * (k / 32) + c * 2 + h];
 }
 
 __global__ void k_repack_f16_tc(const __half* __restrict__ w, int n_rows, int k,
@@ -381,18 +418,30 @@ inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threa
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(int nb, bool q4) {
-  return 1024 + (size_t)kTcStages * kF16TcChunkBytes + (size_t)kTcStages * nb * 128 +
-         (q4 ? (size_t)kTcStages * kQ4TcChunkBytes : 0) + (4 * kTcStages + 1) * 8 + 16;
+size_t tc_gemm_smem_bytes(int nb, bool q4, int stages) {
+  return 1024 + (size_t)stages * kF16TcChunkBytes + (size_t)stages * nb * 128 +
+         (q4 ? (size_t)stages * kQ4TcChunkBytes : 0) + (4 * stages + 1) * 8 + 16;
+}
+
+// The deepest ring (up to 4 stages) that fits one CTA's shared memory.
+int tc_gemm_stages(int nb, bool q4) {
+  int st = kTcMaxStages;
+  while (st > 2 && tc_gemm_smem_bytes(nb, q4, st) > 227 * 1024) --st;
+  return st;
 }
 
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
   if (!a.w || !a.act || a.n_rows <= 0 || a.n_rows % kTcM || a.k <= 0 || a.k % kTcChunkK ||
       a.nb < 16 || a.nb > kTcMaxNb || a.nb % 16 || a.nb_valid < 1 || a.nb_valid > a.nb ||
-      a.splits < 1 || (a.k / kTcChunkK) % a.splits || (!a.part == !a.out) ||
-      (a.out && a.splits != 1))
+      a.splits < 1 || (a.k / kTcChunkK) % a.splits)
     return -1;
-  const size_t smem = tc_gemm_smem_bytes(a.nb, a.q4);
+  const int outs = (a.part ? 1 : 0) + (a.out ? 1 : 0) + (a.swiglu_act ? 1 : 0);
+  if (outs != 1 || (!a.part && a.splits != 1) ||
+      (a.swiglu_act && (a.swiglu_nb < a.nb_valid || !a.q4)))
+    return -1;
+  TcGemmArgs args = a;
+  args.stages = tc_gemm_stages(a.nb, a.q4);
+  const size_t smem = tc_gemm_smem_bytes(a.nb, a.q4, args.stages);
   if (cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return -1;
@@ -406,15 +455,25 @@ int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_tc_gemm, a) == cudaSuccess ? 0 : -1;
+  return cudaLaunchKernelEx(&cfg, k_tc_gemm, args) == cudaSuccess ? 0 : -1;
+}
+
+int launch_repack_q4_tc_rows(const uint8_t* packed, const __half* scales, int n_rows, int k,
+                             uint8_t* blob, int src_rows_per_tile, int dst_row_offset,
+                             cudaStream_t st) {
+  const int R = src_rows_per_tile;
+  if (R < 1 || R > kTcM || dst_row_offset < 0 || dst_row_offset + R > kTcM || n_rows % R ||
+      k % kTcChunkK)
+    return -1;
+  const size_t total = (size_t)(n_rows / R) * (k / kTcChunkK) * 2 * R;
+  k_repack_q4_tc<<<blocks_for(total, 256), 256, 0, st>>>(packed, scales, n_rows, k, blob, R,
+                                                         dst_row_offset);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 int launch_repack_q4_tc(const uint8_t* packed, const __half* scales, int n_rows, int k,
                         uint8_t* blob, cudaStream_t st) {
-  if (n_rows % kTcM || k % kTcChunkK) return -1;
-  const size_t total = (size_t)(n_rows / kTcM) * (k / kTcChunkK) * 2 * kTcM;
-  k_repack_q4_tc<<<blocks_for(total, 256), 256, 0, st>>>(packed, scales, n_rows, k, blob);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_repack_q4_tc_rows(packed, scales, n_rows, k, blob, kTcM, 0, st);
 }
 
 int launch_repack_f16_tc(const __half* w, int n_rows, int k, uint8_t* blob, cudaStream_t st) {

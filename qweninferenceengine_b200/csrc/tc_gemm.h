@@ -55,25 +55,40 @@ struct TcGemmArgs {
   float* part = nullptr;       // fp32 partials [split][nb_valid][n_rows], or
   __half* out = nullptr;       //   fp16 results out[b * ld_out + n] (splits == 1)
   long long ld_out = 0;
+  // SwiGLU epilogue (splits == 1, no part/out): every 128-row tile holds 64
+  // gate rows then the 64 matching up rows; row j of the tile pair is written
+  // as half(silu(half(g)) * half(u)) into activation tiles of swiglu_nb rows
+  // at k index 64 * tile + j (activations.metal:9-27).
+  uint8_t* swiglu_act = nullptr;
+  int swiglu_nb = 0;
   int* err = nullptr;
   bool pdl = false;            // launch as a programmatic dependent of the previous kernel
+  int stages = 0;              // ring depth, set by launch_tc_gemm
 };
 
 // K splits for a launch: the largest divisor d of the chunk count with
-// tiles * d <= 2 * sm_count and at least 2 chunks per split (1 if none).
+// tiles * d <= sm_count (one wave at one CTA per SM) and at least 2 chunks per
+// split (1 if none).
 inline int tc_choose_splits(int n_tiles, int n_chunks, int sm_count) {
   int best = 1;
   for (int d = 1; d <= n_chunks; ++d)
-    if (n_chunks % d == 0 && n_tiles * d <= 2 * sm_count && n_chunks / d >= 2) best = d;
+    if (n_chunks % d == 0 && n_tiles * d <= sm_count && n_chunks / d >= 2) best = d;
   return best;
 }
 
-size_t tc_gemm_smem_bytes(int nb, bool q4);
+size_t tc_gemm_smem_bytes(int nb, bool q4, int stages);
+int tc_gemm_stages(int nb, bool q4);
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st);
 
 // Weight repacking (device to device) into the blobs above.
 int launch_repack_q4_tc(const uint8_t* packed, const __half* scales, int n_rows, int k,
                         uint8_t* blob, cudaStream_t st);
+// Rows of a source matrix into half tiles: source row i goes to tile
+// i / src_rows_per_tile, tile row dst_row_offset + i % src_rows_per_tile (the
+// gate/up pairing: gate with offset 0, up with offset 64, 64 rows per tile).
+int launch_repack_q4_tc_rows(const uint8_t* packed, const __half* scales, int n_rows, int k,
+                             uint8_t* blob, int src_rows_per_tile, int dst_row_offset,
+                             cudaStream_t st);
 int launch_repack_f16_tc(const __half* w, int n_rows, int k, uint8_t* blob, cudaStream_t st);
 // Row-major fp16 activations x[b * ld + k] (b < rows) -> activation tiles of
 // nb rows (rows..nb-1 zero).

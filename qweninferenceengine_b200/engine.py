@@ -170,8 +170,8 @@ class QwenEngine:
         ms = np.zeros(n.value, np.float32)
         check(lib().qwen_engine_profile_step(self._h, ms.ctypes.data_as(ctypes.c_void_p), n.value,
                                              ctypes.byref(n)))
-        per_layer = ["qkv_gemm", "qkv_finish", "attention", "o_gemm", "o_finish", "gu_gemm",
-                     "swiglu_finish", "down_gemm", "down_finish"]
+        per_layer = ["qkv_gemm", "qkv_finish", "attention", "o_gemm", "o_finish",
+                     "gu_gemm_swiglu", "down_gemm", "down_finish"]
         names = ["rmsnorm"] + per_layer * ((n.value - 2) // len(per_layer)) + ["lm_gemm"]
         return list(zip(names, ms.tolist()))
 
