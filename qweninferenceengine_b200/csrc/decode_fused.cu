@@ -305,7 +305,7 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
                                uint32_t chunk, uint32_t L, uint16_t tag, uint8_t* uni, __half* qs,
                                volatile Misc* misc, int ct, unsigned long long* at) {
   auto astamp = [&](int k) {
-    if (at && layer == 14 && ct == 0) at[k] = globaltimer();
+    if (at && layer == p.n_layers / 2 && ct == 0) at[k] = globaltimer();
   };
   astamp(0);
   const int warp = ct >> 5, lane = ct & 31, g = lane >> 2, t = lane & 3;
@@ -773,7 +773,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         const int u = (int)gridDim.x - 1 - (int)blockIdx.x;
         if (u < (int)(2 * S_eff) && warp < kAttnWarpsFused)
           attention_unit(p, layer, u & 1, u >> 1, S_eff, chunk, L, (uint16_t)tagof(layer), uni,
-                         xn, misc, ct, nullptr);
+                         xn, misc, ct,
+                         trace ? trace + 3 + p.n_layers * kTraceStampsPerLayer + 2 : nullptr);
       }
       cbar();
       lstamp(layer, kTsAttnDone);

@@ -56,7 +56,13 @@ enum TraceStamp : int {
   kTsLayerStart = 0, kTsXReady, kTsQKVDone, kTsAttnDone, kTsOReady, kTsODone, kTsGUReady,
   kTsGUDone, kTsDownReady, kTsDownDone, kTraceStampsPerLayer
 };
-inline int trace_stride_for(int n_layers) { return 3 + n_layers * kTraceStampsPerLayer + 2; }
+// Per CTA: 3 head stamps, 10 per layer, 2 for the LM head, then 5 inside the
+// attention unit of the middle layer (start, q/k/v in, partial done, partials
+// of all splits in, output written) on the CTAs that run one.
+constexpr int kAttnTraceStamps = 5;
+inline int trace_stride_for(int n_layers) {
+  return 3 + n_layers * kTraceStampsPerLayer + 2 + kAttnTraceStamps;
+}
 
 // One streamed unit of weights for one CTA, packed in 64 bits:
 //   bits  0..7   phase  (layer * 5 + FusedPhase, or n_layers * 5 for the LM head)

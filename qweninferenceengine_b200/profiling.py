@@ -21,6 +21,7 @@ from .engine import QwenConfig, QwenEngine
 
 STAMPS = ["start", "x_ready", "qkv_done", "attn_done", "o_ready", "o_done", "gu_ready",
           "gu_done", "h_ready", "down_done"]
+ATTN_STAMPS = ["unit_start", "qkv_in", "partial_done", "splits_in", "output_written"]
 
 
 def run_case(layers: int, steps: int) -> None:
@@ -46,7 +47,7 @@ def run_trace(layers: int, ctx: int, show_layers) -> dict:
     eng.trace(False)
     eng.close()
     k = len(STAMPS)
-    grid = tr.size // (3 + k * layers + 2)
+    grid = tr.size // (3 + k * layers + 2 + len(ATTN_STAMPS))
     tr = tr.reshape(grid, -1)
     t0 = tr[:, 2].min()
     rel = np.where(tr > 0, (tr - t0) / 1000.0, np.nan)
@@ -56,6 +57,15 @@ def run_trace(layers: int, ctx: int, show_layers) -> dict:
            "end_us": float(np.nanmax(rel[:, 4 + k * layers])), "layers": {}}
     periods = np.diff(np.nanmedian(ph[:, :, 0], axis=0))
     out["layer_period_us"] = float(np.median(periods)) if periods.size else None
+    mid = layers // 2
+    att = rel[:, 3 + k * layers + 2:]
+    have = ~np.isnan(att[:, 0])
+    if have.any():
+        base = np.nanmedian(ph[:, mid, 0])
+        out["attention_unit"] = {name: (float(np.nanmin(att[have, j]) - base),
+                                        float(np.nanmedian(att[have, j]) - base),
+                                        float(np.nanmax(att[have, j]) - base))
+                                 for j, name in enumerate(ATTN_STAMPS)}
     for layer in show_layers:
         if layer >= layers:
             continue
@@ -89,6 +99,10 @@ def main() -> None:
     print(f"step {r['ms_step']:.3f} ms, model kernels {r['ms_model']:.3f} ms, grid {r['grid']}, "
           f"median layer period {r['layer_period_us']:.2f} us, LM head from {r['lm_start_us']:.1f} "
           f"to {r['end_us']:.1f} us")
+    if "attention_unit" in r:
+        print(f"attention units of layer {a.layers // 2} (us from the layer's median start; min / med / max)")
+        for name, (lo, med, hi) in r["attention_unit"].items():
+            print(f"  {name:14s} {lo:7.2f} {med:7.2f} {hi:7.2f}")
     for layer, rows in r["layers"].items():
         print(f"layer {layer} (us from the layer's median start; n = CTAs with the stamp)")
         for name, (n, lo, med, hi) in rows.items():
