@@ -260,9 +260,10 @@ int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n)
  * start, then 10 per layer at [3 + 10*layer + k]: k = 0 layer start, 1 x ready,
  * 2 QKV done, 3 attention done, 4 attention output ready, 5 O done, 6 gate/up
  * input ready, 7 gate/up done, 8 h ready, 9 down done; then LM-head start and
- * consumer end; then 5 stamps inside the attention unit of layer n_layers/2
- * (unit start, q/k/v in, partial done, all splits' partials in, output
- * written; zero on CTAs without a unit); stride 3 + 10*n_layers + 2 + 5.
+ * consumer end; then 7 stamps inside the attention unit of layer n_layers/2
+ * (unit start, q/k/v in, warp 0's positions done, the unit's warps merged,
+ * partials written, all splits' partials in, output slice written; zero on
+ * CTAs without a unit); stride 3 + 10*n_layers + 2 + 7.
  * qwen_engine_get_trace copies the last step's stamps ([grid][stride]) when
  * n >= *needed, and always reports *needed. */
 int qwen_engine_trace(qwen_engine* e, int32_t enable);

@@ -63,6 +63,10 @@ constexpr int kAWl = kAWm + kAttnWarpsFused * 8 * 4;
 constexpr int kAKnew = kAWl + kAttnWarpsFused * 8 * 4;    // [128] fp16 new k
 constexpr int kAVnew = kAKnew + 256;                      // [128] fp16 new v
 static_assert(kAVnew + 256 <= kUnionBytes, "attention buffers exceed the union region");
+// Merge factors, after the warp merge buffer (which aliases the dead V rows).
+constexpr int kAFac = kAVs + kAttnWarpsFused * 6 * 128 * 4;  // 36 floats
+constexpr int kACFac = kAFac + 256;                           // [74][2] + [6] floats
+static_assert(kACFac + (kMaxAttnSplits * 2 + 8) * 4 <= kAPt, "merge factors exceed the V rows");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kAttnWarpsFused * 6 * 128 * 4 <= kAPt, "warp merge buffer aliases the V rows");
 
@@ -224,8 +228,15 @@ __device__ __forceinline__ int it_phase_of(const FusedItem* items, int i) {
 
 // RMSNorm of xloc (rmsnorm.metal:9-46): out = half(half(x * s) * gamma).
 // Writes Q4 x fragments (frags) and/or plain fp16 (plain).  256 consumer threads.
-__device__ __forceinline__ void rmsnorm_out(const __half* xloc, const __half* __restrict__ gamma, float* red2,
-                            volatile Misc* misc, uint4* frags, __half* plain, int ct) {
+// gamma_u: this thread's 8 gamma values (unit ct, threads < 192), loaded by
+// the caller before its wait for x so the load is off the critical path.
+__device__ __forceinline__ uint4 gamma_prefetch(const __half* __restrict__ gamma, int ct) {
+  return ct < kHidden / 8 ? __ldg(reinterpret_cast<const uint4*>(gamma) + ct) : make_uint4(0, 0, 0, 0);
+}
+
+// RMSNorm of xloc (rmsnorm.metal:9-46): out = half(half(x * s) * gamma).
+__device__ __forceinline__ void rmsnorm_out(const __half* xloc, uint4 gamma_u, float* red2,
+                                            uint4* frags, __half* plain, int ct) {
   float ss = 0.f;
   for (int i = ct; i < kHidden; i += 256) {
     const float v = h2f(xloc[i]);
@@ -234,23 +245,19 @@ __device__ __forceinline__ void rmsnorm_out(const __half* xloc, const __half* __
   ss = warp_sum(ss);
   if ((ct & 31) == 0) red2[ct >> 5] = ss;
   cbar();
-  if (ct == 0) {
-    float tot = 0.f;
-    for (int w = 0; w < kConsumerWarps; ++w) tot += red2[w];
-    misc->scale = 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
-  }
-  cbar();
-  const float s = misc->scale;
-  for (int u = ct; u < kHidden / 8; u += 256) {
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) tot += red2[w];
+  const float s = 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
+  if (ct < kHidden / 8) {
     __half v[8];
-    const uint4 raw = reinterpret_cast<const uint4*>(xloc)[u];
-    const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gamma) + u);
+    const uint4 raw = reinterpret_cast<const uint4*>(xloc)[ct];
     const __half* xv = reinterpret_cast<const __half*>(&raw);
-    const __half* gv = reinterpret_cast<const __half*>(&graw);
+    const __half* gv = reinterpret_cast<const __half*>(&gamma_u);
 #pragma unroll
     for (int q = 0; q < 8; ++q) v[q] = __hmul(f2h(h2f(xv[q]) * s), gv[q]);
-    if (frags) frags[u] = make_xfrag(v);
-    if (plain) reinterpret_cast<uint4*>(plain)[u] = *reinterpret_cast<uint4*>(v);
+    if (frags) frags[ct] = make_xfrag(v);
+    if (plain) reinterpret_cast<uint4*>(plain)[ct] = *reinterpret_cast<uint4*>(v);
   }
   cbar();
 }
@@ -494,27 +501,39 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
       if (head < 6) wo[(warp * 6 + head) * kHeadDim + d] = o[i][j];
     }
   abar();
+  astamp(3);
+  // Rescale factors of the 4 warps per head, computed once (they depend on the
+  // head only); factor 0 for a warp without positions.
+  float* fac = reinterpret_cast<float*>(uni + kAFac);  // [4][6] factors, [6] max, [6] sum
+  if (ct < 6) {
+    const int head = ct;
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarpsFused; ++w) M = fmaxf(M, wm[w * 8 + head]);
+    float Ls = 0.f;
+    for (int w = 0; w < kAttnWarpsFused; ++w) {
+      const float mw = wm[w * 8 + head];
+      const float c = mw == -INFINITY ? 0.f : expf(mw - M);
+      fac[w * 6 + head] = c;
+      Ls += wl[w * 8 + head] * c;
+    }
+    fac[24 + head] = M;
+    fac[30 + head] = Ls;
+  }
+  abar();
   unsigned long long* part = p.attn_part + ((size_t)kvh * kMaxAttnSplits + s) * kAttnPartWords;
   for (int idx = ct; idx < 6 * kHeadDim; idx += 128) {
     const int head = idx / kHeadDim, d = idx % kHeadDim;
-    float M = -INFINITY;
-    for (int w = 0; w < kAttnWarpsFused; ++w) M = fmaxf(M, wm[w * 8 + head]);
-    float Ls = 0.f, O = 0.f;
-    for (int w = 0; w < kAttnWarpsFused; ++w) {
-      const float mw = wm[w * 8 + head];
-      if (mw == -INFINITY) continue;
-      const float c = expf(mw - M);
-      Ls += wl[w * 8 + head] * c;
-      O += wo[(w * 6 + head) * kHeadDim + d] * c;
-    }
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarpsFused; ++w) O += wo[(w * 6 + head) * kHeadDim + d] * fac[w * 6 + head];
     st_tag32(part + idx, tag, O);
     if (d == 0) {
-      st_tag32(part + 768 + head, tag, M);
-      st_tag32(part + 774 + head, tag, Ls);
+      st_tag32(part + 768 + head, tag, fac[24 + head]);
+      st_tag32(part + 774 + head, tag, fac[30 + head]);
     }
   }
   abar();
-  astamp(3);
+  astamp(4);
   // ---- combine: this unit produces outputs [z0, z1) of its kv head.
   const uint32_t Z = (768 + S_eff - 1) / S_eff;
   const uint32_t z0 = min(768u, s * Z), z1 = min(768u, z0 + Z);
@@ -563,19 +582,30 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
     }
   }
   abar();
-  astamp(4);
-  for (uint32_t z = z0 + ct; z < z1; z += 128) {
-    const uint32_t hl = z / kHeadDim - h0;
+  astamp(5);
+  // Per (split, head of the slice) rescale factors and per-head totals, once.
+  float* cfac = reinterpret_cast<float*>(uni + kACFac);  // [S_eff][nh] factors, then [nh] totals
+  float* ctot = cfac + kMaxAttnSplits * 2;
+  if (ct < (int)nh) {
+    const uint32_t hl = ct;
     float M = -INFINITY;
     for (uint32_t sp = 0; sp < S_eff; ++sp) M = fmaxf(M, stage[sp * per_split + nz + hl]);
-    float Ls = 0.f, O = 0.f;
+    float Ls = 0.f;
     for (uint32_t sp = 0; sp < S_eff; ++sp) {
       const float c = expf(stage[sp * per_split + nz + hl] - M);
+      cfac[sp * nh + hl] = c;
       Ls += stage[sp * per_split + nz + nh + hl] * c;
-      O += stage[sp * per_split + (z - z0)] * c;
     }
-    st_tag16(p.attn_ll + kvh * 768 + z, tag, f2h(O / Ls));
+    ctot[hl] = Ls;
   }
+  abar();
+  for (uint32_t z = z0 + ct; z < z1; z += 128) {
+    const uint32_t hl = z / kHeadDim - h0;
+    float O = 0.f;
+    for (uint32_t sp = 0; sp < S_eff; ++sp) O += stage[sp * per_split + (z - z0)] * cfac[sp * nh + hl];
+    st_tag16(p.attn_ll + kvh * 768 + z, tag, f2h(O / ctot[hl]));
+  }
+  astamp(6);
 }
 
 }  // namespace
@@ -702,6 +732,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       const uint16_t ph = (uint16_t)(layer * kPhasesPerLayer);
       if (ct == 0) misc->cphase = ph * 1000 + cur;
       lstamp(layer, kTsLayerStart);
+      // Activation-independent inputs of this layer's QKV phase, fetched before
+      // the wait for x: the input RMSNorm gamma, and for the first QKV tile the
+      // rows' biases and the RoPE cos/sin of threads 0..15.
+      const uint4 gamma_in = gamma_prefetch(p.norms + (size_t)(2 * layer) * kHidden, ct);
+      const int e_qkv = phase_end(ph + kPhQKV);
+      const int qtile = e_qkv > cur ? (int)unpack_item(items[cur]).tile : -1;
+      float qbias = 0.f, qcos = 1.f, qsin = 0.f;
+      if (qtile >= 0 && ct < 16) {
+        const int head = qtile >> 3, j = qtile & 7, r = ct;
+        const int row = head * 128 + (r < 8 ? 8 * j + r : 64 + 8 * j + (r - 8));
+        qbias = h2f(p.qkv_bias[(size_t)layer * kQKVRows + row]);
+        if (r < 8 && head < 14) {
+          qcos = rope[2 * (8 * j + r)];
+          qsin = rope[2 * (8 * j + r) + 1];
+        }
+      }
       // ---- x after the previous layer (or the embedding row, :57-60)
       if (layer == 0) {
         const uint4* src = reinterpret_cast<const uint4*>(p.embed + (size_t)token * kHidden);
@@ -716,9 +762,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       lstamp(layer, kTsXReady);
       // ---- P1: RMSNorm -> QKV -> bias -> RoPE -> q, KV cache
       {
-        const int e = phase_end(ph + kPhQKV);
+        const int e = e_qkv;
         if (e > cur) {
-          rmsnorm_out(xloc, p.norms + (size_t)(2 * layer) * kHidden, red2, misc, xf, nullptr, ct);
+          rmsnorm_out(xloc, gamma_in, red2, xf, nullptr, ct);
           const uint16_t tg = (uint16_t)tagof(layer);
           __half* kc = p.kc + (size_t)layer * p.kv_layer_stride + (size_t)(L - 1) * kKVDim;
           __half* vc = p.vc + (size_t)layer * p.kv_layer_stride + (size_t)(L - 1) * kKVDim;
@@ -727,14 +773,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           ksplit(e, [&](int tile, int r, float sum) {
             const int head = tile >> 3, j = tile & 7;
             const int row = head * 128 + (r < 8 ? 8 * j + r : 64 + 8 * j + (r - 8));
-            red2[r] = h2f(f2h(sum + h2f(bias[row])));
+            const bool pre = tile == qtile;  // prefetched bias / cos / sin
+            red2[r] = h2f(f2h(sum + (pre ? qbias : h2f(bias[row]))));
             __syncwarp(0xffffu);
             if (r >= 8) return;
             const float x1 = red2[r], x2 = red2[r + 8];
             const int i = 8 * j + r;  // rotate-half pair index (rope.metal:17-22)
             __half o1, o2;
             if (head < 14) {
-              const float c = rope[2 * i], sn = rope[2 * i + 1];
+              const float c = pre ? qcos : rope[2 * i], sn = pre ? qsin : rope[2 * i + 1];
               o1 = f2h(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
               o2 = f2h(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, c)));
             } else {
@@ -782,6 +829,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       {
         const int e = phase_end(ph + kPhO);
         if (e > cur) {
+          const __half* ob = p.o_bias + (size_t)layer * kHidden;
+          const int otile = (int)unpack_item(items[cur]).tile;
+          const float obias = ct < 16 ? h2f(ob[16 * otile + ct]) : 0.f;
           poll_units<1>(p.attn_ll, kHidden / 8, ct, 256, tagof(layer), misc, p.err,
                         kSiteAttnOut * 100 + layer, [&](int u, const __half* v) {
                           __half tmp[8];
@@ -791,17 +841,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
                         });
           cbar();
           lstamp(layer, kTsOReady);
-          const __half* ob = p.o_bias + (size_t)layer * kHidden;
           const uint16_t tg = (uint16_t)tagof(2 * layer + 1);
           ksplit(e, [&](int tile, int r, float sum) {
             const int row = 16 * tile + r;
-            const __half o = f2h(sum + h2f(ob[row]));
+            const __half o = f2h(sum + (tile == otile ? obias : h2f(ob[row])));
             st_tag16(p.x_ll + row, tg, __hadd(xloc[row], o));
           });
         }
       }
       lstamp(layer, kTsODone);
       // ---- P4: x -> RMSNorm -> gate|up -> SwiGLU -> h (each warp owns whole tiles)
+      const uint4 gamma_post = gamma_prefetch(p.norms + (size_t)(2 * layer + 1) * kHidden, ct);
       poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * layer + 1), misc, p.err,
                     kSiteXMid * 100 + layer, [&](int u, const __half* v) {
                       reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
@@ -809,7 +859,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       cbar();
       {
         const int e = phase_end(ph + kPhGU);
-        rmsnorm_out(xloc, p.norms + (size_t)(2 * layer + 1) * kHidden, red2, misc, xf, nullptr, ct);
+        rmsnorm_out(xloc, gamma_post, red2, xf, nullptr, ct);
         lstamp(layer, kTsGUReady);
         const uint16_t tg = (uint16_t)tagof(layer);
         for (int i = cur; i < e; ++i) {
@@ -839,6 +889,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       {
         const int e = phase_end(ph + kPhDown);
         if (e > cur) {
+          const __half* db = p.down_bias + (size_t)layer * kHidden;
+          const int dtile = (int)unpack_item(items[cur]).tile;
+          const float dbias = ct < 16 ? h2f(db[16 * dtile + ct]) : 0.f;
           poll_units<5>(p.h_ll, kInter / 8, ct, 256, tagof(layer), misc, p.err,
                         kSiteH * 100 + layer, [&](int u, const __half* v) {
                           __half tmp[8];
@@ -848,11 +901,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
                         });
           cbar();
           lstamp(layer, kTsDownReady);
-          const __half* db = p.down_bias + (size_t)layer * kHidden;
           const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
           ksplit(e, [&](int tile, int r, float sum) {
             const int row = 16 * tile + r;
-            const __half d = f2h(sum + h2f(db[row]));
+            const __half d = f2h(sum + (tile == dtile ? dbias : h2f(db[row])));
             st_tag16(p.x_ll + row, tg, __hadd(xloc[row], d));
           });
         }
@@ -863,12 +915,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     // ---- final RMSNorm + LM head (each warp owns whole 16-row tiles)
     if (ct == 0) misc->cphase = lm_phase * 1000 + cur;
     stamp(3 + p.n_layers * kTraceStampsPerLayer);
+    const uint4 gamma_final = gamma_prefetch(p.norms + (size_t)(2 * p.n_layers) * kHidden, ct);
     poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * p.n_layers), misc, p.err,
                   kSiteXFinal * 100, [&](int u, const __half* v) {
                     reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
                   });
     cbar();
-    rmsnorm_out(xloc, p.norms + (size_t)(2 * p.n_layers) * kHidden, red2, misc, nullptr, xn, ct);
+    rmsnorm_out(xloc, gamma_final, red2, nullptr, xn, ct);
     {
       const int e = phase_end(lm_phase);
       float d[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};

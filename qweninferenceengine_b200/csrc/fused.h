@@ -56,10 +56,11 @@ enum TraceStamp : int {
   kTsLayerStart = 0, kTsXReady, kTsQKVDone, kTsAttnDone, kTsOReady, kTsODone, kTsGUReady,
   kTsGUDone, kTsDownReady, kTsDownDone, kTraceStampsPerLayer
 };
-// Per CTA: 3 head stamps, 10 per layer, 2 for the LM head, then 5 inside the
-// attention unit of the middle layer (start, q/k/v in, partial done, partials
-// of all splits in, output written) on the CTAs that run one.
-constexpr int kAttnTraceStamps = 5;
+// Per CTA: 3 head stamps, 10 per layer, 2 for the LM head, then 7 inside the
+// attention unit of the middle layer (start, q/k/v in, warp 0's positions
+// done, the unit's warps merged, partials written, partials of all splits in,
+// output slice written) on the CTAs that run one.
+constexpr int kAttnTraceStamps = 7;
 inline int trace_stride_for(int n_layers) {
   return 3 + n_layers * kTraceStampsPerLayer + 2 + kAttnTraceStamps;
 }

@@ -21,7 +21,8 @@ from .engine import QwenConfig, QwenEngine
 
 STAMPS = ["start", "x_ready", "qkv_done", "attn_done", "o_ready", "o_done", "gu_ready",
           "gu_done", "h_ready", "down_done"]
-ATTN_STAMPS = ["unit_start", "qkv_in", "partial_done", "splits_in", "output_written"]
+ATTN_STAMPS = ["unit_start", "qkv_in", "warp0_done", "warps_merged", "partials_out",
+               "splits_in", "output_out"]
 
 
 def run_case(layers: int, steps: int) -> None:
