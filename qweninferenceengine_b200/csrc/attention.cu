@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         Unit w;
         if (!unit_of(p, u, max_s, w)) continue;
-        const int row0 = w.seq * rows_per_seq;
+        const int row0 = (p.row_seq ? p.row_seq[w.seq] : w.seq) * rows_per_seq;
         for (uint32_t base = w.p0; base < w.p1; base += kTilePos, ++it) {
           const int st = it % kStages;
           if (it >= kStages && !attn_wait(&s.empty[st], ((it / kStages) - 1) & 1, s, p.err))
@@ -514,8 +514,9 @@ int launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cuda
       max_splits < 1 || max_splits > kMaxSplits || n_seq < 1 || p.max_ctx < 1)
     return -1;
   const int rows_per_seq = (int)(p.kv_seq_stride / kKVDim);
-  if (n_seq > 1 && rows_per_seq < (int)p.max_ctx) return -1;
-  const uint64_t rows = (uint64_t)(n_seq - 1) * rows_per_seq + p.max_ctx;
+  const int kv_seqs = p.kv_n_seq > 0 ? p.kv_n_seq : n_seq;
+  if (kv_seqs > 1 && rows_per_seq < (int)p.max_ctx) return -1;
+  const uint64_t rows = (uint64_t)(kv_seqs - 1) * rows_per_seq + p.max_ctx;
   CUtensorMap tmk, tmv;
   if (!encode_kv_map(&tmk, p.k, rows) || !encode_kv_map(&tmv, p.v, rows)) return -1;
   int dev = 0, sms = 148;

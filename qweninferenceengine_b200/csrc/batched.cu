@@ -129,12 +129,15 @@ __device__ __forceinline__ float sum_splits(const float* __restrict__ part, int 
 __global__ void __launch_bounds__(64) k_qkv_finish(const float* __restrict__ part, int splits, int nbv,
                                                    const __half* __restrict__ bias,
                                                    const float* __restrict__ rope_cs,
-                                                   const SeqCtl* __restrict__ ctl, int max_ctx,
+                                                   const uint32_t* __restrict__ seq_len,
+                                                   int seq_len_stride,
+                                                   const int32_t* __restrict__ row_seq, int max_ctx,
                                                    __half* __restrict__ q, __half* __restrict__ kc,
                                                    __half* __restrict__ vc, size_t kv_seq_stride) {
   pdl_prologue();
   const int b = blockIdx.x, head = blockIdx.y, t = threadIdx.x;
-  const uint32_t L = ctl[b].seq_len;
+  const uint32_t L = seq_len[(size_t)b * seq_len_stride];
+  const int kvs = row_seq ? row_seq[b] : b;  // the row's KV sequence
   const uint32_t pos = L - 1;
   if (L == 0 || pos >= (uint32_t)max_ctx) return;  // step_begin clamps; never taken
   if (head < kHeads + kKVHeads) {
@@ -150,12 +153,12 @@ __global__ void __launch_bounds__(64) k_qkv_finish(const float* __restrict__ par
       q[(size_t)b * kHidden + i0] = r1;
       q[(size_t)b * kHidden + i0 + 64] = r2;
     } else {
-      __half* kr = kc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
+      __half* kr = kc + (size_t)kvs * kv_seq_stride + (size_t)pos * kKVDim;
       kr[i0 - kHidden] = r1;
       kr[i0 - kHidden + 64] = r2;
     }
   } else {
-    __half* vr = vc + (size_t)b * kv_seq_stride + (size_t)pos * kKVDim;
+    __half* vr = vc + (size_t)kvs * kv_seq_stride + (size_t)pos * kKVDim;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int i = kHidden + kKVDim + t + 64 * e;
@@ -191,6 +194,19 @@ __global__ void __launch_bounds__(512) k_resid_norm_finish(const float* __restri
   }
 }
 
+// Row r = position p0 + r of sequence 0: x[r] = embedding of its prompt id,
+// len[r] = p0 + r + 1 (InferenceEngine.swift:57-60 per position).
+__global__ void __launch_bounds__(192) k_prefill_rows(const int32_t* __restrict__ prompt, int p0,
+                                                      const __half* __restrict__ embed,
+                                                      __half* __restrict__ x,
+                                                      uint32_t* __restrict__ len) {
+  const int r = blockIdx.x;
+  const int32_t tok = prompt[p0 + r];
+  if (threadIdx.x == 0) len[r] = (uint32_t)(p0 + r + 1);
+  reinterpret_cast<uint4*>(x + (size_t)r * kHidden)[threadIdx.x] =
+      reinterpret_cast<const uint4*>(embed + (size_t)tok * kHidden)[threadIdx.x];
+}
+
 struct TcPlan {
   int qkv, o, down;  // K splits (gate/up runs unsplit: its epilogue needs whole sums)
 };
@@ -201,15 +217,16 @@ TcPlan plan_for(int sm_count) {
                 tc_choose_splits(kDownTiles, kChunks8960, sm_count)};
 }
 
-int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManager& s, int n_rows,
-         int k, int splits, float* part, __half* out, long long ld_out, cudaStream_t st,
+int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManager& s, int rows,
+         int n_rows, int k, int splits, float* part, __half* out, long long ld_out, cudaStream_t st,
          uint8_t* swiglu_act = nullptr) {
   TcGemmArgs a;
   a.w = blob;
   a.q4 = q4;
   a.act = act;
-  a.nb = s.tc_nb;
-  a.nb_valid = s.batch;
+  a.nb = act_rows(rows);
+  a.act_stride_rows = s.tc_nb;
+  a.nb_valid = rows;
   a.n_rows = n_rows;
   a.k = k;
   a.splits = splits;
@@ -267,19 +284,45 @@ int tc_state_allocate(InferenceManager& s, int sm_count) {
   if (s.act_h) return QWEN_OK;
   if (s.batch > kTcMaxNb)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "tensor-core step: batch %d > %d", s.batch, kTcMaxNb);
-  s.tc_nb = act_rows(s.batch);
+  // A batch-1 engine also prefills in chunks of kTcPrefillRows positions.
+  s.tc_rows = s.batch == 1 ? kTcPrefillRows : s.batch;
+  s.tc_nb = act_rows(s.tc_rows);
   const TcPlan p = plan_for(sm_count);
   const size_t part = std::max((size_t)p.qkv * kQKVRows,
                                std::max((size_t)p.o * kHidden, (size_t)p.down * kHidden)) *
-                      s.batch;
+                      s.tc_rows;
   QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kHidden), (void**)&s.act_h));
   QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kInter), (void**)&s.act_i));
   QWEN_TRY(s.alloc_tracked(part * sizeof(float), (void**)&s.tc_part));
+  if (s.tc_rows > s.batch) {
+    const size_t R = (size_t)s.tc_rows;
+    QWEN_TRY(s.alloc_tracked(R * kHidden * 2, (void**)&s.tc_px));
+    QWEN_TRY(s.alloc_tracked(R * kHidden * 2, (void**)&s.tc_pq));
+    QWEN_TRY(s.alloc_tracked(R * kVocab * 2, (void**)&s.tc_plogits));
+    QWEN_TRY(s.alloc_tracked(R * sizeof(uint32_t), (void**)&s.tc_row_len));
+    QWEN_TRY(s.alloc_tracked(R * sizeof(int32_t), (void**)&s.tc_row_seq));
+    s.tc_psplits = attn_max_splits(s.max_ctx, s.tc_rows);
+    QWEN_TRY(s.alloc_tracked(attn_scratch_bytes(s.tc_psplits, s.tc_rows), &s.tc_pattn));
+  }
   return QWEN_OK;
 }
 
-int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st,
-                     cudaEvent_t* marks, int* n_marks) {
+TcRows tc_decode_rows(InferenceManager& s) {
+  return TcRows{s.batch,        s.x,           s.q,
+                &s.ctl[0].seq_len, (int)(sizeof(SeqCtl) / sizeof(uint32_t)), nullptr,
+                s.attn_scratch, s.attn_splits, s.logits};
+}
+
+int launch_prefill_rows(InferenceManager& s, const __half* embed, int p0, int rows,
+                        cudaStream_t st) {
+  if (!s.tc_px || rows < 1 || rows > s.tc_rows || p0 < 0 || p0 + rows > s.max_ctx)
+    return set_error(QWEN_ERR_STATE, "chunked prefill: bad rows");
+  k_prefill_rows<<<rows, kHidden / 8, 0, st>>>(s.prompt, p0, embed, s.tc_px, s.tc_row_len);
+  return launch_status("prefill rows");
+}
+
+int enqueue_tc_model(QwenModel& m, InferenceManager& s, const TcRows& v, int sm_count,
+                     cudaStream_t st, cudaEvent_t* marks, int* n_marks) {
   // Optional per-launch timeline: an event after every kernel.
   auto mark = [&]() {
     if (marks) cudaEventRecord(marks[(*n_marks)++], st);
@@ -287,27 +330,30 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
   const TcWeights& t = m.tc;
   if (!t.blob || !s.act_h) return set_error(QWEN_ERR_STATE, "tensor-core step not prepared");
   if (t.rope_ctx < s.max_ctx) return set_error(QWEN_ERR_STATE, "RoPE table shorter than max_ctx");
+  if (v.rows < 1 || v.rows > s.tc_rows) return set_error(QWEN_ERR_STATE, "tensor-core step: %d rows", v.rows);
   const TcPlan p = plan_for(sm_count);
   if (std::max(p.qkv, std::max(p.o, p.down)) > kTcMaxSplits)
     return set_error(QWEN_ERR_STATE, "tensor-core step: split plan exceeds %d", kTcMaxSplits);
-  const int B = s.batch, nb = s.tc_nb;
+  const int B = v.rows, nb = s.tc_nb;
   AttnParams ap{};
-  ap.q = s.q;
+  ap.q = v.q;
   ap.q_seq_stride = kHidden;
   ap.kv_seq_stride = (long long)s.kv_seq_stride();
   ap.kv_pos_stride = kKVDim;
   ap.kv_head_stride = kHeadDim;
-  ap.seq_len = &s.ctl[0].seq_len;
-  ap.seq_len_stride = (int)(sizeof(SeqCtl) / sizeof(uint32_t));
+  ap.seq_len = v.seq_len;
+  ap.seq_len_stride = v.seq_len_stride;
   ap.max_ctx = (uint32_t)s.max_ctx;
   ap.out = s.attn_out;
   ap.out_seq_stride = kHidden;
   ap.act_out = s.act_h;  // the O projection's input tiles, written directly
   ap.act_nb = nb;
+  ap.row_seq = v.row_seq;
+  ap.kv_n_seq = s.batch;
   ap.err = s.err;
-  attn_bind_scratch(ap, s.attn_scratch, s.attn_splits, B);
+  attn_bind_scratch(ap, v.attn_scratch, v.attn_splits, B);
 
-  QWEN_TRY(launch_pdl(k_rms_to_act, dim3(B), dim3(512), st, s.x, m.layers[0].input_norm, s.act_h, nb));
+  QWEN_TRY(launch_pdl(k_rms_to_act, dim3(B), dim3(512), st, v.x, m.layers[0].input_norm, s.act_h, nb));
   mark();
   for (int l = 0; l < m.n_layers; ++l) {
     const QwenLayer& L = m.layers[l];
@@ -318,34 +364,36 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream
     __half* kc = s.kc + (size_t)l * s.kv_layer_stride();
     __half* vc = s.vc + (size_t)l * s.kv_layer_stride();
 
-    QWEN_TRY(gemm(qkv, true, s.act_h, s, kQKVRows, kHidden, p.qkv, s.tc_part, nullptr, 0, st));
+    QWEN_TRY(gemm(qkv, true, s.act_h, s, B, kQKVRows, kHidden, p.qkv, s.tc_part, nullptr, 0, st));
     mark();
     QWEN_TRY(launch_pdl(k_qkv_finish, dim3(B, kHeads + kKVHeads + 1), dim3(64), st, s.tc_part,
-                        p.qkv, B, L.qkv_bias, t.rope_cs, s.ctl, s.max_ctx, s.q, kc, vc,
-                        s.kv_seq_stride()));
+                        p.qkv, B, L.qkv_bias, t.rope_cs, v.seq_len, v.seq_len_stride, v.row_seq,
+                        s.max_ctx, v.q, kc, vc, s.kv_seq_stride()));
     mark();
     ap.k = kc;
     ap.v = vc;
-    if (launch_attention_decode(ap, s.attn_splits, B, st, true) != 0)
+    if (launch_attention_decode(ap, v.attn_splits, B, st, true) != 0)
       return set_error(QWEN_ERR_CUDA, "attention launch failed (%s)", cudaGetErrorString(cudaGetLastError()));
     mark();
-    QWEN_TRY(gemm(o, true, s.act_h, s, kHidden, kHidden, p.o, s.tc_part, nullptr, 0, st));
+    QWEN_TRY(gemm(o, true, s.act_h, s, B, kHidden, kHidden, p.o, s.tc_part, nullptr, 0, st));
     mark();
     QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.o, B, L.o_bias,
-                        s.x, L.post_attn_norm, s.act_h, nb));
+                        v.x, L.post_attn_norm, s.act_h, nb));
     mark();
-    QWEN_TRY(gemm(gu, true, s.act_h, s, 2 * kInter, kHidden, 1, nullptr, nullptr, 0, st, s.act_i));
+    QWEN_TRY(gemm(gu, true, s.act_h, s, B, 2 * kInter, kHidden, 1, nullptr, nullptr, 0, st, s.act_i));
     mark();
-    QWEN_TRY(gemm(down, true, s.act_i, s, kHidden, kInter, p.down, s.tc_part, nullptr, 0, st));
+    QWEN_TRY(gemm(down, true, s.act_i, s, B, kHidden, kInter, p.down, s.tc_part, nullptr, 0, st));
     mark();
     const __half* next_norm = l + 1 < m.n_layers ? m.layers[l + 1].input_norm : m.final_norm;
     QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.down, B,
-                        L.down_bias, s.x, next_norm, s.act_h, nb));
+                        L.down_bias, v.x, next_norm, s.act_h, nb));
     mark();
   }
-  QWEN_TRY(gemm(t.lm, false, s.act_h, s, kVocab, kHidden, 1, nullptr, s.logits, kVocab, st));
-  mark();
-  return launch_status("tensor-core decode step");
+  if (v.logits) {
+    QWEN_TRY(gemm(t.lm, false, s.act_h, s, B, kVocab, kHidden, 1, nullptr, v.logits, kVocab, st));
+    mark();
+  }
+  return launch_status("tensor-core model step");
 }
 
 }  // namespace qwen

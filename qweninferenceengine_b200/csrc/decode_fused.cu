@@ -335,10 +335,14 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
     const int r = lane >> 1, hs = lane & 1;
     const uint32_t pos = base + r;
     uint8_t* dst = vs + r * 272 + hs * 128;
-    if (pos < p1) {
-      const uint8_t* src = (have_new && pos == last)
-                               ? reinterpret_cast<const uint8_t*>(vnew) + hs * 128
-                               : reinterpret_cast<const uint8_t*>(vbase + (size_t)pos * kKVDim) + hs * 128;
+    if (pos < p1 && have_new && pos == last) {
+      // The step's new row is already in shared memory (vnew): a plain copy
+      // (cp.async.*.shared.global only takes a global source).
+      const uint4* src = reinterpret_cast<const uint4*>(vnew) + hs * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(dst)[j] = src[j];
+    } else if (pos < p1) {
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(vbase + (size_t)pos * kKVDim) + hs * 128;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + 16 * j)),

@@ -435,7 +435,7 @@ int QwenEngine::enqueue_step_tc(cudaEvent_t* ev) {
   k_step_begin<<<s.batch, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
                                         s.max_ctx, cfg_.seed, s.err, s.epoch);
   if (ev) cudaEventRecord(ev[1], st);
-  QWEN_TRY(enqueue_tc_model(model_, state_, sm_count_, st));
+  QWEN_TRY(enqueue_tc_model(model_, state_, tc_decode_rows(state_), sm_count_, st));
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
                     s.sampled, nullptr, s.err, st) != 0)
@@ -494,7 +494,13 @@ int QwenEngine::check_device_error() {
 
 int QwenEngine::run_steps(int n) {
   QWEN_TRY(ensure_graph());
-  for (int i = 0; i < n; ++i) QWEN_CUDA(cudaGraphLaunch(graph_exec_, stream_), "cudaGraphLaunch");
+  // At most kMaxQueuedSteps step graphs are queued on the stream at a time
+  // (long prefills would otherwise queue thousands of launches).
+  constexpr int kMaxQueuedSteps = 256;
+  for (int i = 0; i < n; ++i) {
+    if (i > 0 && i % kMaxQueuedSteps == 0) QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
+    QWEN_CUDA(cudaGraphLaunch(graph_exec_, stream_), "cudaGraphLaunch");
+  }
   return QWEN_OK;
 }
 
@@ -629,7 +635,8 @@ int QwenEngine::profile_step(float* ms, int cap, int* n) {
                                         s.max_ctx, cfg_.seed, s.err, s.epoch);
   cudaEventRecord(ev[0], st);
   int marks = 0;
-  int rc = enqueue_tc_model(model_, state_, sm_count_, st, ev.data() + 1, &marks);
+  int rc = enqueue_tc_model(model_, state_, tc_decode_rows(state_), sm_count_, st, ev.data() + 1,
+                            &marks);
   if (rc == QWEN_OK && launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature,
                                      cfg_.top_p, s.u24_, s.sampled, nullptr, s.err, st) != 0)
     rc = launch_status("sample");
@@ -650,6 +657,8 @@ int QwenEngine::prefill(const int32_t* ids, int32_t n) {
   if (n < 1) return set_error(QWEN_ERR_INVALID_ARGUMENT, "empty prompt");
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_TRY(ensure_graph());
+  if (cfg_.kernels == QWEN_KERNELS_TC && state_.batch == 1 && n > 1 && state_.tc_px)
+    return prefill_chunked(ids, n);
   QWEN_TRY(upload_prompt(ids, n, 0));
   std::vector<SeqCtl> c(state_.batch);
   for (auto& x : c) {
@@ -659,6 +668,45 @@ int QwenEngine::prefill(const int32_t* ids, int32_t n) {
   QWEN_CUDA(cudaMemcpyAsync(state_.ctl, c.data(), sizeof(SeqCtl) * c.size(), cudaMemcpyHostToDevice,
                             stream_), "memcpy ctl");
   QWEN_TRY(run_steps(n));
+  return check_device_error();
+}
+
+// Batch-1 prefill on the tensor cores: the prompt's positions go through the
+// model kTcPrefillRows at a time as the rows of one batched step (each row
+// attends to positions 0 .. its own, the rows before it in the chunk included,
+// since their K/V rows are written before attention runs).  The logits of the
+// last position are then sampled exactly as the sequential loop's last prompt
+// step samples them (InferenceEngine.swift:29-52): same uniform, same record.
+int QwenEngine::prefill_chunked(const int32_t* ids, int32_t n) {
+  InferenceManager& s = state_;
+  cudaStream_t st = stream_;
+  QWEN_TRY(upload_prompt(ids, n, 0));
+  const int C = s.tc_rows;
+  int last_rows = 0;
+  for (int p0 = 0; p0 < n; p0 += C) {
+    const int rows = std::min(C, n - p0);
+    const bool final = p0 + rows == n;
+    QWEN_TRY(launch_prefill_rows(s, model_.embed, p0, rows, st));
+    const TcRows v{rows, s.tc_px, s.tc_pq, s.tc_row_len, 1, s.tc_row_seq, s.tc_pattn, s.tc_psplits,
+                   final ? s.tc_plogits : nullptr};
+    QWEN_TRY(enqueue_tc_model(model_, s, v, sm_count_, st));
+    last_rows = rows;
+  }
+  SeqCtl c;
+  std::memset(&c, 0, sizeof(c));
+  c.pos = n - 1;
+  c.n_prompt = n;
+  QWEN_CUDA(cudaMemcpyAsync(s.ctl, &c, sizeof(c), cudaMemcpyHostToDevice, st), "memcpy ctl");
+  k_step_begin<<<1, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
+                                  s.max_ctx, cfg_.seed, s.err, s.epoch);
+  QWEN_CUDA(cudaMemcpyAsync(s.logits, s.tc_plogits + (size_t)(last_rows - 1) * kVocab, kVocab * 2,
+                            cudaMemcpyDeviceToDevice, st), "memcpy logits");
+  if (launch_sample(s.logits, 1, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
+                    s.sampled, nullptr, s.err, st) != 0)
+    return launch_status("sample");
+  k_step_end<<<1, 1, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
+  QWEN_TRY(launch_status("chunked prefill"));
+  QWEN_CUDA(cudaStreamSynchronize(st), "sync");
   return check_device_error();
 }
 

@@ -151,7 +151,15 @@ class InferenceManager {
   uint8_t* act_h = nullptr;      // activation tiles, k = 1536
   uint8_t* act_i = nullptr;      // activation tiles, k = 8960
   float* tc_part = nullptr;      // fp32 split-K partials
-  int tc_nb = 0;                 // activation rows (batch padded to 16)
+  int tc_rows = 0;               // activation rows the buffers hold
+  int tc_nb = 0;                 // tc_rows padded to 16
+  // chunked prefill of a batch-1 engine (rows = consecutive positions)
+  __half *tc_px = nullptr, *tc_pq = nullptr;  // [tc_rows][1536]
+  __half* tc_plogits = nullptr;  // [tc_rows][151936]
+  uint32_t* tc_row_len = nullptr;  // [tc_rows] position + 1 of each row
+  int32_t* tc_row_seq = nullptr;   // [tc_rows] KV sequence of each row (0)
+  void* tc_pattn = nullptr;      // attention scratch for tc_rows rows
+  int tc_psplits = 0;
 
   // cudaMalloc + zero, freed with the state.
   int alloc_tracked(size_t bytes, void** out);
@@ -195,6 +203,7 @@ class QwenEngine {
   int enqueue_step_ops(cudaEvent_t* ev);
   int enqueue_step_fused(cudaEvent_t* ev);
   int enqueue_step_tc(cudaEvent_t* ev);
+  int prefill_chunked(const int32_t* prompt_ids, int32_t n_prompt);
   int enqueue_step(cudaEvent_t* ev);
   int build_step_weights();
   int upload_prompt(const int32_t* prompt_ids, int32_t n_prompt, int32_t start_pos);
@@ -229,12 +238,31 @@ int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st);
 int upload_rope_table(float** cs_dev, int* ctx, int max_ctx, cudaStream_t st);
 
 // Tensor-core batched step (batched.cu): weights, state, and the model part of
-// one step for every sequence of the batch (x -> logits).
+// one step over a set of activation rows (x -> logits).
 int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st);
 int tc_state_allocate(InferenceManager& s, int sm_count);
+// The rows one launch of the model processes: the batch's sequences (decode),
+// or consecutive positions of one sequence (chunked prefill).
+struct TcRows {
+  int rows;
+  __half* x;                 // [rows][1536] inputs (embeddings), residual stream
+  __half* q;                 // [rows][1536] scratch for the rotated queries
+  const uint32_t* seq_len;   // row r: position + 1 at seq_len[r * seq_len_stride]
+  int seq_len_stride;
+  const int32_t* row_seq;    // KV sequence of each row; nullptr: row = sequence
+  void* attn_scratch;
+  int attn_splits;
+  __half* logits;            // [rows][151936]; nullptr: no LM head
+};
+TcRows tc_decode_rows(InferenceManager& s);
 // marks (optional): an event is recorded after every launch, (*n_marks)++.
-int enqueue_tc_model(QwenModel& m, InferenceManager& s, int sm_count, cudaStream_t st,
-                     cudaEvent_t* marks = nullptr, int* n_marks = nullptr);
+int enqueue_tc_model(QwenModel& m, InferenceManager& s, const TcRows& v, int sm_count,
+                     cudaStream_t st, cudaEvent_t* marks = nullptr, int* n_marks = nullptr);
+// Rows for positions p0 .. p0+rows-1 of sequence 0: embeddings of its prompt
+// ids and lengths, on the device.
+int launch_prefill_rows(InferenceManager& s, const __half* embed, int p0, int rows,
+                        cudaStream_t st);
 int tc_kernels_per_step(int n_layers);
+constexpr int kTcPrefillRows = 128;  // positions per chunk of a batch-1 prefill
 
 }  // namespace qwen

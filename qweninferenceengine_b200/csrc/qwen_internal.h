@@ -23,6 +23,9 @@ struct AttnParams {
   long long out_seq_stride;
   uint8_t* act_out;         // if set: the output goes here instead, in the
   int act_nb;               //   tensor-core activation tile layout of act_nb rows
+  const int32_t* row_seq;   // if set: KV sequence of each row (rows = positions of
+                            //   one sequence in a chunked prefill); else row = sequence
+  int kv_n_seq;             // sequences in the caches (0: as many as rows)
   float* part_o;            // scratch: [n_seq][2][max_splits][6][128]
   float* part_ml;           // scratch: [n_seq][2][max_splits][6][2]
   uint32_t* counters;       // scratch: [n_seq][2], zero between launches

@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   uint8_t* sX = sA + S * kF16TcChunkBytes;         // [S][nb rows][128 B]
   const int nb = a.nb;
   const uint32_t xbytes = (uint32_t)nb * 128u;
+  const size_t act_chunk_bytes = (size_t)(a.act_stride_rows > 0 ? a.act_stride_rows : nb) * 128u;
   uint8_t* sR = sX + S * xbytes;                   // [S][4608] (Q4)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sR + (a.q4 ? S * kQ4TcChunkBytes : 0));
   uint64_t* wfull = bars;
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
       auto load_x = [&](int i) {
         const int s = i % S;
         mbar_arrive_expect_tx(xfull + s, xbytes);
-        bulk_g2s(sX + s * xbytes, a.act + (size_t)(c0 + i) * xbytes, xbytes, xfull + s);
+        bulk_g2s(sX + s * xbytes, a.act + (size_t)(c0 + i) * act_chunk_bytes, xbytes, xfull + s);
       };
       const int pre = cps < S ? cps : S;
       for (int i = 0; i < pre; ++i) load_w(i);  // weights do not depend on earlier kernels
@@ -433,7 +434,8 @@ int tc_gemm_stages(int nb, bool q4) {
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
   if (!a.w || !a.act || a.n_rows <= 0 || a.n_rows % kTcM || a.k <= 0 || a.k % kTcChunkK ||
       a.nb < 16 || a.nb > kTcMaxNb || a.nb % 16 || a.nb_valid < 1 || a.nb_valid > a.nb ||
-      a.splits < 1 || (a.k / kTcChunkK) % a.splits)
+      a.splits < 1 || (a.k / kTcChunkK) % a.splits ||
+      (a.act_stride_rows != 0 && (a.act_stride_rows < a.nb || a.act_stride_rows % 16)))
     return -1;
   const int outs = (a.part ? 1 : 0) + (a.out ? 1 : 0) + (a.swiglu_act ? 1 : 0);
   if (outs != 1 || (!a.part && a.splits != 1) ||

@@ -47,7 +47,8 @@ struct TcGemmArgs {
   const uint8_t* w = nullptr;  // Q4 or fp16 weight blob
   bool q4 = true;
   const uint8_t* act = nullptr;
-  int nb = 16;                 // activation rows (multiple of 16, <= 256)
+  int nb = 16;                 // activation rows of the MMA (multiple of 16, <= 256)
+  int act_stride_rows = 0;     // rows per chunk of the activation layout (0: nb)
   int nb_valid = 1;            // rows written out (<= nb)
   int n_rows = 0;              // multiple of 128
   int k = 0;                   // multiple of 64

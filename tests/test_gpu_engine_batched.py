@@ -78,3 +78,40 @@ def test_tc_batch_generate_greedy(cuda, oracle, small_model):
         diff = [j for j in range(gen) if outs[b][j] != ref[j]]
         if diff:
             assert margins[diff[0]] < LOGIT_ABS, f"seq {b} parts at step {diff[0]}"
+
+
+def test_tc_chunked_prefill_matches_sequential_oracle(cuda, oracle, small_model):
+    # batch 1 on the tensor-core path prefills 128 positions per batched step;
+    # 300 positions = chunks of 128, 128, 44.  The result must match the
+    # reference's one-token-at-a-time loop (InferenceEngine.swift:29-52).
+    n, gen = 300, 6
+    prompt = np.random.default_rng(23).integers(0, 151936, size=n).astype(np.int32)
+    cfg = QwenConfig(num_layers=2, max_context_window=512, temperature=0.0, kernels="tc",
+                     stop_on_eos=False)
+    eng = QwenEngine(small_model, cfg)
+    eng.prefill(prompt)
+    got = eng.logits()
+    om = OracleModel(oracle, small_model, 2, 512)
+    for i in range(n - 1):
+        om.forward(int(prompt[i]), i, want_logits=False)
+    ref = om.forward(int(prompt[-1]), n - 1)
+    check_logits(got, ref)
+    k, v = eng.kv(0, 1, n)
+    assert np.abs(k.astype(np.float32) - om.k_cache(1)[:n].astype(np.float32)).max() < 2e-2
+    assert np.abs(v.astype(np.float32) - om.v_cache(1)[:n].astype(np.float32)).max() < 2e-2
+    assert eng.position() == n
+    # greedy continuation from the chunked prefill
+    out = eng.decode(gen - 1)[0].tolist()
+    first = oracle.sample_greedy(ref)
+    ref_ids, margins, lg, cur = [first], [top2_margin(ref)], ref, first
+    for j in range(gen - 1):
+        lg = om.forward(cur, n + j)
+        cur = oracle.sample_greedy(lg)
+        ref_ids.append(cur)
+        margins.append(top2_margin(lg))
+    om.close()
+    eng.close()
+    assert len(out) == gen - 1
+    diff = [j for j in range(gen - 1) if out[j] != ref_ids[j + 1]]
+    if diff:
+        assert margins[diff[0] + 1] < LOGIT_ABS
