@@ -1,18 +1,19 @@
 // tc_gemm.cu -- batched Q4 / fp16 projections on tcgen05 tensor cores.
 //
-// CTA = 128 output rows x nb activation rows, K split over grid.y.  Six warps:
-//   warp 4      producer: one lane issues the 1-D bulk copies of each K chunk
+// CTA = 128 output rows x nb activation rows, K split over grid.y.  Ten warps:
+//   warp 8      producer: one lane issues the 1-D bulk copies of each K chunk
 //               into a 4-stage ring: the weight blob chunk (completion on
 //               wfull[s]) and the activation chunk (xfull[s]).  Launched as a
 //               programmatic dependent, the first stages' weights are fetched
 //               before griddepcontrol.wait, i.e. while the previous kernel of
 //               the stream still runs; activations only after it.
-//   warps 0..3  Q4: thread r dequantises row r of the chunk (16 nibble pairs
-//               -> fp16 via the 0x6400 exponent trick, (q - 8) exact, one
-//               rounding for the product with the block scale) into the
-//               128-byte-swizzled A tile; then the epilogue: row r of the
-//               accumulator read back from tensor memory
-//   warp 5      allocates tensor memory; one lane issues 4 MMAs
+//   warps 0..7  Q4: thread (h, r) dequantises block h of row r of the chunk
+//               (16 nibble pairs -> fp16 via the 0x6400 exponent trick, (q - 8)
+//               exact, one rounding for the product with the block scale) into
+//               the 128-byte-swizzled A tile; then the epilogue: warp w reads
+//               tensor-memory lanes 32(w%4).. (its rows) for half w/4 of the
+//               columns
+//   warp 9      allocates tensor memory; one lane issues 4 MMAs
 //               (M=128, N=nb, K=16) per chunk and commits each stage back to
 //               the producer through empty[s]
 // D[n][b] = sum_k A[n][k] X[b][k]: A (weights) and X (activations) are both
@@ -35,8 +36,10 @@ namespace qwen {
 namespace {
 
 constexpr int kTcMaxStages = 4;  // deeper rings measured slower (one CTA per SM instead of two)
-constexpr int kTcThreads = 192;
-constexpr int kDeqThreads = 128;
+constexpr int kTcThreads = 320;   // warps 0-7 dequant + epilogue, 8 producer, 9 MMA
+constexpr int kDeqThreads = 256;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 // ------------------------------------------------------------ tcgen05 PTX --
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     *abort = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tslot, ncols);
     tmem_relinquish();
   }
@@ -196,7 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   const uint32_t tmem = *tslot;
 
   if (threadIdx.x == 0) pdl_launch_dependents();
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer --
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // --------------------------------------------------------------- MMA --
     if (lane == 0) {
       const uint32_t idesc = f16_idesc(kTcM, nb);
@@ -252,54 +255,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     __syncwarp();
   } else {
     // ------------------------------------------------- dequant (Q4 only) --
-    const int r = threadIdx.x;  // row of the tile
+    // Thread (h, r): block h (32 k) of row r of the chunk.
+    const int r = threadIdx.x & (kTcM - 1), h = threadIdx.x >> 7;
     if (a.q4) {
       for (int i = 0; i < cps; ++i) {
         const int s = i % S;
         if (!tc_wait(wfull + s, (i / S) & 1, abort, a.err)) break;
         const uint8_t* raw = sR + s * kQ4TcChunkBytes;
-        const uint4 p0 = *reinterpret_cast<const uint4*>(raw + r * 16);
-        const uint4 p1 = *reinterpret_cast<const uint4*>(raw + 2048 + r * 16);
-        const __half2 sc = *reinterpret_cast<const __half2*>(raw + 4096 + r * 4);
-        const __half2 s0 = __low2half2(sc), s1 = __high2half2(sc);
+        const uint4 pk = *reinterpret_cast<const uint4*>(raw + h * 2048 + r * 16);
+        const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(raw + 4096 + r * 4 + h * 2));
         uint8_t* arow = sA + s * kF16TcChunkBytes + r * 128;
-        const uint32_t sw = (uint32_t)(r & 7);
-        *reinterpret_cast<uint4*>(arow + ((0u ^ sw) << 4)) = dequant8(p0.x, s0);
-        *reinterpret_cast<uint4*>(arow + ((1u ^ sw) << 4)) = dequant8(p0.y, s0);
-        *reinterpret_cast<uint4*>(arow + ((2u ^ sw) << 4)) = dequant8(p0.z, s0);
-        *reinterpret_cast<uint4*>(arow + ((3u ^ sw) << 4)) = dequant8(p0.w, s0);
-        *reinterpret_cast<uint4*>(arow + ((4u ^ sw) << 4)) = dequant8(p1.x, s1);
-        *reinterpret_cast<uint4*>(arow + ((5u ^ sw) << 4)) = dequant8(p1.y, s1);
-        *reinterpret_cast<uint4*>(arow + ((6u ^ sw) << 4)) = dequant8(p1.z, s1);
-        *reinterpret_cast<uint4*>(arow + ((7u ^ sw) << 4)) = dequant8(p1.w, s1);
+        const uint32_t sw = (uint32_t)(r & 7), j0 = 4u * (uint32_t)h;
+        *reinterpret_cast<uint4*>(arow + (((j0 + 0u) ^ sw) << 4)) = dequant8(pk.x, s2);
+        *reinterpret_cast<uint4*>(arow + (((j0 + 1u) ^ sw) << 4)) = dequant8(pk.y, s2);
+        *reinterpret_cast<uint4*>(arow + (((j0 + 2u) ^ sw) << 4)) = dequant8(pk.z, s2);
+        *reinterpret_cast<uint4*>(arow + (((j0 + 3u) ^ sw) << 4)) = dequant8(pk.w, s2);
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
         mbar_arrive(deq + s);
       }
     }
     // ---------------------------------------------------------- epilogue --
+    // Warp w reads tensor-memory lanes 32(w%4) .. +31 (rows r) and the column
+    // groups of half w/4: groups of 16 columns [g0, g1).
     pdl_wait();  // outputs are written only after the previous kernel completed
     const bool landed = tc_wait(accum, 0, abort, a.err, false);
     tc_fence_after();
     // tcgen05.ld is warp-collective: the decision is the warp's, not the lane's.
     const bool go = __all_sync(0xffffffffu, landed && !*abort);
+    const int groups = nb / 16, gsplit = (groups + 1) / 2;
+    const int g0 = h == 0 ? 0 : gsplit, g1 = h == 0 ? gsplit : groups;
+    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     if (a.swiglu_act) {
-      // Up rows (tensor-memory lanes 64..127, warps 2-3) -> fp16 in shared
-      // memory [b][64] (the A ring is idle once the accumulator is complete),
-      // then warps 0-1 combine them with their gate rows.
+      // Up rows (lanes 64..127) -> fp16 in shared memory [b][64] (the A ring
+      // is idle once the accumulator is complete), then the gate-row warps
+      // combine them.
       __half* ub = reinterpret_cast<__half*>(sA);
-      const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-      if (go && warp >= 2)
-        for (int c = 0; c < nb; c += 16) {
+      if (go && r >= 64)
+        for (int c = 16 * g0; c < 16 * g1; c += 16) {
           float v[16];
           tmem_ld16(lane_addr + (uint32_t)c, v);
 #pragma unroll
           for (int j = 0; j < 16; ++j) ub[(c + j) * 64 + (r - 64)] = f2h(v[j]);
         }
-      asm volatile("bar.sync 2, 128;" ::: "memory");  // the four epilogue warps
-      if (go && warp < 2) {
+      asm volatile("bar.sync 2, 256;" ::: "memory");  // the eight epilogue warps
+      if (go && r < 64) {
         const int hrow = tile * 64 + r;  // k index of the down projection's input
         const int cc = hrow >> 6, jj = (hrow >> 3) & 7;
-        for (int c = 0; c < nb; c += 16) {
+        for (int c = 16 * g0; c < 16 * g1; c += 16) {
           float v[16];
           tmem_ld16(lane_addr + (uint32_t)c, v);
 #pragma unroll
@@ -316,8 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
       }
     } else if (go) {
       const size_t row = (size_t)tile * kTcM + r;
-      const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-      for (int c = 0; c < nb; c += 16) {
+      for (int c = 16 * g0; c < 16 * g1; c += 16) {
         float v[16];
         tmem_ld16(lane_addr + (uint32_t)c, v);
 #pragma unroll
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) tmem_dealloc(tmem, ncols);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, ncols);
 }
 
 // ----------------------------------------------------------- repacking ---

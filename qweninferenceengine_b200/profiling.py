@@ -6,6 +6,15 @@
         regex:k_decode_fused -s 3 -c 1` captures, small enough to capture in
         seconds while its 1.2 GB+ of weights still exceed the L2.
 
+    python -m qweninferenceengine_b200.profiling gemm [--rows 17920] [--k 1536] [--batch 64]
+        One batched Q4 projection on the tensor cores (qwen_gemm_q4_0_batched,
+        eager launches: repack, pack, k_tc_gemm, split sum), repeated --reps
+        times -- the workload for `ncu -k regex:k_tc_gemm` captures.
+
+    python -m qweninferenceengine_b200.profiling attention [--batch 64] [--ctx 2000]
+        Batched decode attention over random caches (qwen_attention_decode_batched),
+        repeated --reps times -- the workload for `ncu -k regex:k_attention_decode`.
+
     python -m qweninferenceengine_b200.profiling trace [--layers 28] [--ctx 512]
         Per-phase critical-path summary of one fused decode step from the
         kernel's %globaltimer stamps (qwen_engine_trace): for each traced layer,
@@ -32,6 +41,35 @@ def run_case(layers: int, steps: int) -> None:
     eng.prefill(np.arange(1, 5, dtype=np.int32))
     eng.decode(steps, record=False)
     eng.close()
+
+
+def run_gemm(rows: int, k: int, batch: int, reps: int) -> None:
+    import torch
+
+    from . import ops
+
+    g = torch.Generator(device="cpu").manual_seed(0)
+    packed = torch.randint(0, 256, (rows * k // 2,), dtype=torch.uint8, generator=g).cuda()
+    scales = (torch.rand(rows * k // 32, generator=g) * 0.003).half().cuda()
+    x = torch.randn(batch, k, generator=g).half().cuda()
+    for _ in range(reps):
+        ops.gemm_q4_0_batched(packed, scales, x)
+    torch.cuda.synchronize()
+
+
+def run_attention(batch: int, ctx: int, reps: int) -> None:
+    import torch
+
+    from . import ops
+
+    g = torch.Generator(device="cpu").manual_seed(0)
+    q = torch.randn(batch, 1536, generator=g).half().cuda()
+    kc = torch.randn(batch, ctx, 256, generator=g).half().cuda()
+    vc = torch.randn(batch, ctx, 256, generator=g).half().cuda()
+    sl = torch.full((batch,), ctx, dtype=torch.int32).cuda()
+    for _ in range(reps):
+        ops.attention_decode_batched(q, kc, vc, sl, ctx)
+    torch.cuda.synchronize()
 
 
 def run_trace(layers: int, ctx: int, show_layers) -> dict:
@@ -88,12 +126,29 @@ def main() -> None:
     c = sub.add_parser("case")
     c.add_argument("--layers", type=int, default=4)
     c.add_argument("--steps", type=int, default=2)
+    gm = sub.add_parser("gemm")
+    gm.add_argument("--rows", type=int, default=17920)
+    gm.add_argument("--k", type=int, default=1536)
+    gm.add_argument("--batch", type=int, default=64)
+    gm.add_argument("--reps", type=int, default=3)
+    at = sub.add_parser("attention")
+    at.add_argument("--batch", type=int, default=64)
+    at.add_argument("--ctx", type=int, default=2000)
+    at.add_argument("--reps", type=int, default=3)
     t = sub.add_parser("trace")
     t.add_argument("--layers", type=int, default=28)
     t.add_argument("--ctx", type=int, default=512)
     a = ap.parse_args()
     if a.cmd == "case":
         run_case(a.layers, a.steps)
+        print("ok")
+        return
+    if a.cmd == "gemm":
+        run_gemm(a.rows, a.k, a.batch, a.reps)
+        print("ok")
+        return
+    if a.cmd == "attention":
+        run_attention(a.batch, a.ctx, a.reps)
         print("ok")
         return
     r = run_trace(a.layers, a.ctx, [1, a.layers // 2, a.layers - 1])
