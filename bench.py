@@ -35,6 +35,18 @@ EMBED_ROW = 1536 * 2
 METRIC = "decode tokens/s (bs1 ctx512 per B200)"
 
 
+# DRAM traffic of one launch of the fused step kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum from one ncu capture of the 28-layer model at context 6:
+# 1.006 x the algorithmic bytes there).  Weights and LM head are read once per
+# launch, so the traffic at another context adds the KV bytes of the extra
+# positions.
+FUSED_TRAFFIC_CTX6 = 1_211_804_160
+
+
+def fused_traffic(ctx: float) -> float:
+    return FUSED_TRAFFIC_CTX6 + KV_BYTES_PER_POS * (ctx - 6)
+
+
 def bytes_per_token(ctx: float) -> float:
     return LAYERS * LAYER_BYTES + LM_BYTES + KV_BYTES_PER_POS * ctx + EMBED_ROW
 
@@ -305,7 +317,10 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "kernel": "model kernels of the step (all layers + LM head)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                         "traffic": None, "algorithmic_bytes": algo,
+                         "traffic": fused_traffic(ctx_prof) if args.kernels == "fused" else None,
+                         "traffic_source": "ncu dram bytes of one 28-layer launch at context 6, "
+                                           "plus the KV bytes of the extra positions",
+                         "algorithmic_bytes": algo,
                          "ms_model": ms_model, "ms_step_unfused_launch": ms_step_prof},
             "e2e": {"value": world * n_e2e / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": 4 + 4,
