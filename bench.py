@@ -118,6 +118,37 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def replica_barrier(world: int) -> None:
+    """Device work of this rank finished, then a host barrier over the replicas
+    (gloo; replicas exchange no data)."""
+    import torch
+
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def replica_max(x: float, world: int) -> float:
+    """The maximum of x over the replicas (the job's time is the slowest rank's)."""
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def replica_tokens_per_s(world: int, tokens_per_rank: int, ms_max: float) -> float:
+    """Whole-job throughput of weak-scaled replicas: every rank decodes
+    tokens_per_rank tokens; the job takes the slowest rank's time."""
+    return world * tokens_per_rank / (ms_max * 1e-3)
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -213,7 +244,8 @@ def run_batched(args, rank, world, local, barrier, max_over_ranks):
     peak, peak_kind = peak_gbs()
     achieved = step_bytes / (ms_model * 1e-3) / 1e9
     return {
-        "metric": "decode tokens/s (bs64 per GPU, replicas)", "value": world * BATCH * steps / (ms * 1e-3),
+        "metric": "decode tokens/s (bs64 per GPU, replicas)",
+        "value": replica_tokens_per_s(world, BATCH * steps, ms),
         "unit": "tokens/s", "n_gpus": world, "steps": steps, "ms_per_step": ms / steps,
         "config": {"workload": "Qwen2.5-1.5B Q4 block-32 decode, 64 sequences per GPU, 1024-token "
                                "prompts, top-p 0.9 T 0.7 (28 layers)",
@@ -248,20 +280,10 @@ def run_ours(args):
     stream = torch.cuda.ExternalStream(eng.stream())
 
     def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
+        replica_barrier(world)
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        import torch.distributed as dist
-
-        t = torch.tensor([x], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return replica_max(x, world)
 
     # ---- device-timed decode: K graph replays, inputs resident in HBM.
     pos0 = eng.position()
@@ -303,7 +325,7 @@ def run_ours(args):
     batched = None if args.no_batched else run_batched(args, rank, world, local, barrier,
                                                        max_over_ranks)
     if rank == 0:
-        tok_s = world * args.steps / (ms * 1e-3)
+        tok_s = replica_tokens_per_s(world, args.steps, ms)
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
