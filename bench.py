@@ -164,6 +164,9 @@ def cpu_baseline(n_tokens: int = 3, warmup: int = 1):
     from oracle_lib import Oracle, OracleModel
 
     o = Oracle()
+    # every host thread (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    threads = o.set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
+                            else os.cpu_count())
     m = OracleModel(o, None, LAYERS, CTX + 8, random_seed=7)
     rng = np.random.default_rng(7)
     for layer in range(LAYERS):
@@ -178,7 +181,7 @@ def cpu_baseline(n_tokens: int = 3, warmup: int = 1):
         tok = int(np.argmax(lg[:151666]))
     dt = time.perf_counter() - t0
     m.close()
-    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{n_tokens} decode tokens (after {warmup} warm-up) of the 28-layer model "
                       f"at ctx {CTX}, random-init weights and KV cache, oracle/liboracle.so"}
 

@@ -13,6 +13,8 @@
 //     available off Apple hardware.
 #include "oracle.h"
 
+#include <omp.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -637,6 +639,11 @@ void oracle_forward(const oracle_model* m, oracle_state* s, int token, int posit
     oracle_gemv_fp16(m->embed.data(), s->residual.data(), logits, kVocab, kHidden,
                      kGemvThreads);                                                   // :259-264
   }
+}
+
+int oracle_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
 }
 
 }  // extern "C"

@@ -74,6 +74,10 @@ float oracle_sampler_exp(float x);
 /* 24-bit uniform for (seed, sequence, step) -- SplitMix64 (Steele et al. 2014). */
 uint32_t oracle_uniform24(uint64_t seed, uint64_t sequence, uint64_t step);
 
+/* OpenMP threads for the row/head loops (n < 1: leave the runtime's default);
+ * returns the thread count now in effect. */
+int oracle_set_threads(int n);
+
 /* ---- whole model -------------------------------------------------------- */
 typedef struct oracle_model oracle_model;
 typedef struct oracle_state oracle_state;

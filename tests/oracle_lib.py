@@ -128,6 +128,10 @@ class MetalRef(_Kernels):
 class Oracle(_Kernels):
     prefix = "oracle_"
 
+    def set_threads(self, n: int) -> int:
+        """OpenMP threads of the oracle's loops (returns the count in effect)."""
+        return self.lib.oracle_set_threads(n)
+
     def __init__(self):
         ensure_oracle_built()
         super().__init__(ORACLE_SO)
@@ -143,6 +147,8 @@ class Oracle(_Kernels):
         L.oracle_sampler_exp.restype = ctypes.c_float
         L.oracle_uniform24.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]
         L.oracle_uniform24.restype = ctypes.c_uint32
+        L.oracle_set_threads.argtypes = [ctypes.c_int]
+        L.oracle_set_threads.restype = ctypes.c_int
         L.oracle_model_load.argtypes = [ctypes.c_char_p, ctypes.c_int]
         L.oracle_model_load.restype = ctypes.c_void_p
         L.oracle_model_free.argtypes = [ctypes.c_void_p]
