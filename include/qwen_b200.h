@@ -263,7 +263,8 @@ int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n)
  * consumer end; then 7 stamps inside the attention unit of layer n_layers/2
  * (unit start, q/k/v in, warp 0's positions done, the unit's warps merged,
  * partials written, all splits' partials in, output slice written; zero on
- * CTAs without a unit); stride 3 + 10*n_layers + 2 + 7.
+ * CTAs without a unit), then warp 0's nanoseconds spent waiting for weight
+ * slots in that layer's gate/up and down phases; stride 3 + 10*n_layers + 2 + 9.
  * qwen_engine_get_trace copies the last step's stamps ([grid][stride]) when
  * n >= *needed, and always reports *needed. */
 int qwen_engine_trace(qwen_engine* e, int32_t enable);

@@ -695,12 +695,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     };
     // K-split processing of items [cur, e): warp w takes block pairs w, w+8, ...
     // of every chunk; the tile's 16 sums meet in shared memory at its last chunk.
+    // Trace: warp 0's time waiting for weight slots in the gate/up ([0]) and
+    // down ([1]) phases of the middle layer.
+    unsigned long long* wtrace =
+        trace ? trace + 3 + p.n_layers * kTraceStampsPerLayer + 2 + 7 : nullptr;
+    int wsel = -1;
+    auto timed_wait = [&](int i, int site) {
+      if (!wtrace || ct != 0 || wsel < 0) return item_wait(i, full, misc, p.err, site);
+      const uint64_t t0 = globaltimer();
+      const bool ok = item_wait(i, full, misc, p.err, site);
+      wtrace[wsel] += globaltimer() - t0;
+      return ok;
+    };
     auto ksplit = [&](int e, auto&& epilogue) {
       float acc_g = 0.f, acc_g8 = 0.f;
       for (int i = cur; i < e; ++i) {
         const ItemFields it = unpack_item(items[i]);
         const int slot = i % kNS;
-        if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100))
+        if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
           q4_chunk(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
                    acc_g8);
         __syncwarp();
@@ -865,13 +877,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         const int e = phase_end(ph + kPhGU);
         rmsnorm_out(xloc, gamma_post, red2, xf, nullptr, ct);
         lstamp(layer, kTsGUReady);
+        wsel = layer == p.n_layers / 2 ? 0 : -1;
+        if (wtrace && ct == 0 && wsel >= 0) wtrace[0] = 0;
         const uint16_t tg = (uint16_t)tagof(layer);
         for (int i = cur; i < e; ++i) {
           const ItemFields it = unpack_item(items[i]);
           if ((it.seq & (kConsumerWarps - 1)) != warp) continue;
           const int slot = i % kNS;
           float acc_g = 0.f, acc_g8 = 0.f;
-          if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100))
+          if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
             q4_chunk(ring + slot * kSlotBytes, it.k0, 0, it.nk, 1, xf, lane, acc_g, acc_g8);
           __syncwarp();
           if (lane == 0) {
@@ -905,6 +919,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
                         });
           cbar();
           lstamp(layer, kTsDownReady);
+          wsel = layer == p.n_layers / 2 ? 1 : -1;
+          if (wtrace && ct == 0 && wsel >= 0) wtrace[1] = 0;
           const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
           ksplit(e, [&](int tile, int r, float sum) {
             const int row = 16 * tile + r;
@@ -915,6 +931,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       }
       cbar();
       lstamp(layer, kTsDownDone);
+      wsel = -1;
     }
     // ---- final RMSNorm + LM head (each warp owns whole 16-row tiles)
     if (ct == 0) misc->cphase = lm_phase * 1000 + cur;

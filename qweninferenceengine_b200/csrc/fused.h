@@ -59,8 +59,9 @@ enum TraceStamp : int {
 // Per CTA: 3 head stamps, 10 per layer, 2 for the LM head, then 7 inside the
 // attention unit of the middle layer (start, q/k/v in, warp 0's positions
 // done, the unit's warps merged, partials written, partials of all splits in,
-// output slice written) on the CTAs that run one.
-constexpr int kAttnTraceStamps = 7;
+// output slice written) on the CTAs that run one, then warp 0's nanoseconds
+// waiting for weight slots in the middle layer's gate/up and down phases.
+constexpr int kAttnTraceStamps = 9;
 inline int trace_stride_for(int n_layers) {
   return 3 + n_layers * kTraceStampsPerLayer + 2 + kAttnTraceStamps;
 }

@@ -32,6 +32,7 @@ STAMPS = ["start", "x_ready", "qkv_done", "attn_done", "o_ready", "o_done", "gu_
           "gu_done", "h_ready", "down_done"]
 ATTN_STAMPS = ["unit_start", "qkv_in", "warp0_done", "warps_merged", "partials_out",
                "splits_in", "output_out"]
+EXTRA_WORDS = 2  # warp 0's slot-wait ns in the middle layer's gate/up and down phases
 
 
 def run_case(layers: int, steps: int) -> None:
@@ -86,7 +87,7 @@ def run_trace(layers: int, ctx: int, show_layers) -> dict:
     eng.trace(False)
     eng.close()
     k = len(STAMPS)
-    grid = tr.size // (3 + k * layers + 2 + len(ATTN_STAMPS))
+    grid = tr.size // (3 + k * layers + 2 + len(ATTN_STAMPS) + EXTRA_WORDS)
     tr = tr.reshape(grid, -1)
     t0 = tr[:, 2].min()
     rel = np.where(tr > 0, (tr - t0) / 1000.0, np.nan)
@@ -97,7 +98,12 @@ def run_trace(layers: int, ctx: int, show_layers) -> dict:
     periods = np.diff(np.nanmedian(ph[:, :, 0], axis=0))
     out["layer_period_us"] = float(np.median(periods)) if periods.size else None
     mid = layers // 2
-    att = rel[:, 3 + k * layers + 2:]
+    waits = tr[:, 3 + k * layers + 2 + len(ATTN_STAMPS):].astype(np.float64) / 1000.0
+    out["slot_wait_us"] = {"gate_up": (float(waits[:, 0].min()), float(np.median(waits[:, 0])),
+                                       float(waits[:, 0].max())),
+                           "down": (float(waits[:, 1].min()), float(np.median(waits[:, 1])),
+                                    float(waits[:, 1].max()))}
+    att = rel[:, 3 + k * layers + 2:3 + k * layers + 2 + len(ATTN_STAMPS)]
     have = ~np.isnan(att[:, 0])
     if have.any():
         base = np.nanmedian(ph[:, mid, 0])
@@ -155,6 +161,8 @@ def main() -> None:
     print(f"step {r['ms_step']:.3f} ms, model kernels {r['ms_model']:.3f} ms, grid {r['grid']}, "
           f"median layer period {r['layer_period_us']:.2f} us, LM head from {r['lm_start_us']:.1f} "
           f"to {r['end_us']:.1f} us")
+    print("warp 0 waiting for weight slots, middle layer (us, min / med / max over CTAs): " +
+          ", ".join(f"{k} {lo:.2f} / {med:.2f} / {hi:.2f}" for k, (lo, med, hi) in r["slot_wait_us"].items()))
     if "attention_unit" in r:
         print(f"attention units of layer {a.layers // 2} (us from the layer's median start; min / med / max)")
         for name, (lo, med, hi) in r["attention_unit"].items():
