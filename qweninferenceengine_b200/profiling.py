@@ -15,6 +15,11 @@
         Batched decode attention over random caches (qwen_attention_decode_batched),
         repeated --reps times -- the workload for `ncu -k regex:k_attention_decode`.
 
+    python -m qweninferenceengine_b200.profiling tcstep [--batch 64] [--ctx 1024]
+        The batched tensor-core step: prefill, then --reps eagerly launched steps
+        with an event after every kernel (qwen_engine_profile_step); prints the
+        per-kernel device times and is the workload for ncu launch lists of it.
+
     python -m qweninferenceengine_b200.profiling trace [--layers 28] [--ctx 512]
         Per-phase critical-path summary of one fused decode step from the
         kernel's %globaltimer stamps (qwen_engine_trace): for each traced layer,
@@ -71,6 +76,22 @@ def run_attention(batch: int, ctx: int, reps: int) -> None:
     for _ in range(reps):
         ops.attention_decode_batched(q, kc, vc, sl, ctx)
     torch.cuda.synchronize()
+
+
+def run_tcstep(batch: int, ctx: int, reps: int, layers: int = 28) -> list:
+    cfg = QwenConfig(num_layers=layers, max_context_window=max(2048, ctx + 64), temperature=0.7,
+                     top_p=0.9, batch=batch, kernels="tc", stop_on_eos=False)
+    eng = QwenEngine(config=cfg, random_seed=7)
+    prompts = np.stack([np.random.default_rng(s).integers(0, 151936, size=ctx)
+                        for s in range(batch)]).astype(np.int32)
+    eng.prefill(prompts)
+    prof = []
+    torch.cuda.nvtx.range_push("tcstep")  # ncu --nvtx --nvtx-include tcstep/ selects these launches
+    for _ in range(reps):
+        prof = eng.profile_step()
+    torch.cuda.nvtx.range_pop()
+    eng.close()
+    return prof
 
 
 def run_trace(layers: int, ctx: int, show_layers) -> dict:
@@ -141,6 +162,11 @@ def main() -> None:
     at.add_argument("--batch", type=int, default=64)
     at.add_argument("--ctx", type=int, default=2000)
     at.add_argument("--reps", type=int, default=3)
+    ts = sub.add_parser("tcstep")
+    ts.add_argument("--batch", type=int, default=64)
+    ts.add_argument("--ctx", type=int, default=1024)
+    ts.add_argument("--reps", type=int, default=2)
+    ts.add_argument("--layers", type=int, default=28)
     t = sub.add_parser("trace")
     t.add_argument("--layers", type=int, default=28)
     t.add_argument("--ctx", type=int, default=512)
@@ -152,6 +178,15 @@ def main() -> None:
     if a.cmd == "gemm":
         run_gemm(a.rows, a.k, a.batch, a.reps)
         print("ok")
+        return
+    if a.cmd == "tcstep":
+        prof = run_tcstep(a.batch, a.ctx, a.reps, a.layers)
+        agg = {}
+        for name, ms in prof:
+            n, t = agg.get(name, (0, 0.0))
+            agg[name] = (n + 1, t + ms)
+        for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+            print(f"{name:16s} x{n:3d} {t:8.3f} ms {1000 * t / n:8.1f} us each")
         return
     if a.cmd == "attention":
         run_attention(a.batch, a.ctx, a.reps)
