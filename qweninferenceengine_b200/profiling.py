@@ -79,6 +79,7 @@ def run_attention(batch: int, ctx: int, reps: int) -> None:
 
 
 def run_tcstep(batch: int, ctx: int, reps: int, layers: int = 28) -> list:
+    import torch
     cfg = QwenConfig(num_layers=layers, max_context_window=max(2048, ctx + 64), temperature=0.7,
                      top_p=0.9, batch=batch, kernels="tc", stop_on_eos=False)
     eng = QwenEngine(config=cfg, random_seed=7)
