@@ -1,21 +1,35 @@
 // tc_gemm.cu -- batched Q4 / fp16 projections on tcgen05 tensor cores.
 //
 // CTA = 128 output rows x nb activation rows, K split over grid.y.  Ten warps:
-//   warp 8      producer: one lane issues the 1-D bulk copies of each K chunk
-//               into a 4-stage ring: the weight blob chunk (completion on
-//               wfull[s]) and the activation chunk (xfull[s]).  Launched as a
-//               programmatic dependent, the first stages' weights are fetched
-//               before griddepcontrol.wait, i.e. while the previous kernel of
-//               the stream still runs; activations only after it.
-//   warps 0..7  Q4: thread (h, r) dequantises block h of row r of the chunk
-//               (16 nibble pairs -> fp16 via the 0x6400 exponent trick, (q - 8)
+//   warp 8      producer: one lane issues the 1-D bulk copies.  Q4 weights go
+//               to a deep ring of raw 4608-byte chunks (up to 32; usually
+//               every chunk of the CTA), all issued before griddepcontrol.wait
+//               -- weights do not depend on the previous kernel of the stream,
+//               so they stream in while it still runs -- and refilled as soon
+//               as a chunk has been read by the dequantising warps.
+//               Activations go to their own ring (up to 12 stages) and fp16
+//               weights to the A ring; the MMAs free both.
+//   warps 0..7  Q4: two groups of four warps take alternate chunks; thread r
+//               of a group dequantises both 32-weight blocks of row r (16
+//               nibble pairs each -> fp16 via the 0x6400 exponent trick, (q - 8)
 //               exact, one rounding for the product with the block scale) into
-//               the 128-byte-swizzled A tile; then the epilogue: warp w reads
+//               the 128-byte-swizzled A tile.  Then the epilogue: warp w reads
 //               tensor-memory lanes 32(w%4).. (its rows) for half w/4 of the
 //               columns
-//   warp 9      allocates tensor memory; one lane issues 4 MMAs
-//               (M=128, N=nb, K=16) per chunk and commits each stage back to
-//               the producer through empty[s]
+//   warps 9-10  warp 9 allocates tensor memory; each MMA warp takes
+//               alternate units (one or two 64-k chunks), one lane issuing 4
+//               MMAs (M=128, N=nb, K=16) per chunk into the warp's own fp32
+//               accumulator and committing the A stage (aempty) and the
+//               activation stage (xempty) back.  Two issuing warps because a
+//               lone MMA warp's wait -> issue -> commit loop, not the tensor
+//               pipe, set the rate at N=64; the epilogue adds the two
+//               accumulators in a fixed order.  Where two accumulators and the
+//               A stages do not fit in tensor memory (nb > 128), warp 10 idles.
+// Three rings because each refill sits on its own loop of latencies: a raw
+// weight chunk is refilled one HBM latency after its dequantisation, an
+// activation chunk one L2 latency (~1.5 us with every CTA reading the same
+// chunk) after its MMAs.  With one ring for everything, that loop bounded the
+// kernel at ring depth / 1.9 us chunks.
 // D[n][b] = sum_k A[n][k] X[b][k]: A (weights) and X (activations) are both
 // K-major, so one tcgen05.mma.kind::f16 per 16 k computes W . X^T.
 //
@@ -35,11 +49,17 @@
 namespace qwen {
 namespace {
 
-constexpr int kTcMaxStages = 4;  // deeper rings measured slower (one CTA per SM instead of two)
-constexpr int kTcThreads = 320;   // warps 0-7 dequant + epilogue, 8 producer, 9 MMA
-constexpr int kDeqThreads = 256;
+constexpr int kTcMaxStages = 4;      // A stages in tensor memory (Q4)
+constexpr int kTcMaxF16Stages = 4;   // A ring (fp16 weights straight from HBM)
+constexpr int kTcMaxXStages = 12;    // activation ring
+constexpr int kTcMaxRawStages = 32;  // Q4 raw-weight ring
+constexpr size_t kTcSmemBudget = 227 * 1024;
+constexpr int kTcThreads = 352;      // warps 0-7 dequant + epilogue, 8 producer, 9-10 MMA
+constexpr int kDeqGroupWarps = 4;    // one dequantising group: 128 threads, one per tile row
+constexpr int kDeqThreads = 256;     // both groups: warps 0-7
+constexpr uint32_t kTmemAStageCols = kTcChunkK / 2;  // a Q4 A stage: 64 fp16 per lane
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;          // allocates tensor memory; MMA warps are 9 and 10
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 // ------------------------------------------------------------ tcgen05 PTX --
@@ -71,6 +91,32 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, u
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// Same with A (M x K, K-major) read from tensor memory at a_tmem: lane m holds
+// row m, two fp16 of k per 32-bit column.
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 consecutive 32-bit columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+      "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]),
+      "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 // Arrive on `bar` once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -139,53 +185,72 @@ __device__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// 8 nibble-permuted weights -> 4 half2 (k0,k1) (k2,k3) (k4,k5) (k6,k7),
-// each (q - 8) * scale rounded once.
-__device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2) {
+// 8 nibble-permuted weights -> 4 half2 (k0,k1) (k2,k3) (k4,k5) (k6,k7) at
+// o[0..3], each (q - 8) * scale rounded once.
+__device__ __forceinline__ void dequant8(uint32_t w, __half2 s2, uint32_t* o) {
   const __half2 off = __floats2half2_rn(1032.0f, 1032.0f);
-  uint32_t o[4];
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
     const uint32_t v = ((w >> (4 * s)) & 0x000F000Fu) | 0x64006400u;  // 1024 + q
     o[s] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v), off), s2));
   }
-  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
   extern __shared__ uint8_t tc_smem[];
-  const int S = a.stages;  // ring depth (host-sized to the shared memory budget)
+  const bool q4 = a.q4;
+  const int U = a.unit;                // 64-k chunks per pipeline unit (Q4: 1 or 2; fp16: 1)
+  const int S = a.stages;              // A stages: tensor memory (Q4) or shared memory (fp16)
+  const int XS = a.xstages;            // activation ring depth
+  const int RS = q4 ? a.raw_stages : 0;  // raw Q4 ring depth
+  const int NW = q4 ? RS : S;          // weight-landing barriers (raw ring, or A ring for fp16)
+  const int SA = q4 ? 0 : S;           // shared-memory A stages
   const uint32_t pad = (1024u - (smem_u32(tc_smem) & 1023u)) & 1023u;
-  uint8_t* sA = tc_smem + pad;                             // [S][128 rows][128 B]
-  uint8_t* sX = sA + S * kF16TcChunkBytes;         // [S][nb rows][128 B]
+  uint8_t* sA = tc_smem + pad;                             // [SA][128 rows][128 B] (fp16)
+  uint8_t* sX = sA + SA * kF16TcChunkBytes;                // [XS][nb rows][128 B]
   const int nb = a.nb;
   const uint32_t xbytes = (uint32_t)nb * 128u;
   const size_t act_chunk_bytes = (size_t)(a.act_stride_rows > 0 ? a.act_stride_rows : nb) * 128u;
-  uint8_t* sR = sX + S * xbytes;                   // [S][4608] (Q4)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + (a.q4 ? S * kQ4TcChunkBytes : 0));
-  uint64_t* wfull = bars;
-  uint64_t* xfull = bars + S;
-  uint64_t* deq = bars + 2 * S;
-  uint64_t* empty = bars + 3 * S;
-  uint64_t* accum = bars + 4 * S;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4 * S + 1);
+  const uint32_t xunit = (uint32_t)U * xbytes;             // activation bytes per unit
+  const uint32_t runit = (uint32_t)U * kQ4TcChunkBytes;    // raw Q4 bytes per unit
+  uint8_t* sR = sX + XS * xunit;                           // [RS][U][4608] (Q4)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + RS * runit);
+  uint64_t* wfull = bars;          // [NW] weight chunk landed
+  uint64_t* rempty = wfull + NW;   // [RS] raw chunk read by its dequantising group
+  uint64_t* xfull = rempty + RS;   // [XS] activation chunk landed
+  uint64_t* xempty = xfull + XS;   // [XS] MMAs reading the activation chunk completed
+  uint64_t* deq = xempty + XS;     // [S]  Q4: A stage written and its activations landed
+  uint64_t* aempty = deq + S;      // [S]  MMAs reading the A stage completed
+  uint64_t* accum = aempty + S;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accum + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_chunks = a.k / kTcChunkK;
   const int cps = n_chunks / a.splits;
+  const int nu = cps / U;  // pipeline units of this CTA
   const int c0 = blockIdx.y * cps;
   const int tile = blockIdx.x;
-  const uint32_t ncols = nb <= 32 ? 32u : nb <= 64 ? 64u : nb <= 128 ? 128u : 256u;
+  // Tensor memory: one fp32 accumulator per MMA warp, acc_cols columns each,
+  // then (Q4) the A stages, 32 columns per chunk (64 fp16 of k per lane).
+  const int MW = a.mma_warps;
+  const uint32_t acc_cols = nb <= 32 ? 32u : nb <= 64 ? 64u : nb <= 128 ? 128u : 256u;
+  const uint32_t a_base = acc_cols * (uint32_t)MW;
+  const uint32_t need = a_base + (q4 ? (uint32_t)(S * U) * kTmemAStageCols : 0u);
+  const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(wfull + s, 1);
+    for (int s = 0; s < NW; ++s) mbar_init(wfull + s, 1);
+    for (int s = 0; s < RS; ++s) mbar_init(rempty + s, kDeqGroupWarps);
+    for (int s = 0; s < XS; ++s) {
       mbar_init(xfull + s, 1);
-      mbar_init(deq + s, kDeqThreads);
-      mbar_init(empty + s, 1);
+      mbar_init(xempty + s, 1);
     }
-    mbar_init(accum, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(deq + s, kDeqGroupWarps);
+      mbar_init(aempty + s, 1);
+    }
+    mbar_init(accum, 2);  // both MMA warps
     *abort = 0;
     fence_mbar_init();
   }
@@ -203,75 +268,152 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     // ---------------------------------------------------------- producer --
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const uint32_t wbytes = a.q4 ? kQ4TcChunkBytes : kF16TcChunkBytes;
+      const uint32_t cbytes = q4 ? kQ4TcChunkBytes : kF16TcChunkBytes;  // weight bytes per chunk
+      // Unit i: chunks c0 + U i .. +U-1, adjacent in the weight blob (one copy)
+      // but not always in the activation tiles (one copy per chunk).
       auto load_w = [&](int i) {
-        const int s = i % S;
-        mbar_arrive_expect_tx(wfull + s, wbytes);
-        uint8_t* wdst = a.q4 ? sR + s * kQ4TcChunkBytes : sA + s * kF16TcChunkBytes;
-        bulk_g2s_stream(wdst, a.w + ((size_t)tile * n_chunks + c0 + i) * wbytes, wbytes, wfull + s,
-                        pol);
+        const int s = i % NW;
+        const uint32_t bytes = cbytes * (uint32_t)U;
+        mbar_arrive_expect_tx(wfull + s, bytes);
+        uint8_t* wdst = q4 ? sR + s * runit : sA + s * kF16TcChunkBytes;
+        bulk_g2s_stream(wdst, a.w + ((size_t)tile * n_chunks + c0 + (size_t)i * U) * cbytes, bytes,
+                        wfull + s, pol);
       };
       auto load_x = [&](int i) {
-        const int s = i % S;
-        mbar_arrive_expect_tx(xfull + s, xbytes);
-        bulk_g2s(sX + s * xbytes, a.act + (size_t)(c0 + i) * act_chunk_bytes, xbytes, xfull + s);
+        const int s = i % XS;
+        mbar_arrive_expect_tx(xfull + s, xunit);
+        for (int j = 0; j < U; ++j)
+          bulk_g2s(sX + s * xunit + j * xbytes, a.act + (size_t)(c0 + i * U + j) * act_chunk_bytes,
+                   xbytes, xfull + s);
       };
-      const int pre = cps < S ? cps : S;
-      for (int i = 0; i < pre; ++i) load_w(i);  // weights do not depend on earlier kernels
+      int nw = nu < NW ? nu : NW, nx = nu < XS ? nu : XS;  // units issued
+      for (int i = 0; i < nw; ++i) load_w(i);  // weights do not depend on earlier kernels
       pdl_wait();
-      for (int i = 0; i < pre; ++i) load_x(i);
-      int i = pre;
-      for (; i < cps; ++i) {
-        const int s = i % S;
-        if (!tc_wait(empty + s, ((i / S) - 1) & 1, abort, a.err)) break;
-        load_w(i);
-        load_x(i);
+      for (int i = 0; i < nx; ++i) load_x(i);
+      // Refill in the order the slots free up: the weight slot of chunk t once
+      // it was read (Q4: dequantised, which precedes its MMAs; fp16: its MMAs
+      // completed), then its activation slot once its MMAs completed.  While a
+      // refill is due, nw == t + NW and nx == t + XS.
+      for (int t = 0; nw < nu || nx < nu; ++t) {
+        if (nw < nu) {
+          const bool ok = q4 ? tc_wait(rempty + t % RS, (t / RS) & 1, abort, a.err)
+                             : tc_wait(aempty + t % S, (t / S) & 1, abort, a.err);
+          if (!ok) break;
+          load_w(nw++);
+        }
+        if (nx < nu) {
+          if (!tc_wait(xempty + t % XS, (t / XS) & 1, abort, a.err)) break;
+          load_x(nx++);
+        }
       }
       // Every issued copy lands before the CTA may exit.
-      for (int j = i > S ? i - S : 0; j < i; ++j) {
-        tc_wait(wfull + j % S, (j / S) & 1, abort, a.err, false);
-        tc_wait(xfull + j % S, (j / S) & 1, abort, a.err, false);
-      }
+      for (int j = nw > NW ? nw - NW : 0; j < nw; ++j)
+        tc_wait(wfull + j % NW, (j / NW) & 1, abort, a.err, false);
+      for (int j = nx > XS ? nx - XS : 0; j < nx; ++j)
+        tc_wait(xfull + j % XS, (j / XS) & 1, abort, a.err, false);
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
+  } else if (warp >= kMmaWarp) {
     // --------------------------------------------------------------- MMA --
-    if (lane == 0) {
-      const uint32_t idesc = f16_idesc(kTcM, nb);
-      for (int i = 0; i < cps; ++i) {
-        const int s = i % S;
-        if (!tc_wait(a.q4 ? deq + s : wfull + s, (i / S) & 1, abort, a.err)) break;
-        if (!tc_wait(xfull + s, (i / S) & 1, abort, a.err)) break;
-        tc_fence_after();
-        const uint64_t ad = sw128_kmajor_desc(smem_u32(sA + s * kF16TcChunkBytes));
-        const uint64_t bd = sw128_kmajor_desc(smem_u32(sX + s * xbytes));
+    // MMA warp m takes units m, m + MW, ... into accumulator m.  The warp
+    // loops converged (every lane waits); lane 0 issues.  One wait per Q4
+    // unit: deq[s] completes only after the unit's activations landed.
+    const int m = warp - kMmaWarp;
+    const uint32_t idesc = f16_idesc(kTcM, nb);
+    const uint32_t dacc = tmem + (uint32_t)m * acc_cols;
+    bool issued = false;
+    for (int i = m; m < MW && i < nu; i += MW) {
+      const int s = i % S, xs = i % XS;
+      bool ok = tc_wait(q4 ? deq + s : wfull + s, (i / S) & 1, abort, a.err);
+      if (!q4) ok = ok && tc_wait(xfull + xs, (i / XS) & 1, abort, a.err);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t bd = sw128_kmajor_desc(smem_u32(sX + xs * xunit));
+        if (q4) {
+          for (int j = 0; j < U; ++j) {
+            const uint32_t at = tmem + a_base + (uint32_t)(s * U + j) * kTmemAStageCols;
+            const uint64_t bj = bd + (uint64_t)((j * xbytes) >> 4);  // next activation tile
 #pragma unroll
-        for (int kk = 0; kk < kTcChunkK / 16; ++kk)  // +32 B of k per MMA inside the atom
-          tc_mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
-        tc_commit(empty + s);
+            for (int kk = 0; kk < kTcChunkK / 16; ++kk)  // 8 columns (16 k) of A, +32 B of X
+              tc_mma_f16_ta(dacc, at + 8u * kk, bj + 2 * kk, idesc,
+                            (i != m || j != 0 || kk != 0) ? 1u : 0u);
+          }
+        } else {
+          const uint64_t ad = sw128_kmajor_desc(smem_u32(sA + s * kF16TcChunkBytes));
+#pragma unroll
+          for (int kk = 0; kk < kTcChunkK / 16; ++kk)  // +32 B of k per MMA inside the atom
+            tc_mma_f16(dacc, ad + 2 * kk, bd + 2 * kk, idesc, (i != m || kk != 0) ? 1u : 0u);
+        }
+        tc_commit(aempty + s);
+        tc_commit(xempty + xs);
       }
-      tc_commit(accum);
+      issued = true;
+      __syncwarp();
+    }
+    // accum completes once both warps' MMAs have (a warp without any arrives
+    // directly).
+    if (lane == 0) {
+      if (issued)
+        tc_commit(accum);
+      else
+        mbar_arrive(accum);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------- dequant (Q4 only) --
-    // Thread (h, r): block h (32 k) of row r of the chunk.
+    // Group h (warps 4h..4h+3) takes chunks h, h+2, ...; thread r of the
+    // group dequantises row r into tensor-memory lane r (warp 4h+q owns lanes
+    // 32q..32q+31).  Waits are made warp-uniform so that the per-warp
+    // arrivals (lane 0 after __syncwarp) and the warp-collective tcgen05.st
+    // stay well-formed on abort.
     const int r = threadIdx.x & (kTcM - 1), h = threadIdx.x >> 7;
-    if (a.q4) {
-      for (int i = 0; i < cps; ++i) {
-        const int s = i % S;
-        if (!tc_wait(wfull + s, (i / S) & 1, abort, a.err)) break;
-        const uint8_t* raw = sR + s * kQ4TcChunkBytes;
-        const uint4 pk = *reinterpret_cast<const uint4*>(raw + h * 2048 + r * 16);
-        const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(raw + 4096 + r * 4 + h * 2));
-        uint8_t* arow = sA + s * kF16TcChunkBytes + r * 128;
-        const uint32_t sw = (uint32_t)(r & 7), j0 = 4u * (uint32_t)h;
-        *reinterpret_cast<uint4*>(arow + (((j0 + 0u) ^ sw) << 4)) = dequant8(pk.x, s2);
-        *reinterpret_cast<uint4*>(arow + (((j0 + 1u) ^ sw) << 4)) = dequant8(pk.y, s2);
-        *reinterpret_cast<uint4*>(arow + (((j0 + 2u) ^ sw) << 4)) = dequant8(pk.z, s2);
-        *reinterpret_cast<uint4*>(arow + (((j0 + 3u) ^ sw) << 4)) = dequant8(pk.w, s2);
-        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-        mbar_arrive(deq + s);
+    const int q = (threadIdx.x >> 5) & 3;
+    if (q4) {
+      const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + a_base;
+      for (int i = h; i < nu; i += 2) {
+        const int s = i % S, rs = i % RS;
+        if (!__all_sync(0xffffffffu, tc_wait(wfull + rs, (i / RS) & 1, abort, a.err))) break;
+        bool failed = false;
+        for (int j = 0; j < U; ++j) {
+          const uint8_t* raw = sR + rs * runit + j * kQ4TcChunkBytes;
+          const uint4 p0 = *reinterpret_cast<const uint4*>(raw + r * 16);
+          const uint4 p1 = *reinterpret_cast<const uint4*>(raw + 2048 + r * 16);
+          const __half2 sc = *reinterpret_cast<const __half2*>(raw + 4096 + r * 4);
+          const __half2 s0 = __low2half2(sc), s1 = __high2half2(sc);
+          uint32_t v[32];
+          dequant8(p0.x, s0, v + 0);
+          dequant8(p0.y, s0, v + 4);
+          dequant8(p0.z, s0, v + 8);
+          dequant8(p0.w, s0, v + 12);
+          dequant8(p1.x, s1, v + 16);
+          dequant8(p1.y, s1, v + 20);
+          dequant8(p1.z, s1, v + 24);
+          dequant8(p1.w, s1, v + 28);
+          if (j == U - 1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(rempty + rs);  // the raw slot may be refilled
+          }
+          if (j == 0) {
+            if (i >= S &&
+                !__all_sync(0xffffffffu, tc_wait(aempty + s, ((i / S) - 1) & 1, abort, a.err))) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+          }
+          tmem_st32(lane_base + (uint32_t)(s * U + j) * kTmemAStageCols, v);
+        }
+        if (failed) break;
+        tmem_wait_st();
+        tc_fence_before();
+        // One warp of the group also waits for the unit's activations, so the
+        // MMA warp needs a single wait per unit.
+        if (q == 0 &&
+            !__all_sync(0xffffffffu, tc_wait(xfull + i % XS, (i / XS) & 1, abort, a.err)))
+          break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(deq + s);
       }
     }
     // ---------------------------------------------------------- epilogue --
@@ -285,42 +427,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     const int groups = nb / 16, gsplit = (groups + 1) / 2;
     const int g0 = h == 0 ? 0 : gsplit, g1 = h == 0 ? gsplit : groups;
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    // The second accumulator holds units 1, 3, ... (none when nu == 1).
+    const bool two = MW == 2 && nu > 1;
+    auto ld_acc = [&](uint32_t col, float (&v)[16]) {
+      tmem_ld16(lane_addr + col, v);
+      if (two) {
+        float w[16];
+        tmem_ld16(lane_addr + acc_cols + col, w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += w[j];
+      }
+    };
     if (a.swiglu_act) {
-      // Up rows (lanes 64..127) -> fp16 in shared memory [b][64] (the A ring
-      // is idle once the accumulator is complete), then the gate-row warps
-      // combine them.
-      __half* ub = reinterpret_cast<__half*>(sA);
-      if (go && r >= 64)
+      // half(gate) and half(up) of every row and column to shared memory
+      // [b][128] (the activation ring is idle once the accumulators are
+      // complete); then all 256 threads form 8 outputs each per 16-byte
+      // store.  The tile's 64 gate rows are k = 64 tile .. +63 of the down
+      // projection's input: exactly activation chunk `tile`, stored whole.
+      __half* gu = reinterpret_cast<__half*>(sX);
+      if (go)
         for (int c = 16 * g0; c < 16 * g1; c += 16) {
           float v[16];
-          tmem_ld16(lane_addr + (uint32_t)c, v);
+          ld_acc((uint32_t)c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) ub[(c + j) * 64 + (r - 64)] = f2h(v[j]);
+          for (int j = 0; j < 16; ++j) gu[(c + j) * 128 + r] = f2h(v[j]);
         }
       asm volatile("bar.sync 2, 256;" ::: "memory");  // the eight epilogue warps
-      if (go && r < 64) {
-        const int hrow = tile * 64 + r;  // k index of the down projection's input
-        const int cc = hrow >> 6, jj = (hrow >> 3) & 7;
-        for (int c = 16 * g0; c < 16 * g1; c += 16) {
-          float v[16];
-          tmem_ld16(lane_addr + (uint32_t)c, v);
+      if (go) {
+        uint8_t* chunk = a.swiglu_act + (size_t)tile * a.swiglu_nb * 128;
+        for (int it = threadIdx.x; it < a.nb_valid * 8; it += kDeqThreads) {
+          const int b = it >> 3, jj = it & 7;
+          const uint4 g8 = *reinterpret_cast<const uint4*>(gu + b * 128 + jj * 8);
+          const uint4 u8 = *reinterpret_cast<const uint4*>(gu + b * 128 + 64 + jj * 8);
+          const uint32_t gw[4] = {g8.x, g8.y, g8.z, g8.w}, uw[4] = {u8.x, u8.y, u8.z, u8.w};
+          uint32_t o[4];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int b = c + j;
-            if (b < a.nb_valid) {
-              const float gt = h2f(f2h(v[j])), up = h2f(ub[b * 64 + r]);
-              const size_t off = ((size_t)cc * a.swiglu_nb + b) * 128 +
-                                 (((uint32_t)jj ^ (uint32_t)(b & 7)) << 4) + (hrow & 7) * 2;
-              *reinterpret_cast<__half*>(a.swiglu_act + off) = f2h(silu_ref(gt) * up);
-            }
+          for (int e = 0; e < 4; ++e) {
+            const float2 g2 = __half22float2(u32_as_h2(gw[e])), u2 = __half22float2(u32_as_h2(uw[e]));
+            o[e] = h2_as_u32(__floats2half2_rn(silu_ref(g2.x) * u2.x, silu_ref(g2.y) * u2.y));
           }
+          *reinterpret_cast<uint4*>(chunk + (size_t)b * 128 + (((uint32_t)jj ^ (uint32_t)(b & 7)) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     } else if (go) {
       const size_t row = (size_t)tile * kTcM + r;
       for (int c = 16 * g0; c < 16 * g1; c += 16) {
         float v[16];
-        tmem_ld16(lane_addr + (uint32_t)c, v);
+        ld_acc((uint32_t)c, v);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int b = c + j;
@@ -420,16 +574,56 @@ inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threa
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(int nb, bool q4, int stages) {
-  return 1024 + (size_t)stages * kF16TcChunkBytes + (size_t)stages * nb * 128 +
-         (q4 ? (size_t)stages * kQ4TcChunkBytes : 0) + (4 * stages + 1) * 8 + 16;
+size_t tc_gemm_smem_bytes(int nb, bool q4, int stages, int xstages, int raw_stages, int unit) {
+  const int rs = q4 ? raw_stages : 0;
+  const int nw = q4 ? rs : stages;
+  const int sa = q4 ? 0 : stages;  // Q4 A stages live in tensor memory
+  return 1024 + (size_t)sa * kF16TcChunkBytes + (size_t)xstages * unit * nb * 128 +
+         (size_t)rs * unit * kQ4TcChunkBytes + 8 * (size_t)(nw + rs + 2 * xstages + 2 * stages + 1) +
+         8;
 }
 
-// The deepest ring (up to 4 stages) that fits one CTA's shared memory.
-int tc_gemm_stages(int nb, bool q4) {
-  int st = kTcMaxStages;
-  while (st > 2 && tc_gemm_smem_bytes(nb, q4, st) > 227 * 1024) --st;
-  return st;
+// Ring depths (in pipeline units of `unit` chunks) for nu units per CTA within
+// 227 KB of shared memory.  Q4: 4 A stages in tensor memory; the activation
+// ring (at most 12 chunks, at least min(nu, 4) units) with room left for
+// min(nu, 8) raw units, then the raw ring with the rest (at most 32 units;
+// even unless it holds every unit).  fp16: activation ring of min(nu, 4),
+// shared-memory A ring (HBM weights) of up to 4: at 64 activation rows two
+// CTAs then share an SM, which the LM head's many tiles need more than depth.
+void tc_gemm_rings(int nb, bool q4, int nu, int unit, int* stages, int* xstages, int* raw_stages) {
+  auto lim = [](int v, int hi) { return v < hi ? v : hi; };
+  if (!q4) {
+    const int xs = lim(nu, 4) < 2 ? 2 : lim(nu, 4);
+    int st = kTcMaxF16Stages;
+    while (st > 2 && tc_gemm_smem_bytes(nb, false, st, xs, 0, 1) > kTcSmemBudget) --st;
+    *stages = st;
+    *xstages = xs;
+    *raw_stages = 0;
+    return;
+  }
+  const int st = kTcMaxStages;
+  const int rs_min = lim(nu, 8);
+  // At least min(nu, st) activation stages: a dequantising warp waits for the
+  // activations of unit i once the MMAs of unit i - st completed, so the
+  // previous fill of its slot (unit i - xs) has landed and the parity wait
+  // cannot alias it.
+  const int xs_min = lim(nu, st) < 2 ? 2 : lim(nu, st);
+  int xs = lim(nu, kTcMaxXStages / unit);
+  if (xs < xs_min) xs = xs_min;
+  while (xs > xs_min && tc_gemm_smem_bytes(nb, true, st, xs, rs_min, unit) > kTcSmemBudget) --xs;
+  // A refilled activation ring has an even depth: with two MMA warps (units
+  // alternate between them) the MMAs of unit i - st having completed implies
+  // those of unit i - xs only when the two units share a warp.
+  if (xs < nu && (xs & 1)) --xs;
+  int rs = lim(nu, kTcMaxRawStages);
+  while (rs > 2 && tc_gemm_smem_bytes(nb, true, st, xs, rs, unit) > kTcSmemBudget) --rs;
+  // A ring that is refilled must have an even depth: unit i then reuses the
+  // slot of unit i - rs of the same dequantising group, which that group has
+  // already read, so its parity wait can never alias a fill two phases back.
+  if (rs < nu && (rs & 1)) --rs;
+  *stages = st;
+  *xstages = xs;
+  *raw_stages = rs;
 }
 
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
@@ -443,8 +637,24 @@ int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
       (a.swiglu_act && (a.swiglu_nb < a.nb_valid || !a.q4)))
     return -1;
   TcGemmArgs args = a;
-  args.stages = tc_gemm_stages(a.nb, a.q4);
-  const size_t smem = tc_gemm_smem_bytes(a.nb, a.q4, args.stages);
+  // Two-chunk units (half the waits and commits per MMA) where the chunk count
+  // is even and the rings still fit; else single chunks.
+  const int cps = (a.k / kTcChunkK) / a.splits;
+  size_t smem = 0;
+  for (int u = (a.q4 && cps % 2 == 0) ? 2 : 1; u >= 1; --u) {
+    args.unit = u;
+    tc_gemm_rings(a.nb, a.q4, cps / u, u, &args.stages, &args.xstages, &args.raw_stages);
+    smem = tc_gemm_smem_bytes(a.nb, a.q4, args.stages, args.xstages, args.raw_stages, u);
+    if (smem <= kTcSmemBudget) break;
+  }
+  // A second MMA warp (and accumulator) where both accumulators and the A
+  // stages fit in the 512 tensor-memory columns.
+  {
+    const int acc = a.nb <= 32 ? 32 : a.nb <= 64 ? 64 : a.nb <= 128 ? 128 : 256;
+    const int astage = a.q4 ? args.stages * args.unit * 32 : 0;
+    args.mma_warps = (2 * acc + astage <= 512) ? 2 : 1;
+  }
+  if (smem > kTcSmemBudget) return -1;
   if (cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return -1;

@@ -64,7 +64,11 @@ struct TcGemmArgs {
   int swiglu_nb = 0;
   int* err = nullptr;
   bool pdl = false;            // launch as a programmatic dependent of the previous kernel
-  int stages = 0;              // ring depth, set by launch_tc_gemm
+  int stages = 0;              // A ring depth, set by launch_tc_gemm
+  int xstages = 0;             // activation ring depth, set by launch_tc_gemm
+  int raw_stages = 0;          // Q4 raw-weight ring depth, set by launch_tc_gemm
+  int unit = 1;                // 64-k chunks per pipeline stage, set by launch_tc_gemm
+  int mma_warps = 1;           // issuing warps / accumulators, set by launch_tc_gemm
 };
 
 // K splits for a launch: the largest divisor d of the chunk count with
@@ -77,8 +81,8 @@ inline int tc_choose_splits(int n_tiles, int n_chunks, int sm_count) {
   return best;
 }
 
-size_t tc_gemm_smem_bytes(int nb, bool q4, int stages);
-int tc_gemm_stages(int nb, bool q4);
+size_t tc_gemm_smem_bytes(int nb, bool q4, int stages, int xstages, int raw_stages, int unit);
+void tc_gemm_rings(int nb, bool q4, int nu, int unit, int* stages, int* xstages, int* raw_stages);
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st);
 
 // Weight repacking (device to device) into the blobs above.
