@@ -38,8 +38,6 @@ constexpr int kLMTiles = 151936 / 16;           // 9496
 constexpr int kLMStepBytes = 512;               // one k16 step of a 16-row fp16 tile
 constexpr int kLMTileBytes = 96 * kLMStepBytes; // 49152
 constexpr int kLMChunkSteps = 24;               // 12288 B per streamed chunk
-constexpr int kLMItemsPerTile = 96 / kLMChunkSteps;  // streamed chunks (items) per LM tile
-static_assert(96 % kLMChunkSteps == 0, "LM tiles split into whole chunks");
 constexpr int kDownChunkBp = 24;                // down tiles stream in chunks of 24 block pairs
 
 constexpr int kSlotBytes = kTile1536Bytes;      // ring slot
