@@ -737,28 +737,25 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       }
       cur = e;
     };
-    // Multi-chunk tiles (down, K = 8960 in 24-pair chunks): each warp takes a
-    // contiguous 1/8 of the tile's block pairs, so it waits for and releases
-    // only the one or two chunks its range touches and streams its pairs
-    // back to back.  Striding every chunk over all warps cost each warp a slot
-    // wait, three block pairs and a release per chunk: ~0.8 us per chunk.
-    // A chunk's empty barrier still gets kConsumerWarps arrivals in all: the
-    // first warp touching it adds the share of the warps that do not.
-    auto ksplit_tile = [&](int e, auto&& epilogue) {
-      for (int a = cur; a < e;) {
-        int b = a;
-        while (b < e - 1 && !unpack_item(items[b]).last) ++b;
-        ++b;  // items [a, b): the chunks of one tile
-        const ItemFields first = unpack_item(items[a]), final_it = unpack_item(items[b - 1]);
-        const int nbp = final_it.k0 + final_it.nk - first.k0;
-        auto lo_of = [&](int w) { return first.k0 + w * nbp / kConsumerWarps; };
-        const int lo = lo_of(warp), hi = lo_of(warp + 1);
+    // Down tiles (K = 8960: kBp8960 block pairs in chunks of kDownChunkBp):
+    // each warp takes a contiguous 1/8 of the tile's block pairs, so it waits
+    // for and releases only the one or two chunks its range touches, found
+    // arithmetically, and streams its pairs back to back.  Striding every
+    // chunk over all warps cost each warp a slot wait, three block pairs and
+    // a release per chunk (~0.8 us per chunk).  A chunk's empty barrier still
+    // gets kConsumerWarps arrivals in all: the first warp touching it adds the
+    // share of the warps that do not.
+    auto ksplit_down = [&](int e, auto&& epilogue) {
+      constexpr int kChunks = (kBp8960 + kDownChunkBp - 1) / kDownChunkBp;
+      auto lo_of = [](int w) { return w * kBp8960 / kConsumerWarps; };
+      const int lo = lo_of(warp), hi = lo_of(warp + 1);
+      for (int a = cur; a + kChunks <= e; a += kChunks) {  // items [a, a + kChunks): one tile
         float acc_g = 0.f, acc_g8 = 0.f;
-        for (int i = a; i < b; ++i) {
+        for (int c = lo / kDownChunkBp; c <= (hi - 1) / kDownChunkBp; ++c) {
+          const int i = a + c;
           const ItemFields it = unpack_item(items[i]);
           const int i0 = it.k0, i1 = it.k0 + it.nk;
           const int s0 = max(lo, i0), s1 = min(hi, i1);
-          if (s0 >= s1) continue;
           int wfirst = -1, ntouch = 0;  // warps whose ranges meet this chunk
           for (int w = 0; w < kConsumerWarps; ++w)
             if (max(lo_of(w), i0) < min(lo_of(w + 1), i1)) {
@@ -783,10 +780,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         if (ct < 16) {
           float sum = 0.f;
           for (int w = 0; w < kConsumerWarps; ++w) sum += red[w * 16 + ct];
-          epilogue(first.tile, ct, sum);
+          epilogue((int)unpack_item(items[a]).tile, ct, sum);
         }
         cbar();
-        a = b;
       }
       cur = e;
     };
@@ -977,7 +973,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           wsel = layer == p.n_layers / 2 ? 1 : -1;
           if (wtrace && ct == 0 && wsel >= 0) wtrace[1] = 0;
           const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
-          ksplit_tile(e, [&](int tile, int r, float sum) {
+          ksplit_down(e, [&](int tile, int r, float sum) {
             const int row = 16 * tile + r;
             const __half d = f2h(sum + (tile == dtile ? dbias : h2f(db[row])));
             st_tag16(p.x_ll + row, tg, __hadd(xloc[row], d));
