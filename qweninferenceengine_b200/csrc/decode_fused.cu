@@ -299,6 +299,24 @@ __device__ __forceinline__ void q4_chunk(const uint8_t* slot, int k0, int b_begi
   acc_g8 += g8a + g8b;
 }
 
+// Same with three block pairs in flight: the single-tile phases (QKV, O) give
+// each warp 3 strided block pairs, which q4_chunk runs as a pair then a tail,
+// two dependent rounds.
+__device__ __forceinline__ void q4_chunk3(const uint8_t* slot, int k0, int b_begin, int b_end,
+                                          int b_step, const uint4* xf, int lane, float& acc_g,
+                                          float& acc_g8) {
+  float ga = 0.f, g8a = 0.f, gb = 0.f, g8b = 0.f, gc = 0.f, g8c = 0.f;
+  int b = b_begin;
+  for (; b + 2 * b_step < b_end; b += 3 * b_step) {
+    q4_bp(slot, k0, b, xf, lane, ga, g8a);
+    q4_bp(slot, k0, b + b_step, xf, lane, gb, g8b);
+    q4_bp(slot, k0, b + 2 * b_step, xf, lane, gc, g8c);
+  }
+  for (; b < b_end; b += b_step) q4_bp(slot, k0, b, xf, lane, ga, g8a);
+  acc_g += ga + gb + gc;
+  acc_g8 += g8a + g8b + g8c;
+}
+
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -713,8 +731,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         const ItemFields it = unpack_item(items[i]);
         const int slot = i % kNS;
         if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
-          q4_chunk(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
-                   acc_g8);
+          q4_chunk3(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
+                    acc_g8);
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&empty[slot]);
