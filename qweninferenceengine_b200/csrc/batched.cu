@@ -20,6 +20,8 @@
 //   part  <- W_down . act_i
 //   x     <- half(x + half(part + b_down)); act_h <- rmsnorm_next(x)
 // then logits = LM . act_h (fp16 out, no split).
+#include <cooperative_groups.h>
+
 #include <cmath>
 #include <vector>
 
@@ -69,6 +71,26 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), "launch");
+}
+
+// Same, launched as clusters of `cluster_x` CTAs along x.
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), "launch");
 }
 
@@ -167,31 +189,44 @@ __global__ void __launch_bounds__(64) k_qkv_finish(const float* __restrict__ par
   }
 }
 
-// x <- half(x + half(sum + bias)); act_h row <- rmsnorm(x) with gamma.
-__global__ void __launch_bounds__(512) k_resid_norm_finish(const float* __restrict__ part, int splits,
-                                                           int nbv, const __half* __restrict__ bias,
-                                                           __half* __restrict__ x,
-                                                           const __half* __restrict__ gamma,
-                                                           uint8_t* __restrict__ act, int nb) {
+// x <- half(x + half(sum + bias)); act_h row <- rmsnorm(x) with gamma.  A
+// cluster of kFinCtas CTAs per row, one column per thread, so every thread
+// issues all its split loads at once (one CTA per row kept 84 of 148 SMs idle
+// and walked three columns per thread); the row's sum of squares meets in
+// distributed shared memory, added in rank order.
+constexpr int kFinCtas = 4;
+constexpr int kFinThreads = kHidden / kFinCtas;  // 384
+__global__ void __launch_bounds__(kFinThreads) k_resid_norm_finish(
+    const float* __restrict__ part, int splits, int nbv, const __half* __restrict__ bias,
+    __half* __restrict__ x, const __half* __restrict__ gamma, uint8_t* __restrict__ act, int nb) {
   pdl_prologue();
-  __shared__ float red[16];
-  const int b = blockIdx.x;
+  namespace cg = cooperative_groups;
+  __shared__ float red[kFinThreads / 32];
+  __shared__ float cta_ss;  // this CTA's sum of squares, read by the cluster
+  cg::cluster_group cluster = cg::this_cluster();
+  const int b = blockIdx.y;
+  const int i = (int)cluster.block_rank() * kFinThreads + (int)threadIdx.x;
   __half* xr = x + (size_t)b * kHidden;
-  float v[3];
+  const __half y = f2h(sum_splits(part, splits, nbv, kHidden, b, i) + h2f(bias[i]));
+  const __half xn = __hadd(xr[i], y);
+  xr[i] = xn;
+  const float v = h2f(xn);
+  const float acc = warp_sum(v * v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
 #pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    const int i = threadIdx.x + 512 * j;
-    const __half y = f2h(sum_splits(part, splits, nbv, kHidden, b, i) + h2f(bias[i]));
-    const __half xn = __hadd(xr[i], y);
-    xr[i] = xn;
-    v[j] = h2f(xn);
+    for (int w = 0; w < kFinThreads / 32; ++w) t += red[w];
+    cta_ss = t;
   }
-  const float s = rms_scale_row<512, 3>(v, red);
+  cluster.sync();
+  float tot = 0.f;
 #pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    const int i = threadIdx.x + 512 * j;
-    *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v[j] * s), gamma[i]);
-  }
+  for (int r = 0; r < kFinCtas; ++r) tot += *cluster.map_shared_rank(&cta_ss, r);
+  const float sc = 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
+  *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v * sc), gamma[i]);
+  cluster.sync();  // peers may still be reading cta_ss
 }
 
 // Row r = position p0 + r of sequence 0: x[r] = embedding of its prompt id,
@@ -377,16 +412,18 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, const TcRows& v, int sm_
     mark();
     QWEN_TRY(gemm(o, true, s.act_h, s, B, kHidden, kHidden, p.o, s.tc_part, nullptr, 0, st));
     mark();
-    QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.o, B, L.o_bias,
-                        v.x, L.post_attn_norm, s.act_h, nb));
+    QWEN_TRY(launch_pdl_cluster(k_resid_norm_finish, dim3(kFinCtas, B), dim3(kFinThreads), kFinCtas,
+                                st, s.tc_part, p.o, B, L.o_bias, v.x, L.post_attn_norm, s.act_h,
+                                nb));
     mark();
     QWEN_TRY(gemm(gu, true, s.act_h, s, B, 2 * kInter, kHidden, 1, nullptr, nullptr, 0, st, s.act_i));
     mark();
     QWEN_TRY(gemm(down, true, s.act_i, s, B, kHidden, kInter, p.down, s.tc_part, nullptr, 0, st));
     mark();
     const __half* next_norm = l + 1 < m.n_layers ? m.layers[l + 1].input_norm : m.final_norm;
-    QWEN_TRY(launch_pdl(k_resid_norm_finish, dim3(B), dim3(512), st, s.tc_part, p.down, B,
-                        L.down_bias, v.x, next_norm, s.act_h, nb));
+    QWEN_TRY(launch_pdl_cluster(k_resid_norm_finish, dim3(kFinCtas, B), dim3(kFinThreads), kFinCtas,
+                                st, s.tc_part, p.down, B, L.down_bias, v.x, next_norm, s.act_h,
+                                nb));
     mark();
   }
   if (v.logits) {
