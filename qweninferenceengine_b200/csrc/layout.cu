@@ -125,21 +125,29 @@ static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items
     for (int t = 0; t < kQKVTiles; ++t)
       add_tile(t % grid, ph + kPhQKV, t, lb + kLayerQKVOff + (size_t)t * kTile1536Bytes, kBp1536,
                kBp1536, kBpBytes);
-    for (int t = 0; t < kOTiles; ++t)
-      add_tile(least(0, grid), ph + kPhO, t, lb + kLayerOOff + (size_t)t * kTile1536Bytes,
-               kBp1536, kBp1536, kBpBytes);
-    // gate/up: every consumer warp owns at most one tile per layer
-    const int gu_cap = (kGUTiles + grid - 1) / grid;
-    for (int t = 0; t < kGUTiles; ++t) {
+    // The least-loaded CTA that holds fewer than `cap` tiles of the phase: a
+    // phase lasts as long as its busiest CTA, so O and down tiles are spread
+    // one per CTA (without the cap the byte balance over the whole step gave
+    // ~52 CTAs two O tiles each, run back to back) and gate/up tiles one per
+    // consumer warp.
+    auto least_capped = [&](uint16_t phase, int cap) {
       int best = -1;
       for (int c = 0; c < grid; ++c)
-        if (tiles_in_phase[c][ph + kPhGU] < gu_cap && (best < 0 || load[c] < load[best])) best = c;
-      add_tile(best, ph + kPhGU, t, lb + kLayerGUOff + (size_t)t * kTile1536Bytes, kBp1536,
-               kBp1536, kBpBytes);
-    }
+        if (tiles_in_phase[c][phase] < cap && (best < 0 || load[c] < load[best])) best = c;
+      return best;
+    };
+    const int o_cap = (kOTiles + grid - 1) / grid;
+    for (int t = 0; t < kOTiles; ++t)
+      add_tile(least_capped(ph + kPhO, o_cap), ph + kPhO, t,
+               lb + kLayerOOff + (size_t)t * kTile1536Bytes, kBp1536, kBp1536, kBpBytes);
+    const int gu_cap = (kGUTiles + grid - 1) / grid;
+    for (int t = 0; t < kGUTiles; ++t)
+      add_tile(least_capped(ph + kPhGU, gu_cap), ph + kPhGU, t,
+               lb + kLayerGUOff + (size_t)t * kTile1536Bytes, kBp1536, kBp1536, kBpBytes);
+    const int down_cap = (kDownTiles + grid - 1) / grid;
     for (int t = 0; t < kDownTiles; ++t)
-      add_tile(least(0, grid), ph + kPhDown, t, lb + kLayerDownOff + (size_t)t * kTile8960Bytes,
-               kBp8960, kDownChunkBp, kBpBytes);
+      add_tile(least_capped(ph + kPhDown, down_cap), ph + kPhDown, t,
+               lb + kLayerDownOff + (size_t)t * kTile8960Bytes, kBp8960, kDownChunkBp, kBpBytes);
   }
   const uint16_t lm_phase = (uint16_t)(n_layers * kPhasesPerLayer);
   for (int t = 0; t < kLMTiles; ++t)
