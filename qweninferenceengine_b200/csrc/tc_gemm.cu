@@ -1,7 +1,7 @@
 // tc_gemm.cu -- batched Q4 / fp16 projections on tcgen05 tensor cores.
 //
 // CTA = 128 output rows x nb activation rows, K split over grid.y.  Ten warps:
-//   warp 8      producer: one lane issues the 1-D bulk copies.  Q4 weights go
+//   warp 16     producer: one lane issues the 1-D bulk copies.  Q4 weights go
 //               to a deep ring of raw 4608-byte chunks (up to 32; usually
 //               every chunk of the CTA), all issued before griddepcontrol.wait
 //               -- weights do not depend on the previous kernel of the stream,
@@ -9,14 +9,14 @@
 //               as a chunk has been read by the dequantising warps.
 //               Activations go to their own ring (up to 12 stages) and fp16
 //               weights to the A ring; the MMAs free both.
-//   warps 0..7  Q4: two groups of four warps take alternate chunks; thread r
+//   warps 0..15 Q4: four groups of four warps take units in turn; thread r
 //               of a group dequantises both 32-weight blocks of row r (16
 //               nibble pairs each -> fp16 via the 0x6400 exponent trick, (q - 8)
 //               exact, one rounding for the product with the block scale) into
 //               the 128-byte-swizzled A tile.  Then the epilogue: warp w reads
 //               tensor-memory lanes 32(w%4).. (its rows) for half w/4 of the
 //               columns
-//   warps 9-10  warp 9 allocates tensor memory; each MMA warp takes
+//   warps 17-18 warp 17 allocates tensor memory; each MMA warp takes
 //               alternate units (one or two 64-k chunks), one lane issuing 4
 //               MMAs (M=128, N=nb, K=16) per chunk into the warp's own fp32
 //               accumulator and committing the A stage (aempty) and the
@@ -54,12 +54,13 @@ constexpr int kTcMaxF16Stages = 4;   // A ring (fp16 weights straight from HBM)
 constexpr int kTcMaxXStages = 12;    // activation ring
 constexpr int kTcMaxRawStages = 32;  // Q4 raw-weight ring
 constexpr size_t kTcSmemBudget = 227 * 1024;
-constexpr int kTcThreads = 352;      // warps 0-7 dequant + epilogue, 8 producer, 9-10 MMA
+constexpr int kDeqGroups = 4;        // dequantising groups of 4 warps (one thread per tile row)
+constexpr int kDeqThreads = kDeqGroups * 128;      // warps 0-15: dequant + epilogue
+constexpr int kTcThreads = kDeqThreads + 3 * 32;   // + producer warp + 2 MMA warps
 constexpr int kDeqGroupWarps = 4;    // one dequantising group: 128 threads, one per tile row
-constexpr int kDeqThreads = 256;     // both groups: warps 0-7
 constexpr uint32_t kTmemAStageCols = kTcChunkK / 2;  // a Q4 A stage: 64 fp16 per lane
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;          // allocates tensor memory; MMA warps are 9 and 10
+constexpr int kProducerWarp = kDeqThreads / 32;   // 16
+constexpr int kMmaWarp = kProducerWarp + 1;       // allocates tensor memory; MMA warps 17, 18
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 // ------------------------------------------------------------ tcgen05 PTX --
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     __syncwarp();
   } else {
     // ------------------------------------------------- dequant (Q4 only) --
-    // Group h (warps 4h..4h+3) takes chunks h, h+2, ...; thread r of the
+    // Group h (warps 4h..4h+3) takes units h, h+4, ...; thread r of the
     // group dequantises row r into tensor-memory lane r (warp 4h+q owns lanes
     // 32q..32q+31).  Waits are made warp-uniform so that the per-warp
     // arrivals (lane 0 after __syncwarp) and the warp-collective tcgen05.st
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     const int q = (threadIdx.x >> 5) & 3;
     if (q4) {
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + a_base;
-      for (int i = h; i < nu; i += 2) {
+      for (int i = h; i < nu; i += kDeqGroups) {
         const int s = i % S, rs = i % RS;
         if (!__all_sync(0xffffffffu, tc_wait(wfull + rs, (i / RS) & 1, abort, a.err))) break;
         bool failed = false;
@@ -424,8 +425,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     tc_fence_after();
     // tcgen05.ld is warp-collective: the decision is the warp's, not the lane's.
     const bool go = __all_sync(0xffffffffu, landed && !*abort);
-    const int groups = nb / 16, gsplit = (groups + 1) / 2;
-    const int g0 = h == 0 ? 0 : gsplit, g1 = h == 0 ? gsplit : groups;
+    // Column groups of 16 split over the four dequantising groups.
+    const int groups = nb / 16, gq = (groups + kDeqGroups - 1) / kDeqGroups;
+    const int g0 = min(groups, h * gq), g1 = min(groups, g0 + gq);
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     // The second accumulator holds units 1, 3, ... (none when nu == 1).
     const bool two = MW == 2 && nu > 1;
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) gu[(c + j) * 128 + r] = f2h(v[j]);
         }
-      asm volatile("bar.sync 2, 256;" ::: "memory");  // the eight epilogue warps
+      asm volatile("bar.sync 2, %0;" ::"r"(kDeqThreads) : "memory");  // the epilogue warps
       if (go) {
         uint8_t* chunk = a.swiglu_act + (size_t)tile * a.swiglu_nb * 128;
         for (int it = threadIdx.x; it < a.nb_valid * 8; it += kDeqThreads) {
@@ -586,9 +588,10 @@ size_t tc_gemm_smem_bytes(int nb, bool q4, int stages, int xstages, int raw_stag
 // Ring depths (in pipeline units of `unit` chunks) for nu units per CTA within
 // 227 KB of shared memory.  Q4: 4 A stages in tensor memory; the activation
 // ring (at most 12 chunks, at least min(nu, 4) units) with room left for
-// min(nu, 8) raw units, then the raw ring with the rest (at most 32 units;
-// even unless it holds every unit).  fp16: activation ring of min(nu, 4),
-// shared-memory A ring (HBM weights) of up to 4: at 64 activation rows two
+// min(nu, 8) raw units, then the raw ring with the rest (at most 32 units; a
+// multiple of the dequantising group count unless it holds every unit).  fp16:
+// activation ring of min(nu, 4), shared-memory A ring (HBM weights) of up to
+// 4: at 64 activation rows two
 // CTAs then share an SM, which the LM head's many tiles need more than depth.
 void tc_gemm_rings(int nb, bool q4, int nu, int unit, int* stages, int* xstages, int* raw_stages) {
   auto lim = [](int v, int hi) { return v < hi ? v : hi; };
@@ -617,10 +620,12 @@ void tc_gemm_rings(int nb, bool q4, int nu, int unit, int* stages, int* xstages,
   if (xs < nu && (xs & 1)) --xs;
   int rs = lim(nu, kTcMaxRawStages);
   while (rs > 2 && tc_gemm_smem_bytes(nb, true, st, xs, rs, unit) > kTcSmemBudget) --rs;
-  // A ring that is refilled must have an even depth: unit i then reuses the
-  // slot of unit i - rs of the same dequantising group, which that group has
-  // already read, so its parity wait can never alias a fill two phases back.
-  if (rs < nu && (rs & 1)) --rs;
+  // A ring that is refilled must have a depth that is a multiple of the group
+  // count: unit i then reuses the slot of unit i - rs of the same dequantising
+  // group, which that group has already read, so its parity wait can never
+  // alias a fill two phases back.
+  if (rs < nu) rs -= rs % kDeqGroups;
+  if (rs == 0) rs = kDeqGroups < nu ? kDeqGroups : nu;
   *stages = st;
   *xstages = xs;
   *raw_stages = rs;
