@@ -591,8 +591,8 @@ size_t tc_gemm_smem_bytes(int nb, bool q4, int stages, int xstages, int raw_stag
 // min(nu, 8) raw units, then the raw ring with the rest (at most 32 units; a
 // multiple of the dequantising group count unless it holds every unit).  fp16:
 // activation ring of min(nu, 4), shared-memory A ring (HBM weights) of up to
-// 4: at 64 activation rows two
-// CTAs then share an SM, which the LM head's many tiles need more than depth.
+// 4: at 64 activation rows two CTAs then share an SM, which the LM head's many
+// tiles need more than depth.
 void tc_gemm_rings(int nb, bool q4, int nu, int unit, int* stages, int* xstages, int* raw_stages) {
   auto lim = [](int v, int hi) { return v < hi ? v : hi; };
   if (!q4) {
