@@ -1,6 +1,7 @@
 // tc_gemm.cu -- batched Q4 / fp16 projections on tcgen05 tensor cores.
 //
-// CTA = 128 output rows x nb activation rows, K split over grid.y.  Ten warps:
+// CTA = 128 output rows x nb activation rows, K split over grid.y.  Q4 launches
+// run 19 warps (fp16 launches 11: two dequant/epilogue groups instead of four):
 //   warp 16     producer: one lane issues the 1-D bulk copies.  Q4 weights go
 //               to a deep ring of raw 4608-byte chunks (up to 32; usually
 //               every chunk of the CTA), all issued before griddepcontrol.wait
@@ -54,13 +55,15 @@ constexpr int kTcMaxF16Stages = 4;   // A ring (fp16 weights straight from HBM)
 constexpr int kTcMaxXStages = 12;    // activation ring
 constexpr int kTcMaxRawStages = 32;  // Q4 raw-weight ring
 constexpr size_t kTcSmemBudget = 227 * 1024;
-constexpr int kDeqGroups = 4;        // dequantising groups of 4 warps (one thread per tile row)
-constexpr int kDeqThreads = kDeqGroups * 128;      // warps 0-15: dequant + epilogue
-constexpr int kTcThreads = kDeqThreads + 3 * 32;   // + producer warp + 2 MMA warps
+// Warp layout for NG groups of four dequantising/epilogue warps: warps
+// 0 .. 4NG-1, then the producer warp, then the two MMA warps.  Q4 launches use
+// four groups; the fp16 LM head (no dequantisation) two, so that two CTAs with
+// 60 registers per thread still fit one SM.
+constexpr int kDeqGroups = 4;                      // Q4 launches
+constexpr int kF16DeqGroups = 2;                   // fp16 launches
+__host__ __device__ constexpr int tc_threads(int ng) { return ng * 128 + 3 * 32; }
 constexpr int kDeqGroupWarps = 4;    // one dequantising group: 128 threads, one per tile row
 constexpr uint32_t kTmemAStageCols = kTcChunkK / 2;  // a Q4 A stage: 64 fp16 per lane
-constexpr int kProducerWarp = kDeqThreads / 32;   // 16
-constexpr int kMmaWarp = kProducerWarp + 1;       // allocates tensor memory; MMA warps 17, 18
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 // ------------------------------------------------------------ tcgen05 PTX --
@@ -197,7 +200,11 @@ __device__ __forceinline__ void dequant8(uint32_t w, __half2 s2, uint32_t* o) {
   }
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
+template <int NG>
+__global__ void __launch_bounds__(tc_threads(NG), 1) k_tc_gemm(TcGemmArgs a) {
+  constexpr int kDeqThreads = NG * 128;         // dequant + epilogue threads
+  constexpr int kProducerWarp = NG * 4;
+  constexpr int kMmaWarp = kProducerWarp + 1;   // allocates tensor memory; MMA warps +0, +1
   extern __shared__ uint8_t tc_smem[];
   const bool q4 = a.q4;
   const int U = a.unit;                // 64-k chunks per pipeline unit (Q4: 1 or 2; fp16: 1)
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     const int q = (threadIdx.x >> 5) & 3;
     if (q4) {
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + a_base;
-      for (int i = h; i < nu; i += kDeqGroups) {
+      for (int i = h; i < nu; i += NG) {
         const int s = i % S, rs = i % RS;
         if (!__all_sync(0xffffffffu, tc_wait(wfull + rs, (i / RS) & 1, abort, a.err))) break;
         bool failed = false;
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(TcGemmArgs a) {
     // tcgen05.ld is warp-collective: the decision is the warp's, not the lane's.
     const bool go = __all_sync(0xffffffffu, landed && !*abort);
     // Column groups of 16 split over the four dequantising groups.
-    const int groups = nb / 16, gq = (groups + kDeqGroups - 1) / kDeqGroups;
+    const int groups = nb / 16, gq = (groups + NG - 1) / NG;
     const int g0 = min(groups, h * gq), g1 = min(groups, g0 + gq);
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     // The second accumulator holds units 1, 3, ... (none when nu == 1).
@@ -660,12 +667,13 @@ int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
     args.mma_warps = (2 * acc + astage <= 512) ? 2 : 1;
   }
   if (smem > kTcSmemBudget) return -1;
-  if (cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  void (*kernel)(TcGemmArgs) = a.q4 ? k_tc_gemm<kDeqGroups> : k_tc_gemm<kF16DeqGroups>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return -1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_rows / kTcM, a.splits);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(tc_threads(a.q4 ? kDeqGroups : kF16DeqGroups));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -673,7 +681,7 @@ int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_tc_gemm, args) == cudaSuccess ? 0 : -1;
+  return cudaLaunchKernelEx(&cfg, kernel, args) == cudaSuccess ? 0 : -1;
 }
 
 int launch_repack_q4_tc_rows(const uint8_t* packed, const __half* scales, int n_rows, int k,
