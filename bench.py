@@ -40,7 +40,7 @@ METRIC = "decode tokens/s (bs1 ctx512 per B200)"
 # 1.006 x the algorithmic bytes there).  Weights and LM head are read once per
 # launch, so the traffic at another context adds the KV bytes of the extra
 # positions.
-FUSED_TRAFFIC_CTX6 = 1_212_612_864
+FUSED_TRAFFIC_CTX6 = 1_212_492_544
 
 
 def fused_traffic(ctx: float) -> float:
