@@ -1,31 +1,33 @@
 // tc_gemm.cu -- batched Q4 / fp16 projections on tcgen05 tensor cores.
 //
-// CTA = 128 output rows x nb activation rows, K split over grid.y.  Q4 launches
-// run 19 warps (fp16 launches 11: two dequant/epilogue groups instead of four):
-//   warp 16     producer: one lane issues the 1-D bulk copies.  Q4 weights go
+// CTA = 128 output rows x nb activation rows, K split over grid.y.  NG groups
+// of four warps (NG = 4 for Q4 launches, 2 for the fp16 LM head) plus three:
+//   warp 4NG    producer: one lane issues the 1-D bulk copies.  Q4 weights go
 //               to a deep ring of raw 4608-byte chunks (up to 32; usually
 //               every chunk of the CTA), all issued before griddepcontrol.wait
 //               -- weights do not depend on the previous kernel of the stream,
 //               so they stream in while it still runs -- and refilled as soon
 //               as a chunk has been read by the dequantising warps.
 //               Activations go to their own ring (up to 12 stages) and fp16
-//               weights to the A ring; the MMAs free both.
-//   warps 0..15 Q4: four groups of four warps take units in turn; thread r
-//               of a group dequantises both 32-weight blocks of row r (16
-//               nibble pairs each -> fp16 via the 0x6400 exponent trick, (q - 8)
-//               exact, one rounding for the product with the block scale) into
-//               the 128-byte-swizzled A tile.  Then the epilogue: warp w reads
-//               tensor-memory lanes 32(w%4).. (its rows) for half w/4 of the
-//               columns
-//   warps 17-18 warp 17 allocates tensor memory; each MMA warp takes
-//               alternate units (one or two 64-k chunks), one lane issuing 4
-//               MMAs (M=128, N=nb, K=16) per chunk into the warp's own fp32
-//               accumulator and committing the A stage (aempty) and the
-//               activation stage (xempty) back.  Two issuing warps because a
-//               lone MMA warp's wait -> issue -> commit loop, not the tensor
-//               pipe, set the rate at N=64; the epilogue adds the two
-//               accumulators in a fixed order.  Where two accumulators and the
-//               A stages do not fit in tensor memory (nb > 128), warp 10 idles.
+//               weights to a shared-memory A ring; the MMAs free both.
+//   warps 0..4NG-1  Q4: the groups take units (one or two 64-k chunks) in
+//               turn; thread r of a group dequantises both 32-weight blocks of
+//               row r per chunk (16 nibble pairs each -> fp16 via the 0x6400
+//               exponent trick, (q - 8) exact, one rounding for the product
+//               with the block scale) and stores the row's 64 values into
+//               tensor-memory lane r with one tcgen05.st (one A stage per
+//               group).  Then the epilogue: warp w reads tensor-memory lanes
+//               32(w%4).. (its rows) for its group's share of the columns
+//   warps 4NG+1, 4NG+2  the first allocates tensor memory; each MMA warp takes
+//               alternate units, one lane issuing 4 MMAs (M=128, N=nb, K=16)
+//               per chunk (A from tensor memory, or from shared memory for
+//               fp16) into the warp's own fp32 accumulator and committing the
+//               A stage (aempty) and the activation stage (xempty) back.  Two
+//               issuing warps because a lone MMA warp's wait -> issue -> commit
+//               loop, not the tensor pipe, set the rate at N=64; the epilogue
+//               adds the two accumulators in a fixed order.  Where two
+//               accumulators and the A stages do not fit in tensor memory
+//               (nb > 128), the second MMA warp idles.
 // Three rings because each refill sits on its own loop of latencies: a raw
 // weight chunk is refilled one HBM latency after its dequantisation, an
 // activation chunk one L2 latency (~1.5 us with every CTA reading the same
