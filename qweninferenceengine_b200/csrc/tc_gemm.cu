@@ -640,6 +640,31 @@ void tc_gemm_rings(int nb, bool q4, int nu, int unit, int* stages, int* xstages,
   *raw_stages = rs;
 }
 
+// Launch plan of a GEMM with cps chunks per CTA: unit size, ring depths, MMA
+// warps and dequantising groups, shared memory.  smem > the budget: no plan.
+struct TcLaunchPlan {
+  int unit, stages, xstages, raw_stages, mma_warps, groups;
+  size_t smem;
+};
+static TcLaunchPlan tc_gemm_plan(int nb, bool q4, int cps) {
+  TcLaunchPlan pl{};
+  pl.groups = q4 ? kDeqGroups : kF16DeqGroups;
+  // Two-chunk units (half the waits and commits per MMA) where the chunk count
+  // is even and the rings still fit; else single chunks.
+  for (int u = (q4 && cps % 2 == 0) ? 2 : 1; u >= 1; --u) {
+    pl.unit = u;
+    tc_gemm_rings(nb, q4, cps / u, u, &pl.stages, &pl.xstages, &pl.raw_stages);
+    pl.smem = tc_gemm_smem_bytes(nb, q4, pl.stages, pl.xstages, pl.raw_stages, u);
+    if (pl.smem <= kTcSmemBudget) break;
+  }
+  // A second MMA warp (and accumulator) where both accumulators and the A
+  // stages fit in the 512 tensor-memory columns.
+  const int acc = nb <= 32 ? 32 : nb <= 64 ? 64 : nb <= 128 ? 128 : 256;
+  const int astage = q4 ? pl.stages * pl.unit * 32 : 0;
+  pl.mma_warps = (2 * acc + astage <= 512) ? 2 : 1;
+  return pl;
+}
+
 int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
   if (!a.w || !a.act || a.n_rows <= 0 || a.n_rows % kTcM || a.k <= 0 || a.k % kTcChunkK ||
       a.nb < 16 || a.nb > kTcMaxNb || a.nb % 16 || a.nb_valid < 1 || a.nb_valid > a.nb ||
@@ -651,24 +676,14 @@ int launch_tc_gemm(const TcGemmArgs& a, cudaStream_t st) {
       (a.swiglu_act && (a.swiglu_nb < a.nb_valid || !a.q4)))
     return -1;
   TcGemmArgs args = a;
-  // Two-chunk units (half the waits and commits per MMA) where the chunk count
-  // is even and the rings still fit; else single chunks.
-  const int cps = (a.k / kTcChunkK) / a.splits;
-  size_t smem = 0;
-  for (int u = (a.q4 && cps % 2 == 0) ? 2 : 1; u >= 1; --u) {
-    args.unit = u;
-    tc_gemm_rings(a.nb, a.q4, cps / u, u, &args.stages, &args.xstages, &args.raw_stages);
-    smem = tc_gemm_smem_bytes(a.nb, a.q4, args.stages, args.xstages, args.raw_stages, u);
-    if (smem <= kTcSmemBudget) break;
-  }
-  // A second MMA warp (and accumulator) where both accumulators and the A
-  // stages fit in the 512 tensor-memory columns.
-  {
-    const int acc = a.nb <= 32 ? 32 : a.nb <= 64 ? 64 : a.nb <= 128 ? 128 : 256;
-    const int astage = a.q4 ? args.stages * args.unit * 32 : 0;
-    args.mma_warps = (2 * acc + astage <= 512) ? 2 : 1;
-  }
-  if (smem > kTcSmemBudget) return -1;
+  const TcLaunchPlan pl = tc_gemm_plan(a.nb, a.q4, (a.k / kTcChunkK) / a.splits);
+  if (pl.smem > kTcSmemBudget) return -1;
+  args.unit = pl.unit;
+  args.stages = pl.stages;
+  args.xstages = pl.xstages;
+  args.raw_stages = pl.raw_stages;
+  args.mma_warps = pl.mma_warps;
+  const size_t smem = pl.smem;
   void (*kernel)(TcGemmArgs) = a.q4 ? k_tc_gemm<kDeqGroups> : k_tc_gemm<kF16DeqGroups>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
@@ -728,3 +743,16 @@ int launch_splits_to_f16(const float* part, int splits, int nb_valid, int n_rows
 }
 
 }  // namespace qwen
+
+// Test hook (not part of the public header): the plan launch_tc_gemm would use
+// for nb activation rows and cps chunks per CTA, as {unit, stages, xstages,
+// raw_stages, mma_warps, dequant groups, shared memory bytes}.  Host
+// arithmetic only.  Returns 0, or -1 when no plan fits shared memory.
+extern "C" int qwen_tc_gemm_plan(int nb, int q4, int cps, long long* out7) {
+  if (!out7 || nb < 16 || nb > qwen::kTcMaxNb || nb % 16 || cps < 1) return -1;
+  const auto pl = qwen::tc_gemm_plan(nb, q4 != 0, cps);
+  const long long v[7] = {pl.unit, pl.stages, pl.xstages, pl.raw_stages, pl.mma_warps, pl.groups,
+                          (long long)pl.smem};
+  for (int i = 0; i < 7; ++i) out7[i] = v[i];
+  return pl.smem <= qwen::kTcSmemBudget ? 0 : -1;
+}
