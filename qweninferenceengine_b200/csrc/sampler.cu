@@ -2,9 +2,11 @@
 // InferenceEngine.swift:273-368) as a radix select over a thread-block cluster.
 //
 // One cluster of 8 CTAs per sequence; CTA r owns ids [r*chunk, (r+1)*chunk)
-// and keeps their fixed-point weights in shared memory.  Cluster-wide
-// reductions go through distributed shared memory (hardware cluster barriers,
-// no spin loops).
+// and keeps their fixed-point weights in shared memory.  The maximum and the
+// final count go through distributed shared memory behind hardware cluster
+// barriers; the radix passes' digit totals are pushed into every CTA's shared
+// memory with st.async and awaited on a transaction-count mbarrier (a bounded
+// wait that records kDevWaitTimeout in err when it gives up).
 //
 // Rule (the reference's steps with every order-dependent quantity exact):
 //   greedy (T <= 0): first maximum over non-NaN logits; none -> 151645 (:277-294)
@@ -15,6 +17,9 @@
 //   keep the shortest prefix with sum >= thr = floor(S * trunc(p*2^24) / 2^24) (:339-351)
 //   R = floor(K * u24 / 2^24), K = kept sum; first kept id with running sum > R (:353-367)
 // Both selections run as 4-pass weighted radix selects (8-bit digits) on E.
+// The cutoff select's first pass is histogrammed while the weights are made
+// (S is the sum of its totals); the draw's passes take their totals from the
+// cutoff select's while the two prefixes agree, and scan only after they part.
 #include <cooperative_groups.h>
 
 #include "qwen_common.cuh"
@@ -63,15 +68,17 @@ struct SampShared {
   // E >> 16): a warp sees at most 19 * 32 elements, so each half fits 32 bits.
   uint32_t whist[kSampWarps][2][256];
   unsigned long long qsum[4][256];           // quarter-block merges of whist
-  unsigned long long hsum[4][256];           // this CTA's digit weights, read by the cluster
+  unsigned long long inbox[2][kSampCluster][256];  // each rank's digit weights, pushed by that rank
+  uint64_t xbar[2];                          // inbox barriers (transaction bytes)
   unsigned long long tot[256];               // cluster totals of the running pass
+  unsigned long long tot1[4][256];           // the nucleus select's totals per pass
+  unsigned long long above1[4];              // its weight above the prefix after each pass
   float red_f[32];
   int red_i[32];
   unsigned long long red_u[32];
   uint32_t red_c[32];
   float cl_f[kSampCluster];                  // per-CTA partials read by the cluster
   int cl_i;
-  unsigned long long cl_u;
   uint32_t cl_cnt;
   uint32_t sel;
   unsigned long long sel_above;
@@ -111,122 +118,134 @@ __device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SampShared& 
   return v + s.red_c[w];
 }
 
-// Weighted radix select over E (descending order), 4 passes of 8-bit digits.
-// Members: every E (restrict_kept false), or E > e_star plus a virtual weight
-// tie_weight at value e_star (restrict_kept true).  Returns the value at which
-// the running weight from the top first reaches `target`, and the weight
-// strictly above that value.  `buf0` picks this select's pair of cluster
-// exchange buffers (a fresh pair per select, so no select waits for the
-// previous one's remote readers).
-struct SelectResult {
-  uint32_t value;
-  unsigned long long above;
-};
+// Weighted radix selects over E (descending order), 4 passes of 8-bit digits.
+// A pass histograms the members' weights by digit (per warp, two exact 32-bit
+// halves), sums the histograms over the cluster, and picks the digit at which
+// the running weight from the top first reaches the target.
 
-__device__ SelectResult radix_select(SampShared& s, cg::cluster_group& cluster, int n_local,
-                                     unsigned long long target, bool restrict_kept,
-                                     uint32_t e_star, unsigned long long tie_weight, int buf0) {
-  uint32_t prefix = 0, mask = 0;
-  unsigned long long above = 0;
+// Zeroes this warp's digit histogram.
+__device__ __forceinline__ void hist_clear(SampShared& s) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    const int buf = buf0 + (pass & 1);
-    uint32_t* hlo = s.whist[wid][0];
-    uint32_t* hhi = s.whist[wid][1];
 #pragma unroll
-    for (int d = lane; d < 256; d += 32) hlo[d] = hhi[d] = 0;
-    __syncwarp();
-    // Zero weights change no sum, so they are skipped.  When every member of a
-    // warp falls in one digit (peaked distributions put almost all weights in
-    // digit 0 of the upper passes) the warp reduces first and adds once.
-    for (int k = 0; k < kSampPerThread; ++k) {
-      const int i = k * kSampThreads + (int)threadIdx.x;
-      const uint32_t e = i < n_local ? s.e[i] : 0u;
-      const bool member = e != 0u && (e & mask) == prefix && !(restrict_kept && e <= e_star);
-      const uint32_t d = (e >> shift) & 255u;
-      const uint32_t mm = __ballot_sync(0xffffffffu, member);
-      if (mm == 0u) continue;
-      const uint32_t d0 = __shfl_sync(0xffffffffu, d, __ffs(mm) - 1);
-      if (__all_sync(0xffffffffu, !member || d == d0)) {
-        const uint32_t lo = __reduce_add_sync(0xffffffffu, member ? (e & 0xFFFFu) : 0u);
-        const uint32_t hi = __reduce_add_sync(0xffffffffu, member ? (e >> 16) : 0u);
-        if (lane == 0) {
-          atomicAdd(&hlo[d0], lo);
-          atomicAdd(&hhi[d0], hi);
-        }
-      } else if (member) {
-        atomicAdd(&hlo[d], e & 0xFFFFu);
-        atomicAdd(&hhi[d], e >> 16);
-      }
+  for (int d = lane; d < 256; d += 32) s.whist[wid][0][d] = s.whist[wid][1][d] = 0;
+  __syncwarp();
+}
+
+// Adds weight e at digit d to this warp's histogram for each lane that is a
+// member.  Zero weights change no sum, so callers pass them as non-members.
+// When every member of the warp falls in one digit (peaked distributions put
+// almost all weights in digit 0 of the later passes) the warp reduces first
+// and adds once.  (Partitioning the warp by digit with match.any before the
+// adds measured slower on flat distributions than the colliding atomics.)
+__device__ __forceinline__ void hist_add(SampShared& s, bool member, uint32_t e, uint32_t d) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint32_t* hlo = s.whist[wid][0];
+  uint32_t* hhi = s.whist[wid][1];
+  const uint32_t mm = __ballot_sync(0xffffffffu, member);
+  if (mm == 0u) return;
+  const uint32_t d0 = __shfl_sync(0xffffffffu, d, __ffs(mm) - 1);
+  if (__all_sync(0xffffffffu, !member || d == d0)) {
+    const uint32_t lo = __reduce_add_sync(0xffffffffu, member ? (e & 0xFFFFu) : 0u);
+    const uint32_t hi = __reduce_add_sync(0xffffffffu, member ? (e >> 16) : 0u);
+    if (lane == 0) {
+      atomicAdd(&hlo[d0], lo);
+      atomicAdd(&hhi[d0], hi);
     }
-    __syncthreads();
-    {
-      const int d = threadIdx.x & 255, q = threadIdx.x >> 8;
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int w = 0; w < kSampWarps / 4; ++w) {
-        lo += s.whist[q * (kSampWarps / 4) + w][0][d];
-        hi += s.whist[q * (kSampWarps / 4) + w][1][d];
-      }
-      s.qsum[q][d] = ((unsigned long long)hi << 16) + lo;
-    }
-    __syncthreads();
-    if (threadIdx.x < 256) {
-      const int d = threadIdx.x;
-      s.hsum[buf][d] = s.qsum[0][d] + s.qsum[1][d] + s.qsum[2][d] + s.qsum[3][d];
-    }
-    cluster.sync();
-    // Cluster totals per digit (every CTA computes the same).
-    if (threadIdx.x < 256) {
-      const int d = threadIdx.x;
-      unsigned long long part[kSampCluster];
-#pragma unroll
-      for (int r = 0; r < kSampCluster; ++r) part[r] = cluster.map_shared_rank(&s, r)->hsum[buf][d];
-      unsigned long long sum = 0;
-#pragma unroll
-      for (int r = 0; r < kSampCluster; ++r) sum += part[r];
-      if (restrict_kept && (e_star & mask) == prefix && (uint32_t)d == ((e_star >> shift) & 255u))
-        sum += tie_weight;
-      s.tot[d] = sum;
-    }
-    __syncthreads();
-    // Selected digit: the largest d with above + sum(tot[d..255]) >= target
-    // (digit 0 when the total falls short).  One warp: lane l holds digits
-    // 255-8l .. 248-8l in descending order.
-    if (wid == 0) {
-      unsigned long long v[8], mine = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        v[j] = s.tot[255 - 8 * lane - j];
-        mine += v[j];
-      }
-      unsigned long long incl = mine;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const uint32_t hit = __ballot_sync(0xffffffffu, above + incl >= target);
-      const int L = hit ? __ffs(hit) - 1 : 31;
-      if (lane == L) {
-        unsigned long long run = above + incl - mine;
-        int j = 0;
-        for (; j < 7; ++j) {
-          if (run + v[j] >= target) break;
-          run += v[j];
-        }
-        s.sel = (uint32_t)(255 - 8 * lane - j);
-        s.sel_above = run;
-      }
-    }
-    __syncthreads();
-    const uint32_t sel = s.sel;
-    prefix |= sel << shift;
-    mask |= 255u << shift;
-    above = s.sel_above;
+  } else if (member) {
+    atomicAdd(&hlo[d], e & 0xFFFFu);
+    atomicAdd(&hhi[d], e >> 16);
   }
-  return SelectResult{prefix, above};
+}
+
+// Cluster totals of exchange n into s.tot.  Every CTA merges its warp
+// histograms and pushes the 256 sums into inbox[n & 1][its rank] of every CTA
+// of the cluster (itself included) with st.async, which completes transaction
+// bytes on the receiver's xbar[n & 1]; each CTA then waits for the 8 ranks'
+// bytes and sums them in rank order (so every CTA holds the same totals).
+// A CTA pushes exchange n + 2 only after it has received exchange n + 1 from
+// every rank, which each rank sends after it has read its inbox of exchange
+// n: two inboxes suffice.  A push may land before the receiver's expect_tx of
+// that exchange; the phase cannot complete before the receiver's own arrival.
+__device__ void hist_totals(SampShared& s, int rank, uint32_t n, int* err) {
+  __syncthreads();
+  {
+    const int d = threadIdx.x & 255, q = threadIdx.x >> 8;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int w = 0; w < kSampWarps / 4; ++w) {
+      lo += s.whist[q * (kSampWarps / 4) + w][0][d];
+      hi += s.whist[q * (kSampWarps / 4) + w][1][d];
+    }
+    s.qsum[q][d] = ((unsigned long long)hi << 16) + lo;
+  }
+  __syncthreads();
+  const int buf = n & 1;
+  if (threadIdx.x == 0)
+    mbar_arrive_expect_tx(&s.xbar[buf], (uint32_t)(kSampCluster * 256 * sizeof(unsigned long long)));
+  if (threadIdx.x < 256) {
+    const int d = threadIdx.x;
+    const unsigned long long h = s.qsum[0][d] + s.qsum[1][d] + s.qsum[2][d] + s.qsum[3][d];
+    const uint32_t src = smem_u32(&s.inbox[buf][rank][d]), bar = smem_u32(&s.xbar[buf]);
+#pragma unroll
+    for (int r = 0; r < kSampCluster; ++r) {
+      uint32_t rdst, rbar;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(src), "r"(r));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(bar), "r"(r));
+      asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u64 [%0], %1, [%2];"
+                   ::"r"(rdst), "l"(h), "r"(rbar) : "memory");
+    }
+    const uint32_t parity = (n >> 1) & 1;
+    uint32_t ok = 0;
+    for (uint32_t it = 0; it < (1u << 22) && !ok; ++it)
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(ok)
+          : "r"(bar), "r"(parity)
+          : "memory");
+    if (!ok) raise_error(err, kDevWaitTimeout);
+    unsigned long long sum = 0;
+#pragma unroll
+    for (int r = 0; r < kSampCluster; ++r) sum += s.inbox[buf][r][d];
+    s.tot[d] = sum;
+  }
+  __syncthreads();
+}
+
+// Selected digit of the pass: the largest d with above + sum(tot[d..255]) >=
+// target (digit 0 when the total falls short) into s.sel, and the weight of
+// the digits above it plus `above` into s.sel_above.  One warp: lane l holds
+// digits 255-8l .. 248-8l in descending order.
+__device__ void pick_digit(SampShared& s, unsigned long long above, unsigned long long target) {
+  const int lane = threadIdx.x & 31;
+  if ((threadIdx.x >> 5) == 0) {
+    unsigned long long v[8], mine = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = s.tot[255 - 8 * lane - j];
+      mine += v[j];
+    }
+    unsigned long long incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t hit = __ballot_sync(0xffffffffu, above + incl >= target);
+    const int L = hit ? __ffs(hit) - 1 : 31;
+    if (lane == L) {
+      unsigned long long run = above + incl - mine;
+      int j = 0;
+      for (; j < 7; ++j) {
+        if (run + v[j] >= target) break;
+        run += v[j];
+      }
+      s.sel = (uint32_t)(255 - 8 * lane - j);
+      s.sel_above = run;
+    }
+  }
+  __syncthreads();
 }
 
 __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThreads)
@@ -242,6 +261,11 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   const int chunk = (vocab + kSampCluster - 1) / kSampCluster;
   const int lo = rank * chunk;
   const int n_local = max(0, min(vocab, lo + chunk) - lo);
+  if (threadIdx.x == 0) {   // visible to the cluster after the first cluster.sync below
+    mbar_init(&s.xbar[0], 1);
+    mbar_init(&s.xbar[1], 1);
+    fence_mbar_init();
+  }
 
   // ---- greedy ---------------------------------------------------------
   if (!(temperature > 0.0f)) {
@@ -322,46 +346,99 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
     cluster.sync();
     return;
   }
-  // ---- fixed-point weights + sum ---------------------------------------
-  unsigned long long part = 0;
+  // ---- fixed-point weights, histogrammed by their first digit -----------
+  // The first pass of the nucleus select needs every weight, so it is built
+  // here; the total S is the sum of its cluster totals.
+  hist_clear(s);
 #pragma unroll
   for (int k = 0; k < kSampPerThread; ++k) {
     const int i = k * kSampThreads + (int)threadIdx.x;
+    uint32_t E = 0u;
     if (i < n_local) {
       const float e = sampler_exp(__fsub_rn(sc[k], M));
-      const uint32_t E = __float2uint_rz(__fmul_rn(e, 2147483648.0f));
+      E = __float2uint_rz(__fmul_rn(e, 2147483648.0f));
       s.e[i] = E;
-      part += E;
     }
+    hist_add(s, E != 0u, E, E >> 24);
   }
-  part = block_sum_u64(part, s);
-  if (threadIdx.x == 0) s.cl_u = part;
-  cluster.sync();
-  __shared__ unsigned long long s_S;
-  if (threadIdx.x == 0) {
-    unsigned long long t = 0;
-    for (int r = 0; r < kSampCluster; ++r) t += cluster.map_shared_rank(&s, r)->cl_u;
-    s_S = t;
-  }
-  __syncthreads();
-  const unsigned long long S = s_S;
+  uint32_t xn = 0;   // exchanges so far
+  hist_totals(s, rank, xn++, err);
+  const unsigned long long S = block_sum_u64(threadIdx.x < 256 ? s.tot[threadIdx.x] : 0ull, s);
   const float pc = fminf(fmaxf(top_p, 0.0f), 1.0f);
   const uint32_t p24 = (uint32_t)__float2uint_rz(__fmul_rn(pc, 16777216.0f));
   unsigned long long thr = mul_shift24(S, p24);
   if (thr == 0) thr = 1;
 
-  // ---- nucleus cutoff ----------------------------------------------------
-  const SelectResult c1 = radix_select(s, cluster, n_local, thr, false, 0, 0, 0);
-  const uint32_t e_star = c1.value;
-  const unsigned long long need = thr - c1.above;
+  // ---- nucleus cutoff: the value e_star where the weight from the top first
+  // reaches thr, and the weight strictly above it ------------------------------
+  uint32_t prefix = 0, mask = 0;
+  unsigned long long above = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    if (pass > 0) {
+      hist_clear(s);
+#pragma unroll
+      for (int k = 0; k < kSampPerThread; ++k) {
+        const int i = k * kSampThreads + (int)threadIdx.x;
+        const uint32_t e = i < n_local ? s.e[i] : 0u;
+        hist_add(s, e != 0u && (e & mask) == prefix, e, (e >> shift) & 255u);
+      }
+      hist_totals(s, rank, xn++, err);
+    }
+    if (threadIdx.x < 256) s.tot1[pass][threadIdx.x] = s.tot[threadIdx.x];
+    pick_digit(s, above, thr);
+    prefix |= s.sel << shift;
+    mask |= 255u << shift;
+    above = s.sel_above;
+    if (threadIdx.x == 0) s.above1[pass] = above;
+  }
+  const uint32_t e_star = prefix;
+  const unsigned long long above_star = above;   // weight of E > e_star
+  const unsigned long long need = thr - above_star;
   const unsigned long long k_tie = (need + e_star - 1) / e_star;  // e_star >= 1
-  const unsigned long long kept = c1.above + k_tie * e_star;
+  const unsigned long long kept = above_star + k_tie * e_star;
 
-  // ---- draw ----------------------------------------------------------------
+  // ---- draw: the same select over the kept set (E > e_star, plus k_tie
+  // copies of e_star as one weight at e_star) for R + 1 ----------------------
+  // While the draw's prefix equals e_star's, its digit totals follow from the
+  // nucleus select's: above e_star's digit they are the same members; at that
+  // digit they are the weight above e_star not yet counted above the prefix,
+  // plus the tie weight; below it there are none.  Only passes after the
+  // prefixes part scan the weights (and those members all exceed e_star).
   const unsigned long long R = mul_shift24(kept, u24[seq] & 0xFFFFFFu);
-  const SelectResult c2 = radix_select(s, cluster, n_local, R + 1, true, e_star, k_tie * e_star, 2);
-  const uint32_t e2 = c2.value;
-  const unsigned long long j = (R - c2.above) / e2;   // index inside the tie group (id order)
+  prefix = 0;
+  mask = 0;
+  above = 0;
+  bool on_star = true;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t ds = (e_star >> shift) & 255u;
+    if (on_star) {
+      if (threadIdx.x < 256) {
+        const uint32_t d = threadIdx.x;
+        s.tot[d] = d > ds ? s.tot1[pass][d]
+                 : d == ds ? (above_star - s.above1[pass]) + k_tie * e_star : 0ull;
+      }
+      __syncthreads();
+    } else {
+      hist_clear(s);
+#pragma unroll
+      for (int k = 0; k < kSampPerThread; ++k) {
+        const int i = k * kSampThreads + (int)threadIdx.x;
+        const uint32_t e = i < n_local ? s.e[i] : 0u;
+        hist_add(s, e > e_star && (e & mask) == prefix, e, (e >> shift) & 255u);
+      }
+      hist_totals(s, rank, xn++, err);
+    }
+    pick_digit(s, above, R + 1);
+    const uint32_t sel = s.sel;
+    on_star = on_star && sel == ds;
+    prefix |= sel << shift;
+    mask |= 255u << shift;
+    above = s.sel_above;
+  }
+  const uint32_t e2 = prefix;
+  const unsigned long long j = (R - above) / e2;   // index inside the tie group (id order)
 
   // ---- j-th smallest id with E == e2 ---------------------------------------
   // Threads own contiguous id ranges so that block order = id order.
