@@ -462,6 +462,7 @@ int QwenEngine::ensure_graph() {
     state_.fused_scratch_bytes = bytes;
   }
   if (cfg_.kernels == QWEN_KERNELS_TC) QWEN_TRY(tc_state_allocate(state_, sm_count_));
+  sampler_prepare();
   QWEN_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "BeginCapture");
   const int rc = enqueue_step(nullptr);
   cudaGraph_t g = nullptr;

@@ -63,6 +63,9 @@ int launch_dequant_q4(const uint8_t* packed, const __half* scales, size_t n_weig
 // Deterministic sampler (greedy when temperature <= 0).  scratch: see
 // sampler_scratch_bytes.
 size_t sampler_scratch_bytes(int n_seq);
+// Host set-up of the sampler for the current device (cluster-size query); call
+// before capturing a launch_sample into a CUDA graph.
+void sampler_prepare();
 int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
                   float top_p, const uint32_t* u24, int32_t* out_ids, void* scratch,
                   int* err, cudaStream_t st);

@@ -1,8 +1,9 @@
 // sampler.cu -- on-device token sampler (extractNextTokenID,
 // InferenceEngine.swift:273-368) as a radix select over a thread-block cluster.
 //
-// One cluster of 8 CTAs per sequence; CTA r owns ids [r*chunk, (r+1)*chunk)
-// and keeps their fixed-point weights in shared memory.  The maximum and the
+// One cluster of C CTAs per sequence (C = 16 when the batch fits in one wave
+// of 16-CTA clusters, else 8); CTA r owns ids [r*chunk, (r+1)*chunk) and keeps
+// their fixed-point weights in shared memory.  The maximum and the
 // final count go through distributed shared memory behind hardware cluster
 // barriers; the radix passes' digit totals are pushed into every CTA's shared
 // memory with st.async and awaited on a transaction-count mbarrier (a bounded
@@ -29,9 +30,7 @@ namespace cg = cooperative_groups;
 
 namespace qwen {
 
-constexpr int kSampCluster = 8;
 constexpr int kSampThreads = 1024;
-constexpr int kSampMaxChunk = (kVocab + kSampCluster - 1) / kSampCluster;  // 18992
 
 // exp for the sampler: Cody-Waite reduction with the two-part ln2 split of
 // Cephes expf, degree-7 Taylor polynomial in Horner form with fused
@@ -60,15 +59,19 @@ __device__ __forceinline__ unsigned long long mul_shift24(unsigned long long a, 
 }
 
 constexpr int kSampWarps = kSampThreads / 32;
-constexpr int kSampPerThread = (kSampMaxChunk + kSampThreads - 1) / kSampThreads;  // 19
 
+// Shared memory of one CTA of a C-CTA cluster (C = 8 or 16).
+template <int C>
 struct SampShared {
-  uint32_t e[kSampMaxChunk];                 // scaled floats, then fixed-point weights
+  static constexpr int kC = C;
+  static constexpr int kChunk = (kVocab + C - 1) / C;                           // 18992 / 9496
+  static constexpr int kPerThread = (kChunk + kSampThreads - 1) / kSampThreads;  // 19 / 10
+  uint32_t e[kChunk];                        // scaled floats, then fixed-point weights
   // Per-warp digit weights of the running pass as two exact halves (E & 0xFFFF,
   // E >> 16): a warp sees at most 19 * 32 elements, so each half fits 32 bits.
   uint32_t whist[kSampWarps][2][256];
   unsigned long long qsum[4][256];           // quarter-block merges of whist
-  unsigned long long inbox[2][kSampCluster][256];  // each rank's digit weights, pushed by that rank
+  unsigned long long inbox[2][C][256];       // each rank's digit weights, pushed by that rank
   uint64_t xbar[2];                          // inbox barriers (transaction bytes)
   unsigned long long tot[256];               // cluster totals of the running pass
   unsigned long long tot1[4][256];           // the nucleus select's totals per pass
@@ -77,14 +80,15 @@ struct SampShared {
   int red_i[32];
   unsigned long long red_u[32];
   uint32_t red_c[32];
-  float cl_f[kSampCluster];                  // per-CTA partials read by the cluster
+  float cl_f[C];                             // per-CTA partials read by the cluster
   int cl_i;
   uint32_t cl_cnt;
   uint32_t sel;
   unsigned long long sel_above;
 };
 
-__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, SampShared& s) {
+template <class SS>
+__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, SS& s) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5;
   __syncthreads();
@@ -96,7 +100,8 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
 }
 
 // Inclusive prefix sum of one value per thread over the block (thread order).
-__device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SampShared& s) {
+template <class SS>
+__device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SS& s) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -124,7 +129,8 @@ __device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SampShared& 
 // the running weight from the top first reaches the target.
 
 // Zeroes this warp's digit histogram.
-__device__ __forceinline__ void hist_clear(SampShared& s) {
+template <class SS>
+__device__ __forceinline__ void hist_clear(SS& s) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
   for (int d = lane; d < 256; d += 32) s.whist[wid][0][d] = s.whist[wid][1][d] = 0;
@@ -137,7 +143,8 @@ __device__ __forceinline__ void hist_clear(SampShared& s) {
 // almost all weights in digit 0 of the later passes) the warp reduces first
 // and adds once.  (Partitioning the warp by digit with match.any before the
 // adds measured slower on flat distributions than the colliding atomics.)
-__device__ __forceinline__ void hist_add(SampShared& s, bool member, uint32_t e, uint32_t d) {
+template <class SS>
+__device__ __forceinline__ void hist_add(SS& s, bool member, uint32_t e, uint32_t d) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   uint32_t* hlo = s.whist[wid][0];
   uint32_t* hhi = s.whist[wid][1];
@@ -160,13 +167,14 @@ __device__ __forceinline__ void hist_add(SampShared& s, bool member, uint32_t e,
 // Cluster totals of exchange n into s.tot.  Every CTA merges its warp
 // histograms and pushes the 256 sums into inbox[n & 1][its rank] of every CTA
 // of the cluster (itself included) with st.async, which completes transaction
-// bytes on the receiver's xbar[n & 1]; each CTA then waits for the 8 ranks'
+// bytes on the receiver's xbar[n & 1]; each CTA then waits for the C ranks'
 // bytes and sums them in rank order (so every CTA holds the same totals).
 // A CTA pushes exchange n + 2 only after it has received exchange n + 1 from
 // every rank, which each rank sends after it has read its inbox of exchange
 // n: two inboxes suffice.  A push may land before the receiver's expect_tx of
 // that exchange; the phase cannot complete before the receiver's own arrival.
-__device__ void hist_totals(SampShared& s, int rank, uint32_t n, int* err) {
+template <class SS>
+__device__ void hist_totals(SS& s, int rank, uint32_t n, int* err) {
   __syncthreads();
   {
     const int d = threadIdx.x & 255, q = threadIdx.x >> 8;
@@ -181,13 +189,13 @@ __device__ void hist_totals(SampShared& s, int rank, uint32_t n, int* err) {
   __syncthreads();
   const int buf = n & 1;
   if (threadIdx.x == 0)
-    mbar_arrive_expect_tx(&s.xbar[buf], (uint32_t)(kSampCluster * 256 * sizeof(unsigned long long)));
+    mbar_arrive_expect_tx(&s.xbar[buf], (uint32_t)(SS::kC * 256 * sizeof(unsigned long long)));
   if (threadIdx.x < 256) {
     const int d = threadIdx.x;
     const unsigned long long h = s.qsum[0][d] + s.qsum[1][d] + s.qsum[2][d] + s.qsum[3][d];
     const uint32_t src = smem_u32(&s.inbox[buf][rank][d]), bar = smem_u32(&s.xbar[buf]);
 #pragma unroll
-    for (int r = 0; r < kSampCluster; ++r) {
+    for (int r = 0; r < SS::kC; ++r) {
       uint32_t rdst, rbar;
       asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(src), "r"(r));
       asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(bar), "r"(r));
@@ -207,7 +215,7 @@ __device__ void hist_totals(SampShared& s, int rank, uint32_t n, int* err) {
     if (!ok) raise_error(err, kDevWaitTimeout);
     unsigned long long sum = 0;
 #pragma unroll
-    for (int r = 0; r < kSampCluster; ++r) sum += s.inbox[buf][r][d];
+    for (int r = 0; r < SS::kC; ++r) sum += s.inbox[buf][r][d];
     s.tot[d] = sum;
   }
   __syncthreads();
@@ -217,7 +225,8 @@ __device__ void hist_totals(SampShared& s, int rank, uint32_t n, int* err) {
 // target (digit 0 when the total falls short) into s.sel, and the weight of
 // the digits above it plus `above` into s.sel_above.  One warp: lane l holds
 // digits 255-8l .. 248-8l in descending order.
-__device__ void pick_digit(SampShared& s, unsigned long long above, unsigned long long target) {
+template <class SS>
+__device__ void pick_digit(SS& s, unsigned long long above, unsigned long long target) {
   const int lane = threadIdx.x & 31;
   if ((threadIdx.x >> 5) == 0) {
     unsigned long long v[8], mine = 0;
@@ -248,17 +257,20 @@ __device__ void pick_digit(SampShared& s, unsigned long long above, unsigned lon
   __syncthreads();
 }
 
-__global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThreads)
+template <int C>
+__global__ void __launch_bounds__(kSampThreads)
     k_sample(const __half* __restrict__ logits, int row_stride, int vocab, float temperature,
              float top_p, const uint32_t* __restrict__ u24, int32_t* __restrict__ out_ids,
              int* err) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  SampShared& s = *reinterpret_cast<SampShared*>(smem_raw);
+  using SS = SampShared<C>;
+  constexpr int kSampPerThread = SS::kPerThread;
+  SS& s = *reinterpret_cast<SS*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int seq = blockIdx.y;
   const __half* lg = logits + (size_t)seq * row_stride;
-  const int chunk = (vocab + kSampCluster - 1) / kSampCluster;
+  const int chunk = (vocab + C - 1) / C;
   const int lo = rank * chunk;
   const int n_local = max(0, min(vocab, lo + chunk) - lo);
   if (threadIdx.x == 0) {   // visible to the cluster after the first cluster.sync below
@@ -295,8 +307,8 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
     }
     cluster.sync();
     if (rank == 0 && threadIdx.x == 0) {
-      for (int r = 1; r < kSampCluster; ++r) {
-        SampShared* rs = cluster.map_shared_rank(&s, r);
+      for (int r = 1; r < C; ++r) {
+        SS* rs = cluster.map_shared_rank(&s, r);
         const float v = rs->cl_f[0];
         const int i = rs->cl_i;
         if (v > best || (v == best && i < idx)) { best = v; idx = i; }
@@ -336,7 +348,7 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
   __shared__ float s_M;
   if (threadIdx.x == 0) {
     float m = -INFINITY;
-    for (int r = 0; r < kSampCluster; ++r) m = fmaxf(m, cluster.map_shared_rank(&s, r)->cl_f[0]);
+    for (int r = 0; r < C; ++r) m = fmaxf(m, cluster.map_shared_rank(&s, r)->cl_f[0]);
     s_M = m;
   }
   __syncthreads();
@@ -471,16 +483,80 @@ __global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThre
 
 size_t sampler_scratch_bytes(int) { return 0; }
 
+template <int C>
+static int launch_sample_c(const __half* logits, int n_seq, int row_stride, int vocab,
+                           float temperature, float top_p, const uint32_t* u24, int32_t* out_ids,
+                           int* err, cudaStream_t st) {
+  const size_t smem = sizeof(SampShared<C>);
+  cudaFuncSetAttribute(k_sample<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (C > 8) cudaFuncSetAttribute(k_sample<C>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, n_seq);
+  cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_sample<C>, logits, row_stride, vocab, temperature, top_p, u24,
+                            out_ids, err) == cudaSuccess ? 0 : -1;
+}
+
+// 16-CTA clusters (half the ids per CTA) for batches that fit in one wave of
+// them; 8-CTA clusters otherwise.  16 is a non-portable cluster size: how many
+// such clusters fit at once is asked of the occupancy calculator, once per
+// device (sampler_prepare asks it ahead of a stream capture).
+static int wide_clusters(int dev) {
+  static int cached[64];
+  static bool known[64];
+  if (dev < 0 || dev >= 64) return 0;
+  if (!known[dev]) {
+    int n = 0;
+    const size_t smem = sizeof(SampShared<16>);
+    if (cudaFuncSetAttribute(k_sample<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+            cudaSuccess &&
+        cudaFuncSetAttribute(k_sample<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+            cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(16, 1);
+      cfg.blockDim = dim3(kSampThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 16;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, k_sample<16>, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();   // a refused query leaves no error behind for the next launch check
+    cached[dev] = n;
+    known[dev] = true;
+  }
+  return cached[dev];
+}
+
+void sampler_prepare() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) wide_clusters(dev);
+}
+
 int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
                   float top_p, const uint32_t* u24, int32_t* out_ids, void*, int* err,
                   cudaStream_t st) {
   if (vocab <= 0 || vocab > kVocab || n_seq <= 0) return -1;
-  const size_t smem = sizeof(SampShared);
-  cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid(kSampCluster, n_seq);
-  k_sample<<<grid, kSampThreads, smem, st>>>(logits, row_stride, vocab, temperature, top_p, u24,
-                                             out_ids, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (n_seq <= wide_clusters(dev))
+    return launch_sample_c<16>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
+                               err, st);
+  return launch_sample_c<8>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
+                            err, st);
 }
 
 }  // namespace qwen

@@ -178,3 +178,19 @@ def test_sampler_top_p_bitexact(cuda, oracle, temp, top_p):
     got = N(ops.sample(T(lg), temp, top_p, T(u.view(np.int32))))
     want = [oracle.sample_top_p(lg[i], temp, top_p, int(u[i])) for i in range(n)]
     assert got.tolist() == want
+
+
+@pytest.mark.parametrize("n", [1, 3, 64])
+def test_sampler_batch_sizes_bitexact(cuda, oracle, n):
+    """Small batches run on 16-CTA clusters, large ones on 8-CTA clusters: both
+    draw the oracle's ids (flat and peaked rows, u24 at both ends)."""
+    rng = np.random.default_rng(100 + n)
+    lg = (rng.standard_normal((n, 151936)) * rng.uniform(0.1, 5, size=(n, 1))).astype(np.float16)
+    u = np.array([oracle.uniform24(11, i, 5) for i in range(n)], np.uint32)
+    u[0] = (1 << 24) - 1
+    if n > 1:
+        u[1] = 0
+    for temp, top_p in ((0.7, 0.8), (1.0, 0.95)):
+        got = N(ops.sample(T(lg), temp, top_p, T(u.view(np.int32))))
+        want = [oracle.sample_top_p(lg[i], temp, top_p, int(u[i])) for i in range(n)]
+        assert got.tolist() == want
