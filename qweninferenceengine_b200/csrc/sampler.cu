@@ -1,8 +1,8 @@
 // sampler.cu -- on-device token sampler (extractNextTokenID,
 // InferenceEngine.swift:273-368) as a radix select over a thread-block cluster.
 //
-// One cluster of C CTAs per sequence (C = 16 when the batch fits in one wave
-// of 16-CTA clusters, else 8); CTA r owns ids [r*chunk, (r+1)*chunk) and keeps
+// One cluster of C CTAs per sequence (C = 16, 8 or 4: the largest whose one
+// wave of clusters holds the batch, else 4); CTA r owns ids [r*chunk, (r+1)*chunk) and keeps
 // their fixed-point weights in shared memory.  The maximum and the
 // final count go through distributed shared memory behind hardware cluster
 // barriers; the radix passes' digit totals are pushed into every CTA's shared
@@ -60,16 +60,20 @@ __device__ __forceinline__ unsigned long long mul_shift24(unsigned long long a, 
 
 constexpr int kSampWarps = kSampThreads / 32;
 
-// Shared memory of one CTA of a C-CTA cluster (C = 8 or 16).
+// Shared memory of one CTA of a C-CTA cluster (C = 4, 8 or 16).
 template <int C>
 struct SampShared {
   static constexpr int kC = C;
-  static constexpr int kChunk = (kVocab + C - 1) / C;                           // 18992 / 9496
-  static constexpr int kPerThread = (kChunk + kSampThreads - 1) / kSampThreads;  // 19 / 10
+  static constexpr int kChunk = (kVocab + C - 1) / C;                           // 37984 / 18992 / 9496
+  static constexpr int kPerThread = (kChunk + kSampThreads - 1) / kSampThreads;  // 38 / 19 / 10
+  // One digit histogram per warp, or per pair of warps when the CTA's weights
+  // take most of shared memory (C = 4).
+  static constexpr int kHist = C >= 8 ? kSampWarps : kSampWarps / 2;
+  static constexpr int kWarpsPerHist = kSampWarps / kHist;
   uint32_t e[kChunk];                        // scaled floats, then fixed-point weights
-  // Per-warp digit weights of the running pass as two exact halves (E & 0xFFFF,
-  // E >> 16): a warp sees at most 19 * 32 elements, so each half fits 32 bits.
-  uint32_t whist[kSampWarps][2][256];
+  // Digit weights of the running pass as two exact halves (E & 0xFFFF, E >> 16):
+  // a histogram sees at most 2 * 38 * 32 elements, so each half fits 32 bits.
+  uint32_t whist[kHist][2][256];
   unsigned long long qsum[4][256];           // quarter-block merges of whist
   unsigned long long inbox[2][C][256];       // each rank's digit weights, pushed by that rank
   uint64_t xbar[2];                          // inbox barriers (transaction bytes)
@@ -86,6 +90,8 @@ struct SampShared {
   uint32_t sel;
   unsigned long long sel_above;
 };
+
+static_assert(sizeof(SampShared<4>) <= 232448, "4-CTA sampler layout exceeds shared memory");
 
 template <class SS>
 __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, SS& s) {
@@ -128,13 +134,20 @@ __device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SS& s) {
 // halves), sums the histograms over the cluster, and picks the digit at which
 // the running weight from the top first reaches the target.
 
-// Zeroes this warp's digit histogram.
+// Zeroes the digit histograms: each warp its own, or the whole block (and a
+// block barrier) when warps share them.
 template <class SS>
 __device__ __forceinline__ void hist_clear(SS& s) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if constexpr (SS::kWarpsPerHist == 1) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
-  for (int d = lane; d < 256; d += 32) s.whist[wid][0][d] = s.whist[wid][1][d] = 0;
-  __syncwarp();
+    for (int d = lane; d < 256; d += 32) s.whist[wid][0][d] = s.whist[wid][1][d] = 0;
+    __syncwarp();
+  } else {
+    uint32_t* h = &s.whist[0][0][0];
+    for (int i = threadIdx.x; i < SS::kHist * 512; i += kSampThreads) h[i] = 0;
+    __syncthreads();
+  }
 }
 
 // Adds weight e at digit d to this warp's histogram for each lane that is a
@@ -145,7 +158,7 @@ __device__ __forceinline__ void hist_clear(SS& s) {
 // adds measured slower on flat distributions than the colliding atomics.)
 template <class SS>
 __device__ __forceinline__ void hist_add(SS& s, bool member, uint32_t e, uint32_t d) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, wid = (threadIdx.x >> 5) / SS::kWarpsPerHist;
   uint32_t* hlo = s.whist[wid][0];
   uint32_t* hhi = s.whist[wid][1];
   const uint32_t mm = __ballot_sync(0xffffffffu, member);
@@ -180,9 +193,9 @@ __device__ void hist_totals(SS& s, int rank, uint32_t n, int* err) {
     const int d = threadIdx.x & 255, q = threadIdx.x >> 8;
     uint32_t lo = 0, hi = 0;
 #pragma unroll
-    for (int w = 0; w < kSampWarps / 4; ++w) {
-      lo += s.whist[q * (kSampWarps / 4) + w][0][d];
-      hi += s.whist[q * (kSampWarps / 4) + w][1][d];
+    for (int w = 0; w < SS::kHist / 4; ++w) {
+      lo += s.whist[q * (SS::kHist / 4) + w][0][d];
+      hi += s.whist[q * (SS::kHist / 4) + w][1][d];
     }
     s.qsum[q][d] = ((unsigned long long)hi << 16) + lo;
   }
@@ -281,17 +294,14 @@ __global__ void __launch_bounds__(kSampThreads)
 
   // ---- greedy ---------------------------------------------------------
   if (!(temperature > 0.0f)) {
-    float v[kSampPerThread];
-#pragma unroll
-    for (int k = 0; k < kSampPerThread; ++k) {
-      const int i = k * kSampThreads + (int)threadIdx.x;
-      v[k] = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
-    }
     float best = -INFINITY;
     int idx = 0x7fffffff;
-#pragma unroll
-    for (int k = 0; k < kSampPerThread; ++k)   // increasing id: the first maximum is kept
-      if (!isnan(v[k]) && v[k] > best) { best = v[k]; idx = lo + k * kSampThreads + (int)threadIdx.x; }
+#pragma unroll 4
+    for (int k = 0; k < kSampPerThread; ++k) {   // increasing id: the first maximum is kept
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      const float v = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
+      if (!isnan(v) && v > best) { best = v; idx = lo + i; }
+    }
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best, o);
       const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
@@ -320,21 +330,40 @@ __global__ void __launch_bounds__(kSampThreads)
   }
 
   // ---- scale + max ---------------------------------------------------
-  float sc[kSampPerThread];
+  // The scaled logits stay in registers when a thread has few (C >= 8), else
+  // they go through e (each thread reads back only what it wrote).
+  constexpr bool kRegs = kSampPerThread <= 20;
+  float sc[kRegs ? kSampPerThread : 1];
   float mx = -INFINITY;
+  if constexpr (kRegs) {
 #pragma unroll
-  for (int k = 0; k < kSampPerThread; ++k) {
-    const int i = k * kSampThreads + (int)threadIdx.x;
-    sc[k] = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
-  }
-#pragma unroll
-  for (int k = 0; k < kSampPerThread; ++k) {
-    float x = 0.0f;
-    if (!isnan(sc[k])) {     // NaN logits keep 0.0 and stay out of the maximum
-      x = __fdiv_rn(sc[k], temperature);
-      mx = fmaxf(mx, x);
+    for (int k = 0; k < kSampPerThread; ++k) {
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      sc[k] = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
     }
-    sc[k] = x;
+#pragma unroll
+    for (int k = 0; k < kSampPerThread; ++k) {
+      float x = 0.0f;
+      if (!isnan(sc[k])) {     // NaN logits keep 0.0 and stay out of the maximum
+        x = __fdiv_rn(sc[k], temperature);
+        mx = fmaxf(mx, x);
+      }
+      sc[k] = x;
+    }
+  } else {
+#pragma unroll 4
+    for (int k = 0; k < kSampPerThread; ++k) {
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      if (i < n_local) {
+        const float v = h2f(lg[lo + i]);
+        float x = 0.0f;
+        if (!isnan(v)) {
+          x = __fdiv_rn(v, temperature);
+          mx = fmaxf(mx, x);
+        }
+        s.e[i] = __float_as_uint(x);
+      }
+    }
   }
   mx = warp_max(mx);
   if ((threadIdx.x & 31) == 0) s.red_f[threadIdx.x >> 5] = mx;
@@ -367,7 +396,10 @@ __global__ void __launch_bounds__(kSampThreads)
     const int i = k * kSampThreads + (int)threadIdx.x;
     uint32_t E = 0u;
     if (i < n_local) {
-      const float e = sampler_exp(__fsub_rn(sc[k], M));
+      float x;
+      if constexpr (kRegs) x = sc[k];
+      else x = __uint_as_float(s.e[i]);
+      const float e = sampler_exp(__fsub_rn(x, M));
       E = __float2uint_rz(__fmul_rn(e, 2147483648.0f));
       s.e[i] = E;
     }
@@ -506,44 +538,58 @@ static int launch_sample_c(const __half* logits, int n_seq, int row_stride, int 
                             out_ids, err) == cudaSuccess ? 0 : -1;
 }
 
-// 16-CTA clusters (half the ids per CTA) for batches that fit in one wave of
-// them; 8-CTA clusters otherwise.  16 is a non-portable cluster size: how many
-// such clusters fit at once is asked of the occupancy calculator, once per
-// device (sampler_prepare asks it ahead of a stream capture).
-static int wide_clusters(int dev) {
-  static int cached[64];
+// How many C-CTA clusters of k_sample<C> fit on the device at once (0 when the
+// occupancy calculator refuses the size).
+template <int C>
+static int active_clusters() {
+  int n = 0;
+  const size_t smem = sizeof(SampShared<C>);
+  if (cudaFuncSetAttribute(k_sample<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return 0;
+  if (C > 8 &&
+      cudaFuncSetAttribute(k_sample<C>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, 1);
+  cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaOccupancyMaxActiveClusters(&n, k_sample<C>, &cfg) != cudaSuccess) n = 0;
+  return n;
+}
+
+// Cluster size per batch: a CTA's time barely depends on how many ids it owns
+// (fixed per-pass costs dominate), so a batch takes as many rounds as it needs
+// waves of clusters.  16-CTA clusters (the fewest ids per CTA) when the batch
+// fits in one wave of them, 8 when it fits in one wave of those, else 4 (the
+// most clusters at once).  16 is a non-portable size.  The counts are asked of
+// the occupancy calculator once per device (sampler_prepare asks ahead of a
+// stream capture).
+static int sample_cluster_size(int dev, int n_seq) {
+  static int fit16[64], fit8[64];
   static bool known[64];
-  if (dev < 0 || dev >= 64) return 0;
+  if (dev < 0 || dev >= 64) return 8;
   if (!known[dev]) {
-    int n = 0;
-    const size_t smem = sizeof(SampShared<16>);
-    if (cudaFuncSetAttribute(k_sample<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
-            cudaSuccess &&
-        cudaFuncSetAttribute(k_sample<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
-            cudaSuccess) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(16, 1);
-      cfg.blockDim = dim3(kSampThreads);
-      cfg.dynamicSmemBytes = smem;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 16;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, k_sample<16>, &cfg) != cudaSuccess) n = 0;
-    }
+    fit16[dev] = active_clusters<16>();
+    fit8[dev] = active_clusters<8>();
     cudaGetLastError();   // a refused query leaves no error behind for the next launch check
-    cached[dev] = n;
     known[dev] = true;
   }
-  return cached[dev];
+  if (n_seq <= fit16[dev]) return 16;
+  if (n_seq <= fit8[dev]) return 8;
+  return 4;
 }
 
 void sampler_prepare() {
   int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) wide_clusters(dev);
+  if (cudaGetDevice(&dev) == cudaSuccess) sample_cluster_size(dev, 1);
 }
 
 int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
@@ -552,11 +598,17 @@ int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, fl
   if (vocab <= 0 || vocab > kVocab || n_seq <= 0) return -1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
-  if (n_seq <= wide_clusters(dev))
-    return launch_sample_c<16>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
-                               err, st);
-  return launch_sample_c<8>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
-                            err, st);
+  switch (sample_cluster_size(dev, n_seq)) {
+    case 16:
+      return launch_sample_c<16>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
+                                 err, st);
+    case 8:
+      return launch_sample_c<8>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
+                                err, st);
+    default:
+      return launch_sample_c<4>(logits, n_seq, row_stride, vocab, temperature, top_p, u24, out_ids,
+                                err, st);
+  }
 }
 
 }  // namespace qwen

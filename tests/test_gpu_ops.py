@@ -180,10 +180,11 @@ def test_sampler_top_p_bitexact(cuda, oracle, temp, top_p):
     assert got.tolist() == want
 
 
-@pytest.mark.parametrize("n", [1, 3, 64])
+@pytest.mark.parametrize("n", [1, 3, 12, 17, 64])
 def test_sampler_batch_sizes_bitexact(cuda, oracle, n):
-    """Small batches run on 16-CTA clusters, large ones on 8-CTA clusters: both
-    draw the oracle's ids (flat and peaked rows, u24 at both ends)."""
+    """Batches run on 16-, 8- or 4-CTA clusters by size (the largest cluster
+    whose one wave holds the batch, else 4): every size draws the oracle's ids
+    (flat and peaked rows, u24 at both ends), greedy included."""
     rng = np.random.default_rng(100 + n)
     lg = (rng.standard_normal((n, 151936)) * rng.uniform(0.1, 5, size=(n, 1))).astype(np.float16)
     u = np.array([oracle.uniform24(11, i, 5) for i in range(n)], np.uint32)
@@ -194,3 +195,6 @@ def test_sampler_batch_sizes_bitexact(cuda, oracle, n):
         got = N(ops.sample(T(lg), temp, top_p, T(u.view(np.int32))))
         want = [oracle.sample_top_p(lg[i], temp, top_p, int(u[i])) for i in range(n)]
         assert got.tolist() == want
+    lg[0, 7] = lg[0].max() + 1.0
+    got = N(ops.sample(T(lg), 0.0, 0.9))
+    assert got.tolist() == [oracle.sample_greedy(lg[i]) for i in range(n)]
