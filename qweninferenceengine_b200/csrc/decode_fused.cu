@@ -3,15 +3,17 @@
 //
 // Replaces the 506 dispatches of InferenceEngine.swift:103-264 per token.
 //
-// Roles inside a CTA (288 threads):
-//   warp 8      producer: streams this CTA's share of every weight byte of the
-//               step, in consumption order, into a ring of shared-memory slots
-//               with TMA bulk copies (cp.async.bulk + mbarrier transaction
-//               counts).  Weights do not depend on activations, so streaming
-//               runs ahead across the dependency waits of the consumers.
-//   warps 0..7  consumers: Q4 dequant + m16n8k16 MMA GEMVs on the slots, with
-//               fused prologues (RMSNorm) and epilogues (bias, RoPE, KV-cache
-//               write, SwiGLU, residual add), and the split-K attention.
+// Inside a CTA (256 threads, 8 warps): Q4 dequant + m16n8k16 MMA GEMVs on a
+// ring of shared-memory weight slots, with fused prologues (RMSNorm) and
+// epilogues (bias, RoPE, KV-cache write, SwiGLU, residual add), and the
+// split-K attention.  The ring streams this CTA's share of every weight byte
+// of the step, in consumption order, with TMA bulk copies (cp.async.bulk +
+// mbarrier transaction counts): the first 14 items at start, then item i + 14
+// as soon as the warps have released item i, issued by the warp whose release
+// completes it.  Weights do not depend on activations, so streaming runs ahead
+// across the dependency waits.  (No separate producer warp: 8 warps are 2 per
+// SM sub-partition, so a thread may hold 255 registers; 9 warps capped it at
+// 168 and the GEMV loops spilled.)
 //
 // Cross-CTA data (x, q, new k/v, attention partials and output, the SwiGLU
 // output h) travels as tagged words: a 32-bit word holds the fp16 value and a
@@ -72,7 +74,6 @@ static_assert(kAttnWarpsFused * 6 * 128 * 4 <= kAPt, "warp merge buffer aliases 
 
 struct Misc {
   int abort;
-  int issued;
   float scale;
   int cphase;           // phase the consumers are in (diagnostics)
   int last_rel[8];      // last item index each consumer warp released (diagnostics)
@@ -81,11 +82,6 @@ struct Misc {
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void abar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
-__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t cnt) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(cnt)
-               : "memory");
-}
 
 // ---------------------------------------------------------- tagged words --
 __device__ __forceinline__ void st_tag16(uint32_t* p, uint16_t tag, __half v) {
@@ -201,13 +197,13 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volati
 
 // Waits for item i of this CTA's list to land in its ring slot.  A slot's
 // mbarrier only tells the current phase from the previous one, so a warp
-// that runs ahead (one that owns every 8th tile) first waits until the
-// producer has issued item i -- from then on the slot's current phase is
-// item i's and the parity wait is exact.
-__device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile Misc* m, int* err,
-                                          int site) {
+// that runs ahead (one that owns every 8th tile) first waits until item i has
+// been issued into the slot (slot_item) -- from then on the slot's current
+// phase is item i's and the parity wait is exact.
+__device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile const int* slot_item,
+                                          volatile Misc* m, int* err, int site) {
   uint64_t t0 = 0;
-  for (uint32_t it = 0; m->issued <= i; ++it) {
+  for (uint32_t it = 0; slot_item[i % kNS] != i; ++it) {
     if ((it & 63) == 0) {
       if (aborted(m, err)) return false;
       const uint64_t now = globaltimer();
@@ -222,9 +218,6 @@ __device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile Misc* 
   return slot_wait(&full[i % kNS], (i / kNS) & 1, m, err, site);
 }
 
-__device__ __forceinline__ int it_phase_of(const FusedItem* items, int i) {
-  return (int)(items[i] & 0xFF);
-}
 
 // RMSNorm of xloc (rmsnorm.metal:9-46): out = half(half(x * s) * gamma).
 // Writes Q4 x fragments (frags) and/or plain fp16 (plain).  256 consumer threads.
@@ -630,10 +623,28 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
   astamp(6);
 }
 
+// Issues item i into its ring slot: the slot's previous readers are done
+// (their releases completed it), so after a proxy fence the bulk copy may
+// overwrite it; slot_item tells waiters the slot now holds item i.
+__device__ __noinline__ void issue_item(int i, const FusedItem* items, const FusedParams& p,
+                                        int lm_phase, uint8_t* ring, uint64_t* full,
+                                        volatile int* slot_item) {
+  const int slot = i % kNS;
+  const ItemFields it = unpack_item(items[i]);
+  size_t off;
+  uint32_t bytes;
+  item_source(it, lm_phase, &off, &bytes);
+  const uint8_t* src = (it.phase == lm_phase ? p.lm : p.q4) + off;
+  fence_proxy_async();
+  mbar_arrive_expect_tx(&full[slot], bytes);
+  bulk_g2s_stream(ring + slot * kSlotBytes, src, bytes, &full[slot], policy_evict_first());
+  __threadfence_block();
+  slot_item[slot] = i;
+}
+
 }  // namespace
 
-// 288 threads = 9 warps: one SM sub-partition holds 3 of them, so each thread
-// can have at most 16384 / 96 -> 168 registers.
+// 256 threads = 8 warps, 2 per SM sub-partition: up to 255 registers a thread.
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
@@ -643,7 +654,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* red2 = reinterpret_cast<float*>(smem + kOffRed2);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  uint64_t* empty = full + kNS;
+  // per slot: releases of the item in it so far, and the item issued into it
+  uint32_t* rel_cnt = reinterpret_cast<uint32_t*>(full + kNS);
+  volatile int* slot_item = reinterpret_cast<volatile int*>(rel_cnt + kNS);
   volatile Misc* misc = reinterpret_cast<volatile Misc*>(smem + kOffMisc);
   uint4* xf = reinterpret_cast<uint4*>(uni);
 
@@ -657,10 +670,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
+      rel_cnt[i] = 0;
+      slot_item[i] = -1;
     }
     misc->abort = 0;
-    misc->issued = 0;
     misc->cphase = -1;
     for (int w = 0; w < 8; ++w) misc->last_rel[w] = -1;
     fence_mbar_init();
@@ -668,36 +681,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   __syncthreads();
 
   unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      if (trace) trace[0] = globaltimer();
-      const uint64_t pol = policy_evict_first();
-      int i = 0;
-      for (; i < n_items; ++i) {
-        const int slot = i % kNS;
-        const uint32_t par = ((i / kNS) & 1) ^ 1;
-        if (!slot_wait(&empty[slot], par, misc, p.err, kSiteEmpty * 100 + (it_phase_of(items, i) % 100))) {
-          if (p.err[2] == (int)blockIdx.x && p.err[3] == (int)threadIdx.x) {
-            p.err[4] = i;
-            p.err[5] = n_items;
-            p.err[6] = misc->cphase;
-            for (int w = 0; w < 8; ++w) p.err[7 + w] = misc->last_rel[w];
-          }
-          break;
-        }
-        const ItemFields it = unpack_item(items[i]);
-        size_t off;
-        uint32_t bytes;
-        item_source(it, lm_phase, &off, &bytes);
-        const uint8_t* src = (it.phase == lm_phase ? p.lm : p.q4) + off;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s_stream(ring + slot * kSlotBytes, src, bytes, &full[slot], pol);
-        misc->issued = i + 1;
-      }
-      if (trace) trace[1] = globaltimer();
-    }
-  } else {
+  if (threadIdx.x == 0) {
+    if (trace) trace[0] = globaltimer();
+    for (int i = 0; i < kNS && i < n_items; ++i) issue_item(i, items, p, lm_phase, ring, full, slot_item);
+  }
+  {
     // ------------------------------------------------------------ consumers
     const int ct = threadIdx.x;
     const uint32_t L = p.seq_ctl[3];       // SeqCtl.seq_len
@@ -706,6 +694,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     auto tagof = [&](uint32_t k) { return (uint32_t)((epoch << 8) + k) & 0xFFFFu; };
     const int g = lane >> 2, t = lane & 3;
     int cur = 0;
+    // Lane 0 of a warp: this warp's share n of item i's kConsumerWarps
+    // releases; the release that completes them refills the slot with item
+    // i + kNS (none once the kernel is aborting).
+    auto release = [&](int i, uint32_t n) {
+      const int slot = i % kNS;
+      __threadfence_block();   // this warp's reads of the slot before its release
+      if (atomicAdd(&rel_cnt[slot], n) + n == (uint32_t)kConsumerWarps) {
+        __threadfence_block();   // every warp's release before the refill
+        rel_cnt[slot] = 0;
+        // (the shared abort flag only: a global read here would sit on the
+        // issuing warp's path at every refill)
+        if (i + kNS < n_items && !misc->abort)
+          issue_item(i + kNS, items, p, lm_phase, ring, full, slot_item);
+      }
+      misc->last_rel[warp] = i;
+    };
     auto phase_end = [&](uint16_t ph) {
       int e = cur;
       while (e < n_items && (int)(items[e] & 0xFF) == ph) ++e;
@@ -719,9 +723,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         trace ? trace + 3 + p.n_layers * kTraceStampsPerLayer + 2 + 7 : nullptr;
     int wsel = -1;
     auto timed_wait = [&](int i, int site) {
-      if (!wtrace || ct != 0 || wsel < 0) return item_wait(i, full, misc, p.err, site);
+      if (!wtrace || ct != 0 || wsel < 0) return item_wait(i, full, slot_item, misc, p.err, site);
       const uint64_t t0 = globaltimer();
-      const bool ok = item_wait(i, full, misc, p.err, site);
+      const bool ok = item_wait(i, full, slot_item, misc, p.err, site);
       wtrace[wsel] += globaltimer() - t0;
       return ok;
     };
@@ -734,10 +738,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           q4_chunk3(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
                     acc_g8);
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&empty[slot]);
-          misc->last_rel[warp] = i;
-        }
+        if (lane == 0) release(i, 1);
         if (it.last) {
           if (t == 0) {
             red[warp * 16 + g] = acc_g;
@@ -784,11 +785,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
             q4_chunk(ring + slot * kSlotBytes, it.k0, s0 - i0, s1 - i0, 1, xf, lane, acc_g, acc_g8);
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive_cnt(&empty[slot],
-                            warp == wfirst ? (uint32_t)(kConsumerWarps - ntouch + 1) : 1u);
-            misc->last_rel[warp] = i;
-          }
+          if (lane == 0) release(i, warp == wfirst ? (uint32_t)(kConsumerWarps - ntouch + 1) : 1u);
         }
         if (t == 0) {
           red[warp * 16 + g] = acc_g;
@@ -957,10 +954,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
             q4_chunk(ring + slot * kSlotBytes, it.k0, 0, it.nk, 1, xf, lane, acc_g, acc_g8);
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive_cnt(&empty[slot], kConsumerWarps);
-            misc->last_rel[warp] = i;
-          }
+          if (lane == 0) release(i, kConsumerWarps);
           if (t == 0) {
             // gate and up with the zero bias of InferenceEngine.swift:82-85, then
             // half(silu(gate) * up) (activations.metal:14-26)
@@ -1019,7 +1013,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         const ItemFields it = unpack_item(items[i]);
         if ((it.seq & (kConsumerWarps - 1)) != warp) continue;
         const int slot = i % kNS;
-        if (item_wait(i, full, misc, p.err, kSiteFull * 100 + it.phase % 100)) {
+        if (item_wait(i, full, slot_item, misc, p.err, kSiteFull * 100 + it.phase % 100)) {
           const uint8_t* sb = ring + slot * kSlotBytes;
           int s = 0;
           for (; s + 1 < it.nk; s += 2) {
@@ -1040,10 +1034,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           }
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_cnt(&empty[slot], kConsumerWarps);
-          misc->last_rel[warp] = i;
-        }
+        if (lane == 0) release(i, kConsumerWarps);
         if (it.last) {
           if (t == 0) {
             p.logits[16 * it.tile + g] = f2h(d[0] + d2[0]);
@@ -1060,11 +1051,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   __syncthreads();
   // Drain: every copy this CTA issued has landed before its shared memory goes away.
   if (threadIdx.x == 0) {
-    const int issued = misc->issued;
     const uint64_t t0 = globaltimer();
-    for (int i = max(0, issued - kNS); i < issued; ++i)
-      while (!mbar_try_wait(&full[i % kNS], (i / kNS) & 1))
+    for (int sl = 0; sl < kNS; ++sl) {
+      const int i = slot_item[sl];
+      if (i < 0) continue;
+      while (!mbar_try_wait(&full[sl], (i / kNS) & 1))
         if (globaltimer() - t0 > kWaitNs) break;
+    }
+    if (trace) trace[1] = globaltimer();
   }
 }
 

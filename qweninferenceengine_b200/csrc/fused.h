@@ -42,7 +42,7 @@ constexpr int kDownChunkBp = 24;                // down tiles stream in chunks o
 
 constexpr int kSlotBytes = kTile1536Bytes;      // ring slot
 constexpr int kConsumerWarps = 8;
-constexpr int kFusedThreads = (kConsumerWarps + 1) * 32;
+constexpr int kFusedThreads = kConsumerWarps * 32;
 constexpr int kAttnWarpsFused = 4;
 constexpr int kMaxAttnSplits = 74;
 constexpr int kAttnPartWords = 6 * 128 + 12;     // o[6][128], m[6], l[6]
