@@ -294,7 +294,8 @@ __device__ __forceinline__ void q4_chunk(const uint8_t* slot, int k0, int b_begi
 
 // Same with three block pairs in flight: the single-tile phases (QKV, O) give
 // each warp 3 strided block pairs, which q4_chunk runs as a pair then a tail,
-// two dependent rounds.
+// two dependent rounds; the down ranges (17-18 pairs a warp) gain from the
+// third chain too now that registers do not spill.
 __device__ __forceinline__ void q4_chunk3(const uint8_t* slot, int k0, int b_begin, int b_end,
                                           int b_step, const uint4* xf, int lane, float& acc_g,
                                           float& acc_g8) {
@@ -783,7 +784,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
             }
           const int slot = i % kNS;
           if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
-            q4_chunk(ring + slot * kSlotBytes, it.k0, s0 - i0, s1 - i0, 1, xf, lane, acc_g, acc_g8);
+            q4_chunk3(ring + slot * kSlotBytes, it.k0, s0 - i0, s1 - i0, 1, xf, lane, acc_g, acc_g8);
           __syncwarp();
           if (lane == 0) release(i, warp == wfirst ? (uint32_t)(kConsumerWarps - ntouch + 1) : 1u);
         }
