@@ -174,7 +174,8 @@ __device__ __forceinline__ void poll_units(const uint32_t* src, int n_units, int
         return;
       }
     }
-    __nanosleep(32);
+    // no sleep between rounds: a hop is on the step's critical path, and a
+    // 32 ns back-off measured 0.8% slower end to end
   }
 }
 
@@ -594,7 +595,6 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
           break;
         }
       }
-      __nanosleep(32);
     }
   }
   abar();
