@@ -602,17 +602,20 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
   // Per (split, head of the slice) rescale factors and per-head totals, once.
   float* cfac = reinterpret_cast<float*>(uni + kACFac);  // [S_eff][nh] factors, then [nh] totals
   float* ctot = cfac + kMaxAttnSplits * 2;
-  if (ct < (int)nh) {
-    const uint32_t hl = ct;
+  // A warp per head of the slice, a lane per split (fixed-order reductions).
+  for (uint32_t hl = ct >> 5; hl < nh; hl += kAttnWarpsFused) {
+    const uint32_t ln = ct & 31;
     float M = -INFINITY;
-    for (uint32_t sp = 0; sp < S_eff; ++sp) M = fmaxf(M, stage[sp * per_split + nz + hl]);
+    for (uint32_t sp = ln; sp < S_eff; sp += 32) M = fmaxf(M, stage[sp * per_split + nz + hl]);
+    M = warp_max(M);
     float Ls = 0.f;
-    for (uint32_t sp = 0; sp < S_eff; ++sp) {
+    for (uint32_t sp = ln; sp < S_eff; sp += 32) {
       const float c = expf(stage[sp * per_split + nz + hl] - M);
       cfac[sp * nh + hl] = c;
       Ls += stage[sp * per_split + nz + nh + hl] * c;
     }
-    ctot[hl] = Ls;
+    Ls = warp_sum(Ls);
+    if (ln == 0) ctot[hl] = Ls;
   }
   abar();
   for (uint32_t z = z0 + ct; z < z1; z += 128) {
