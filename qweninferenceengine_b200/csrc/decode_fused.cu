@@ -977,14 +977,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           const __half* db = p.down_bias + (size_t)layer * kHidden;
           const int dtile = (int)unpack_item(items[cur]).tile;
           const float dbias = ct < 16 ? h2f(db[16 * dtile + ct]) : 0.f;
-          poll_units<5>(p.h_ll, kInter / 8, ct, 256, tagof(layer), misc, p.err,
-                        kSiteH * 100 + layer, [&](int u, const __half* v) {
-                          __half tmp[8];
+          // Each warp polls only the h units of its own K range (block pairs
+          // [w*140/8, (w+1)*140/8), the range ksplit_down gives it) and starts
+          // its GEMV once they are in: no CTA-wide wait for the last of the
+          // 1120 units.  (The cbar after gate/up ended every read of xf.)
+          {
+            const int blo = warp * kBp8960 / kConsumerWarps;
+            const int bhi = (warp + 1) * kBp8960 / kConsumerWarps;
+            poll_units<5>(p.h_ll + 64 * blo, 8 * (bhi - blo), lane, 32, tagof(layer), misc, p.err,
+                          kSiteH * 100 + layer, [&](int u, const __half* v) {
+                            __half tmp[8];
 #pragma unroll
-                          for (int q = 0; q < 8; ++q) tmp[q] = v[q];
-                          xf[u] = make_xfrag(tmp);
-                        });
-          cbar();
+                            for (int q = 0; q < 8; ++q) tmp[q] = v[q];
+                            xf[8 * blo + u] = make_xfrag(tmp);
+                          });
+            __syncwarp();
+          }
           lstamp(layer, kTsDownReady);
           wsel = layer == p.n_layers / 2 ? 1 : -1;
           if (wtrace && ct == 0 && wsel >= 0) wtrace[1] = 0;
