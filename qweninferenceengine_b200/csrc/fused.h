@@ -49,9 +49,10 @@ constexpr int kAttnPartWords = 6 * 128 + 12;     // o[6][128], m[6], l[6]
 
 enum FusedPhase : uint16_t { kPhQKV = 0, kPhAttn = 1, kPhO = 2, kPhGU = 3, kPhDown = 4 };
 constexpr int kPhasesPerLayer = 5;
-// Trace stamps per CTA: [0] producer start, [1] producer done, [2] consumer
-// start, then per layer kTraceStampsPerLayer stamps (see TraceStamp), then
-// LM start, consumer end.
+// Trace stamps per CTA: [0] first weight items issued, [1] copies drained at
+// exit, [2] consumer start, then per layer kTraceStampsPerLayer stamps (see
+// TraceStamp), then LM start, consumer end.  kTsDownReady is warp 0's h range
+// in (each down warp polls its own range).
 enum TraceStamp : int {
   kTsLayerStart = 0, kTsXReady, kTsQKVDone, kTsAttnDone, kTsOReady, kTsODone, kTsGUReady,
   kTsGUDone, kTsDownReady, kTsDownDone, kTraceStampsPerLayer
