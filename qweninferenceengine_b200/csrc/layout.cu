@@ -256,3 +256,21 @@ int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
 }
 
 }  // namespace qwen
+
+// Test hook (not part of the public header): the fused step's work schedule
+// for n_layers layers on `grid` CTAs, exactly as build_fused_weights builds it.
+// Writes the packed items (fused.h: FusedItem) into items_out (capacity
+// items_cap) and the per-CTA begin offsets into begin_out[grid + 1].  Host
+// arithmetic only.  Returns the item count, or -1 when an argument is out of
+// range or the capacity is too small.
+extern "C" long long qwen_fused_schedule(int n_layers, int grid, unsigned long long* items_out,
+                                         long long items_cap, unsigned int* begin_out) {
+  if (n_layers < 1 || n_layers > 64 || grid < 1 || grid > 1024 || !items_out || !begin_out) return -1;
+  std::vector<qwen::FusedItem> items;
+  std::vector<uint32_t> begin;
+  qwen::build_schedule(n_layers, grid, items, begin);
+  if ((long long)items.size() > items_cap) return -1;
+  std::copy(items.begin(), items.end(), items_out);
+  std::copy(begin.begin(), begin.end(), begin_out);
+  return (long long)items.size();
+}
