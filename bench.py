@@ -190,10 +190,14 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 10))
-    cb = cpu_baseline(n_tokens=steps, warmup=min(args.warmup, 1))
+    # one step = one decode token of the CPU port (~0.2-0.4 s on the host cores):
+    # the requested warm-up (at most 5) and at most 50 timed steps keep the run
+    # well under a minute
+    steps = max(1, min(args.steps, 50))
+    warm = max(0, min(args.warmup, 5))
+    cb = cpu_baseline(n_tokens=steps, warmup=warm)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": steps, "warmup": min(args.warmup, 1),
+            "n_gpus": args.gpus, "steps": steps, "warmup": warm,
             "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 (fp32 accumulate), int4 weights",
             "data": "synthetic",
