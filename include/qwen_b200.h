@@ -151,7 +151,11 @@ int qwen_quantize_q4(const float* w, size_t n, uint8_t* packed, uint16_t* scales
  * of (E desc, id asc) whose sum reaches floor(sum(E) * trunc(top_p*2^24) / 2^24),
  * draw R = floor(kept * u24 / 2^24) and return the first kept id whose running
  * sum exceeds R.  u24[n_seq] are 24-bit uniforms (device).
- * out_ids: int32 [n_seq], device. */
+ * out_ids: int32 [n_seq], device.
+ * Each sequence runs on one thread-block cluster of 16, 8 or 4 CTAs, chosen
+ * by batch size from occupancy-calculator counts that the first call on a
+ * device asks for (no allocation); when capturing this call into a CUDA
+ * graph, make one call on that device before the capture. */
 int qwen_sample(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uint32_t vocab,
                 float temperature, float top_p, const uint32_t* u24, int32_t* out_ids,
                 void* stream);
