@@ -112,6 +112,16 @@ class QwenEngine:
         res = [out[i, : n_out[i]].tolist() for i in range(b)]
         return res if batched else res[0]
 
+    def generate_text(self, prompt: str, tokenizer, max_tokens: int = 64, write=None) -> str:
+        """generate(prompt:maxTokens:) on text (InferenceEngine.swift:29-52): the
+        prompt (ChatML, see tokenizer.format_prompt) is encoded with a
+        tokenizer.QwenTokenizer, fed through forward(), and each generated
+        token's text is passed to `write` (e.g. sys.stdout.write) as it
+        completes.  Returns the generated text."""
+        from .tokenizer import stream_generate
+
+        return stream_generate(self.forward, tokenizer, prompt, max_tokens, write)
+
     def prefill(self, prompt_ids) -> None:
         p = np.ascontiguousarray(prompt_ids, dtype=np.int32)
         if p.ndim == 1:
