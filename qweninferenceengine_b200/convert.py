@@ -52,7 +52,11 @@ class SafeTensors:
         return list(self.header)
 
     def f32(self, name: str) -> np.ndarray | None:
-        """The tensor as fp32 (flattened), or None when the file lacks it."""
+        """The tensor as fp32 (flattened), or None when the file lacks it.
+
+        A NaN or infinite value is an error naming the tensor: the pipeline's
+        quantizer would trap on Int(round(NaN)) (QwenPipelines.swift:124-131),
+        and the device quantizer would otherwise turn it into a plausible nibble."""
         meta = self.header.get(name)
         if meta is None:
             return None
@@ -60,10 +64,15 @@ class SafeTensors:
         raw = self.data[b:e]
         dtype = meta["dtype"]
         if dtype == "BF16":
-            return (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
-        if dtype == "F16":
-            return raw.view(np.float16).astype(np.float32)
-        raise ValueError(f"unsupported dtype {dtype} for {name}")
+            out = (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+        elif dtype == "F16":
+            out = raw.view(np.float16).astype(np.float32)
+        else:
+            raise ValueError(f"unsupported dtype {dtype} for {name}")
+        if not np.isfinite(out).all():
+            bad = int(np.count_nonzero(~np.isfinite(out)))
+            raise ValueError(f"tensor {name} holds {bad} non-finite value(s) (NaN or Inf)")
+        return out
 
 
 def device_quantizer(w: np.ndarray):

@@ -2,18 +2,20 @@
 
     python -m qweninferenceengine_b200.profiling case  [--layers 4] [--steps 2]
         A small decode run (random-init model with `--layers` layers, a short
-        prompt, a few decode steps): the workload for `ncu --set full -k
-        regex:k_decode_fused -s 3 -c 1` captures, small enough to capture in
+        prompt, a few decode steps): the workload for `ncu --set full --clock-control
+        none -k regex:k_decode_fused -s 3 -c 1` captures, small enough to capture in
         seconds while its 1.2 GB+ of weights still exceed the L2.
 
     python -m qweninferenceengine_b200.profiling gemm [--rows 17920] [--k 1536] [--batch 64]
         One batched Q4 projection on the tensor cores (qwen_gemm_q4_0_batched,
         eager launches: repack, pack, k_tc_gemm, split sum), repeated --reps
-        times -- the workload for `ncu -k regex:k_tc_gemm` captures.
+        times -- the workload for `ncu --clock-control none -k regex:k_tc_gemm`
+        captures.
 
     python -m qweninferenceengine_b200.profiling attention [--batch 64] [--ctx 2000]
         Batched decode attention over random caches (qwen_attention_decode_batched),
-        repeated --reps times -- the workload for `ncu -k regex:k_attention_decode`.
+        repeated --reps times -- the workload for `ncu --clock-control none -k
+        regex:k_attention_decode`.
 
     python -m qweninferenceengine_b200.profiling tcstep [--batch 64] [--ctx 1024]
         The batched tensor-core step: prefill, then --reps eagerly launched steps
@@ -87,7 +89,7 @@ def run_tcstep(batch: int, ctx: int, reps: int, layers: int = 28) -> list:
                         for s in range(batch)]).astype(np.int32)
     eng.prefill(prompts)
     prof = []
-    torch.cuda.nvtx.range_push("tcstep")  # ncu --nvtx --nvtx-include tcstep/ selects these launches
+    torch.cuda.nvtx.range_push("tcstep")  # ncu --clock-control none --nvtx --nvtx-include tcstep/ selects these launches
     for _ in range(reps):
         prof = eng.profile_step()
     torch.cuda.nvtx.range_pop()

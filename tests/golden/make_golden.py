@@ -1,6 +1,6 @@
 """Generates tests/golden/metal_ref_vectors.npz from the reference's own Metal
 kernels compiled as C++ (oracle/_ref/libqwen_metal_ref.so, built by
-`make -C oracle ref` from the reference tree).
+`make -C oracle ref REF_DIR=<reference tree>`).
 
 These fixtures pin the oracle where the reference tree is absent: every entry
 holds the inputs and the compiled reference's outputs (fp16 as uint16 bit

@@ -125,6 +125,16 @@ def test_missing_weight_writes_nothing_and_bad_dtype_fails(oracle, tmp_path):
                           np.zeros(H + 2 * KV, np.float16))
 
 
+@pytest.mark.parametrize("bad", [np.nan, np.inf, -np.inf])
+def test_non_finite_weight_is_an_error_naming_the_tensor(oracle, tmp_path, bad):
+    w = np.full((H, H), 0.01, np.float16)
+    w[3, 5] = bad
+    src = str(tmp_path / "m.safetensors")
+    write_safetensors(src, {"model.layers.0.self_attn.q_proj.weight": ("F16", (H, H), w.tobytes())})
+    with pytest.raises(ValueError, match=r"model\.layers\.0\.self_attn\.q_proj\.weight holds 1 non-finite"):
+        cv.convert(src, str(tmp_path / "w"), 1, quantize=oracle.quantize_q4, hidden=H, kv_dim=KV)
+
+
 def test_default_quantizer_needs_a_device(checkpoint, tmp_path):
     import torch
 
