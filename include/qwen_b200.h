@@ -6,6 +6,11 @@
  * uint16_t bit patterns, streams are cudaStream_t passed as void*.  Every
  * entry point returns a status (QWEN_OK == 0); qwen_last_error() gives a
  * thread-local message for the last failure.  Nothing here exits or aborts.
+ * Operator entry points return once their kernels are enqueued: a failure
+ * only the device can see (a bounded wait that gave up, a device-resident
+ * length out of range) is recorded on the device and reported by
+ * qwen_ops_status().  Engine calls synchronise and report such failures
+ * themselves.
  *
  * Each declaration names the reference interface it replaces
  * (Raiden-Makoto/QwenInferenceEngine, file:line).
@@ -36,6 +41,14 @@ extern "C" {
 
 const char* qwen_last_error(void);
 int qwen_abi_version(void);
+
+/* Synchronises `stream` and reports the first device-side failure recorded by
+ * an operator kernel on the current device since the last call (then clears
+ * it): QWEN_ERR_DEVICE_TIMEOUT for a bounded wait that gave up,
+ * QWEN_ERR_INVALID_ARGUMENT for a device-resident length out of range, else
+ * QWEN_OK.  The reference has no asynchronous operators (every Metal command
+ * buffer is waited for, InferenceEngine.swift:266-268). */
+int qwen_ops_status(void* stream);
 
 /* ======================================================================
  * Operators: one entry per reference Metal pipeline (MetalManager.swift:43-49
@@ -90,7 +103,9 @@ int qwen_swiglu(uint16_t* gate, const uint16_t* up, uint32_t n, void* stream);
 /* Fused GQA decode attention (the engine's split-K kernel; replaces the
  * attention_scores -> softmax -> attn_weighted_sum chain,
  * InferenceEngine.swift:162-182).  q: 12x128 fp16 (after RoPE); caches in the
- * reference layout [pos][256]; L = *seq_len positions; out: 1536 fp16. */
+ * reference layout [pos][256]; L = *seq_len positions; out: 1536 fp16.
+ * L outside [1, max_ctx] leaves `out` untouched and is reported by
+ * qwen_ops_status. */
 int qwen_attention_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                           uint16_t* out, const uint32_t* seq_len, uint32_t max_ctx,
                           void* stream);
@@ -114,8 +129,10 @@ int qwen_attention_decode_batched(const uint16_t* q, const uint16_t* k_cache,
  * 1 MiB device array inside this library (held on every GPU that loads it until
  * exit); requests needing more are rejected with QWEN_ERR_INVALID_ARGUMENT.
  * All calls on a device share that array: calls that overlap on the GPU race,
- * so serialise them.  The first call on a device resolves the array's address
- * and should come before any stream capture. */
+ * so serialise them.  The first call on a device (and the first after its
+ * context changes) resolves the array's address and should come before any
+ * stream capture.  Device-side failures go to the status word that
+ * qwen_ops_status reads, itself a fixed device array. */
 int qwen_attention_decode_noalloc(const uint16_t* q, const uint16_t* k_cache,
                                   const uint16_t* v_cache, uint16_t* out,
                                   const uint32_t* seq_len, uint32_t max_ctx, void* stream);
@@ -184,7 +201,27 @@ typedef struct qwen_engine_config {
   float top_p;         /* default 0.8 (:273) */
   uint64_t seed;       /* uniform stream seed (the reference's RNG is unseeded) */
   int stop_on_eos;     /* generate() stops at 151645 / 151643 (:41) */
+  int ctx_overflow;    /* QWEN_CTX_CLAMP (default) or QWEN_CTX_ERROR, below */
+  int prefill_mode;    /* QWEN_PREFILL_CHUNKED (default) or QWEN_PREFILL_STEPS, below */
 } qwen_engine_config;
+
+/* Prompt processing.  QWEN_PREFILL_STEPS: the reference's loop, one full
+ * decode step per prompt token (InferenceEngine.swift:34-36).
+ * QWEN_PREFILL_CHUNKED (fused and tensor-core engines): the prompt positions of
+ * every sequence run as the rows of batched tensor-core steps, a chunk at a
+ * time, without the LM head and sampler except for each sequence's last
+ * position, whose sample is drawn exactly as the loop's last step draws it.
+ * The per-op engine (QWEN_KERNELS_OPS) always uses the loop. */
+#define QWEN_PREFILL_CHUNKED 0
+#define QWEN_PREFILL_STEPS 1
+
+/* Positions past max_ctx - 1.  QWEN_CTX_CLAMP: the reference's rule,
+ * min(position, maxContextWindow - 1) (InferenceEngine.swift:55) -- the step
+ * overwrites the last KV slot and attends max_ctx positions.  QWEN_CTX_ERROR:
+ * forward / decode / generate return QWEN_ERR_INVALID_ARGUMENT instead of
+ * running such a step. */
+#define QWEN_CTX_CLAMP 0
+#define QWEN_CTX_ERROR 1
 
 void qwen_engine_config_default(qwen_engine_config* cfg);
 
@@ -238,6 +275,13 @@ int qwen_engine_get_logits(qwen_engine* e, int32_t seq, uint16_t* host_logits);
 int qwen_engine_get_kv(qwen_engine* e, int32_t seq, int32_t layer, int32_t n_pos,
                        uint16_t* host_k, uint16_t* host_v);
 
+/* The inverse of qwen_engine_get_kv: overwrites positions [0, n_pos) of one
+ * layer's KV cache of sequence `seq` from host buffers in the reference layout
+ * (either may be NULL).  For replaying a cache into the engine (the reference
+ * has no such entry point; InferenceManager.swift:63-65 owns the buffers). */
+int qwen_engine_set_kv(qwen_engine* e, int32_t seq, int32_t layer, int32_t n_pos,
+                       const uint16_t* host_k, const uint16_t* host_v);
+
 /* Current position (tokens consumed) of sequence `seq`. */
 int qwen_engine_position(qwen_engine* e, int32_t seq, int32_t* position);
 
@@ -273,6 +317,20 @@ int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n)
  * n >= *needed, and always reports *needed. */
 int qwen_engine_trace(qwen_engine* e, int32_t enable);
 int qwen_engine_get_trace(qwen_engine* e, uint64_t* host, size_t n, size_t* needed);
+
+/* Every device-side dependency wait of the fused decode step gives up after
+ * timeout_ns (default 2 s; 1 ms .. 60 s accepted), after which the step
+ * finishes without its remaining work and the call that ran it returns
+ * QWEN_ERR_DEVICE_TIMEOUT; the engine stays usable.  (The reference waits
+ * without limit: commandBuffer.waitUntilCompleted, InferenceEngine.swift:266-268.) */
+int qwen_engine_set_wait_timeout(qwen_engine* e, uint64_t timeout_ns);
+
+/* Test hook, no reference counterpart: site 9 makes every down-phase wait of
+ * the fused step expect data that nothing writes, so the waits run out and
+ * the timeout path runs; site 0 turns the hook off. */
+#define QWEN_STALL_NONE 0
+#define QWEN_STALL_FUSED_H 9
+int qwen_engine_test_stall(qwen_engine* e, int32_t site);
 
 /* Device and stream the engine runs on (for callers that time it). */
 int qwen_engine_stream(qwen_engine* e, void** stream);

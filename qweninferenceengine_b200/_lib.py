@@ -25,6 +25,12 @@ QWEN_KERNELS_FUSED = 0
 QWEN_KERNELS_OPS = 1
 QWEN_KERNELS_TC = 2
 
+QWEN_CTX_CLAMP = 0
+QWEN_CTX_ERROR = 1
+
+QWEN_PREFILL_CHUNKED = 0
+QWEN_PREFILL_STEPS = 1
+
 c_void_p, c_int, c_uint32, c_int32, c_uint64, c_size_t, c_float = (
     ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint64,
     ctypes.c_size_t, ctypes.c_float)
@@ -37,13 +43,15 @@ class EngineConfig(ctypes.Structure):
 
     _fields_ = [("device", c_int), ("max_ctx", c_int), ("batch", c_int), ("n_layers", c_int),
                 ("kernels", c_int), ("temperature", c_float), ("top_p", c_float),
-                ("seed", c_uint64), ("stop_on_eos", c_int)]
+                ("seed", c_uint64), ("stop_on_eos", c_int), ("ctx_overflow", c_int),
+                ("prefill_mode", c_int)]
 
 
 # name -> (restype, argtypes)
 SIGNATURES = {
     "qwen_last_error": (ctypes.c_char_p, []),
     "qwen_abi_version": (c_int, []),
+    "qwen_ops_status": (c_int, [c_void_p]),
     "qwen_gemv_q4_0": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_uint32, c_void_p,
                                c_uint32, c_void_p]),
     "qwen_gemv_fp16": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p]),
@@ -82,8 +90,11 @@ SIGNATURES = {
     "qwen_engine_prefill": (c_int, [c_void_p, _i32p, c_int32]),
     "qwen_engine_get_logits": (c_int, [c_void_p, c_int32, _u16p]),
     "qwen_engine_get_kv": (c_int, [c_void_p, c_int32, c_int32, c_int32, _u16p, _u16p]),
+    "qwen_engine_set_kv": (c_int, [c_void_p, c_int32, c_int32, c_int32, _u16p, _u16p]),
     "qwen_engine_position": (c_int, [c_void_p, c_int32, _i32p]),
     "qwen_engine_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "qwen_engine_set_wait_timeout": (c_int, [c_void_p, c_uint64]),
+    "qwen_engine_test_stall": (c_int, [c_void_p, c_int32]),
     "qwen_engine_kernels_per_step": (c_int, [c_void_p, _i32p]),
     "qwen_engine_trace": (c_int, [c_void_p, c_int32]),
     "qwen_engine_get_trace": (c_int, [c_void_p, ctypes.POINTER(c_uint64), c_size_t,

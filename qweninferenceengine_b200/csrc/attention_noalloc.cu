@@ -18,11 +18,14 @@
 //     behind.  The merge tickets that must start at zero are cleared on the
 //     caller's stream before each launch.  Calls that overlap on the GPU (two
 //     streams, or two host threads) race on the array: serialise them.
-//   * The first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current) and caches it; make that
-//     first call before any stream capture.
-#include <mutex>
-
+//   * The first call on a device (and the first after the device's context
+//     changes, e.g. after cudaDeviceReset) looks up the array's device address
+//     with cudaGetSymbolAddress, with that device current, and caches it per
+//     context; make that first call before any stream capture.
+//   * A device-side failure (a bounded wait that gave up, a length beyond
+//     max_ctx) is recorded in the operator status word, which qwen_ops_status
+//     reports; that word is a __device__ array too, so recording it allocates
+//     nothing either.
 #include "../../include/qwen_b200.h"
 #include "qwen_common.cuh"
 #include "qwen_internal.h"
@@ -31,31 +34,21 @@
 namespace qwen {
 
 constexpr size_t kNoAllocScratchBytes = (size_t)1 << 20;
-constexpr int kNoAllocMaxDevices = 64;
 
 // Device-side scratch.  In host code this name is only a stand-in for the
 // symbol: its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_attn_noalloc_scratch[kNoAllocScratchBytes];
 
-static std::mutex g_noalloc_mu;
-static void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+static DeviceSymbolCache g_noalloc_cache;
+
+// Set-up, with the device current: the array's device address.
+static int lookup_scratch(void** p) {
+  return cuda_status(cudaGetSymbolAddress(p, g_attn_noalloc_scratch),
+                     "cudaGetSymbolAddress(attention scratch)");
+}
 
 static int noalloc_scratch_address(void** out) {
-  int dev = 0;
-  if (int rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return set_error(QWEN_ERR_INVALID_ARGUMENT, "attention_decode_noalloc: device %d beyond %d",
-                     dev, kNoAllocMaxDevices);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    if (int rc = cuda_status(cudaGetSymbolAddress(&p, g_attn_noalloc_scratch),
-                             "cudaGetSymbolAddress(attention scratch)"))
-      return rc;
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
-  return QWEN_OK;
+  return symbol_address_cached(g_noalloc_cache, lookup_scratch, out);
 }
 
 }  // namespace qwen
@@ -91,7 +84,7 @@ extern "C" int qwen_attention_decode_noalloc(const uint16_t* q, const uint16_t* 
   p.max_ctx = max_ctx;
   p.out = reinterpret_cast<__half*>(out);
   p.out_seq_stride = kHidden;
-  p.err = nullptr;
+  if (int rc = ops_status_word(&p.err)) return rc;
   attn_bind_scratch(p, scratch, splits, 1);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // The merge tickets must start at zero (an earlier call that failed part

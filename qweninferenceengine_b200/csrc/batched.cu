@@ -231,13 +231,20 @@ __global__ void __launch_bounds__(kFinThreads) k_resid_norm_finish(
 
 // Row r = position p0 + r of sequence 0: x[r] = embedding of its prompt id,
 // len[r] = p0 + r + 1 (InferenceEngine.swift:57-60 per position).
-__global__ void __launch_bounds__(192) k_prefill_rows(const int32_t* __restrict__ prompt, int p0,
+// Rows of one chunk of a prefill: row r = b * n_pos + j is position p0 + j of
+// sequence b -- the embedding of its prompt id, its length and its KV sequence.
+__global__ void __launch_bounds__(192) k_prefill_rows(const int32_t* __restrict__ prompt,
+                                                      int prompt_stride, int p0, int n_pos,
                                                       const __half* __restrict__ embed,
                                                       __half* __restrict__ x,
-                                                      uint32_t* __restrict__ len) {
-  const int r = blockIdx.x;
-  const int32_t tok = prompt[p0 + r];
-  if (threadIdx.x == 0) len[r] = (uint32_t)(p0 + r + 1);
+                                                      uint32_t* __restrict__ len,
+                                                      int32_t* __restrict__ row_seq) {
+  const int r = blockIdx.x, b = r / n_pos, j = r % n_pos;
+  const int32_t tok = prompt[(size_t)b * prompt_stride + p0 + j];
+  if (threadIdx.x == 0) {
+    len[r] = (uint32_t)(p0 + j + 1);
+    row_seq[r] = b;
+  }
   reinterpret_cast<uint4*>(x + (size_t)r * kHidden)[threadIdx.x] =
       reinterpret_cast<const uint4*>(embed + (size_t)tok * kHidden)[threadIdx.x];
 }
@@ -319,8 +326,9 @@ int tc_state_allocate(InferenceManager& s, int sm_count) {
   if (s.act_h) return QWEN_OK;
   if (s.batch > kTcMaxNb)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "tensor-core step: batch %d > %d", s.batch, kTcMaxNb);
-  // A batch-1 engine also prefills in chunks of kTcPrefillRows positions.
-  s.tc_rows = s.batch == 1 ? kTcPrefillRows : s.batch;
+  // Prefills run in chunks of rows, kTcPrefillRows positions of a batch-1
+  // engine or kTcMaxNb (sequence, position) rows of a larger batch.
+  s.tc_rows = s.batch == 1 ? kTcPrefillRows : kTcMaxNb;
   s.tc_nb = act_rows(s.tc_rows);
   const TcPlan p = plan_for(sm_count);
   const size_t part = std::max((size_t)p.qkv * kQKVRows,
@@ -329,7 +337,7 @@ int tc_state_allocate(InferenceManager& s, int sm_count) {
   QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kHidden), (void**)&s.act_h));
   QWEN_TRY(s.alloc_tracked(act_bytes(s.tc_nb, kInter), (void**)&s.act_i));
   QWEN_TRY(s.alloc_tracked(part * sizeof(float), (void**)&s.tc_part));
-  if (s.tc_rows > s.batch) {
+  {
     const size_t R = (size_t)s.tc_rows;
     QWEN_TRY(s.alloc_tracked(R * kHidden * 2, (void**)&s.tc_px));
     QWEN_TRY(s.alloc_tracked(R * kHidden * 2, (void**)&s.tc_pq));
@@ -348,11 +356,13 @@ TcRows tc_decode_rows(InferenceManager& s) {
                 s.attn_scratch, s.attn_splits, s.logits};
 }
 
-int launch_prefill_rows(InferenceManager& s, const __half* embed, int p0, int rows,
+int launch_prefill_rows(InferenceManager& s, const __half* embed, int p0, int n_pos,
                         cudaStream_t st) {
-  if (!s.tc_px || rows < 1 || rows > s.tc_rows || p0 < 0 || p0 + rows > s.max_ctx)
+  const int rows = s.batch * n_pos;
+  if (!s.tc_px || n_pos < 1 || rows > s.tc_rows || p0 < 0 || p0 + n_pos > s.max_ctx)
     return set_error(QWEN_ERR_STATE, "chunked prefill: bad rows");
-  k_prefill_rows<<<rows, kHidden / 8, 0, st>>>(s.prompt, p0, embed, s.tc_px, s.tc_row_len);
+  k_prefill_rows<<<rows, kHidden / 8, 0, st>>>(s.prompt, s.max_ctx, p0, n_pos, embed, s.tc_px,
+                                               s.tc_row_len, s.tc_row_seq);
   return launch_status("prefill rows");
 }
 

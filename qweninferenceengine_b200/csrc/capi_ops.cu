@@ -91,7 +91,7 @@ using namespace qwen;
 extern "C" {
 
 const char* qwen_last_error(void) { return g_last_error.c_str(); }
-int qwen_abi_version(void) { return 1; }
+int qwen_abi_version(void) { return 2; }
 
 int qwen_gemv_q4_0(const uint8_t* packed, const uint16_t* scales, const uint16_t* x, uint16_t* y,
                    uint32_t k, const uint16_t* bias, uint32_t n_rows, void* stream) {
@@ -193,7 +193,7 @@ int qwen_attention_decode(const uint16_t* q, const uint16_t* k_cache, const uint
   p.max_ctx = max_ctx;
   p.out = HM(out);
   p.out_seq_stride = kHidden;
-  p.err = nullptr;
+  if (int rc = ops_status_word(&p.err)) return rc;
   attn_bind_scratch(p, scratch, splits, 1);
   if (launch_attention_decode(p, splits, 1, reinterpret_cast<cudaStream_t>(stream)) != 0)
     return set_error(QWEN_ERR_CUDA, "attention_decode: launch failed (%s)",
@@ -225,8 +225,10 @@ int qwen_sample(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uin
   if (temperature > 0.0f && !u24) return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: top-p needs u24");
   if (n_seq == 0) return QWEN_OK;
   if (n_seq > 65535) return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: n_seq=%u", n_seq);
+  int* status = nullptr;
+  if (int rc = ops_status_word(&status)) return rc;
   if (launch_sample(H(logits), (int)n_seq, (int)row_stride, (int)vocab, temperature, top_p, u24,
-                    out_ids, nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream)) != 0)
+                    out_ids, nullptr, status, reinterpret_cast<cudaStream_t>(stream)) != 0)
     return launch_status("sample");
   return QWEN_OK;
 }

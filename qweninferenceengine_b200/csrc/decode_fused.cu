@@ -45,7 +45,10 @@ constexpr int kNS = 14;                    // ring slots
 constexpr int kUnionBytes = 20480;         // x fragments + corrections / attention buffers
 constexpr int kMaxXFrags = kInter / 8;     // 1120 fragment units (K = 8960)
 static_assert(kMaxXFrags * 16 <= kUnionBytes, "x fragments exceed the union");
-constexpr uint64_t kWaitNs = 2000000000ull;  // a wait gives up after 2 s
+// Every dependency wait gives up after FusedParams::wait_ns (2 s by default).
+// The final drain of in-flight copies always allows 2 s: a CTA must not exit
+// while a bulk copy may still write its shared memory.
+constexpr uint64_t kDrainNs = 2000000000ull;
 
 constexpr int kOffUnion = kNS * kSlotBytes;
 constexpr int kOffXloc = kOffUnion + kUnionBytes;
@@ -73,11 +76,15 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kAttnWarpsFused * 6 * 128 * 4 <= kAPt, "warp merge buffer aliases the V rows");
 
 struct Misc {
+  unsigned long long wait_ns;   // FusedParams::wait_ns
+  int issued[kNS];              // bulk copies issued into each ring slot so far
   int abort;
   float scale;
   int cphase;           // phase the consumers are in (diagnostics)
   int last_rel[8];      // last item index each consumer warp released (diagnostics)
 };
+
+static_assert(sizeof(Misc) <= 128, "Misc exceeds its shared-memory region");
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void abar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
@@ -115,8 +122,19 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+// True once this CTA or any other has given up.  A CTA that sees another's
+// error raises its own abort flag first: a warp whose wait returned false
+// releases its slot without the data having landed, and the flag is what stops
+// that release from refilling the slot (release() checks it) -- a refill then
+// could put a second copy in flight into the slot, or skip a ring lap so the
+// exit drain would wait on the wrong phase.
 __device__ __forceinline__ bool aborted(volatile Misc* m, const int* err) {
-  return m->abort != 0 || *((volatile const int*)err) != 0;
+  if (m->abort != 0) return true;
+  if (*((volatile const int*)err) != 0) {
+    m->abort = 1;
+    return true;
+  }
+  return false;
 }
 // Records the timeout and where it happened: err[1] = site, err[2] = CTA,
 // err[3] = thread (the first failure wins).
@@ -133,6 +151,8 @@ enum WaitSite : int {
   kSiteEmpty = 1, kSiteFull = 2, kSiteXIn = 3, kSiteQ = 4, kSiteKV = 5, kSiteCombine = 6,
   kSiteAttnOut = 7, kSiteXMid = 8, kSiteH = 9, kSiteXFinal = 10
 };
+
+static_assert(kSiteH == kFusedStallH, "the stall hook's site is the h poll");
 
 // Polls units of 8 consecutive tagged fp16 words: unit u covers words
 // [8u, 8u+8).  Thread `tid` of `nthr` owns units tid, tid+nthr, ... (at most
@@ -169,7 +189,7 @@ __device__ __forceinline__ void poll_units(const uint32_t* src, int n_units, int
       if (aborted(m, err)) return;
       const uint64_t now = globaltimer();
       if (it == 0) t0 = now;
-      else if (now - t0 > kWaitNs) {
+      else if (now - t0 > m->wait_ns) {
         fail(m, err, site);
         return;
       }
@@ -188,7 +208,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volati
       if (aborted(m, err)) return false;
       const uint64_t now = globaltimer();
       if (it == 0) t0 = now;
-      else if (now - t0 > kWaitNs) {
+      else if (now - t0 > m->wait_ns) {
         fail(m, err, site);
         return false;
       }
@@ -209,7 +229,7 @@ __device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile const 
       if (aborted(m, err)) return false;
       const uint64_t now = globaltimer();
       if (it == 0) t0 = now;
-      else if (now - t0 > kWaitNs) {
+      else if (now - t0 > m->wait_ns) {
         fail(m, err, site);
         return false;
       }
@@ -590,7 +610,7 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
         if (aborted(misc, p.err)) break;
         const uint64_t now = globaltimer();
         if (it == 0) t0 = now;
-        else if (now - t0 > kWaitNs) {
+        else if (now - t0 > misc->wait_ns) {
           fail(misc, p.err, kSiteCombine * 100 + layer);
           break;
         }
@@ -632,7 +652,7 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
 // overwrite it; slot_item tells waiters the slot now holds item i.
 __device__ __noinline__ void issue_item(int i, const FusedItem* items, const FusedParams& p,
                                         int lm_phase, uint8_t* ring, uint64_t* full,
-                                        volatile int* slot_item) {
+                                        volatile int* slot_item, volatile int* issued) {
   const int slot = i % kNS;
   const ItemFields it = unpack_item(items[i]);
   size_t off;
@@ -644,6 +664,7 @@ __device__ __noinline__ void issue_item(int i, const FusedItem* items, const Fus
   bulk_g2s_stream(ring + slot * kSlotBytes, src, bytes, &full[slot], policy_evict_first());
   __threadfence_block();
   slot_item[slot] = i;
+  issued[slot] = issued[slot] + 1;
 }
 
 }  // namespace
@@ -676,7 +697,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       mbar_init(&full[i], 1);
       rel_cnt[i] = 0;
       slot_item[i] = -1;
+      misc->issued[i] = 0;
     }
+    misc->wait_ns = p.wait_ns;
     misc->abort = 0;
     misc->cphase = -1;
     for (int w = 0; w < 8; ++w) misc->last_rel[w] = -1;
@@ -687,7 +710,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
   if (threadIdx.x == 0) {
     if (trace) trace[0] = globaltimer();
-    for (int i = 0; i < kNS && i < n_items; ++i) issue_item(i, items, p, lm_phase, ring, full, slot_item);
+    for (int i = 0; i < kNS && i < n_items; ++i) issue_item(i, items, p, lm_phase, ring, full, slot_item, misc->issued);
   }
   {
     // ------------------------------------------------------------ consumers
@@ -710,7 +733,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         // (the shared abort flag only: a global read here would sit on the
         // issuing warp's path at every refill)
         if (i + kNS < n_items && !misc->abort)
-          issue_item(i + kNS, items, p, lm_phase, ring, full, slot_item);
+          issue_item(i + kNS, items, p, lm_phase, ring, full, slot_item, misc->issued);
       }
       misc->last_rel[warp] = i;
     };
@@ -984,7 +1007,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           {
             const int blo = warp * kBp8960 / kConsumerWarps;
             const int bhi = (warp + 1) * kBp8960 / kConsumerWarps;
-            poll_units<5>(p.h_ll + 64 * blo, 8 * (bhi - blo), lane, 32, tagof(layer), misc, p.err,
+            // (test hook: with stall_site == kSiteH the poll expects a tag
+            // nothing writes, so the wait runs out)
+            const uint32_t htag = p.stall_site == kSiteH ? tagof(255) : tagof(layer);
+            poll_units<5>(p.h_ll + 64 * blo, 8 * (bhi - blo), lane, 32, htag, misc, p.err,
                           kSiteH * 100 + layer, [&](int u, const __half* v) {
                             __half tmp[8];
 #pragma unroll
@@ -1061,14 +1087,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     stamp(3 + p.n_layers * kTraceStampsPerLayer + 1);
   }
   __syncthreads();
-  // Drain: every copy this CTA issued has landed before its shared memory goes away.
+  // Drain: every copy this CTA issued has landed before its shared memory goes
+  // away.  A slot's n-th copy completes its barrier's phase n - 1, so the
+  // wait is on the parity of the count of copies issued into it.
   if (threadIdx.x == 0) {
     const uint64_t t0 = globaltimer();
     for (int sl = 0; sl < kNS; ++sl) {
-      const int i = slot_item[sl];
-      if (i < 0) continue;
-      while (!mbar_try_wait(&full[sl], (i / kNS) & 1))
-        if (globaltimer() - t0 > kWaitNs) break;
+      const int n = misc->issued[sl];
+      if (n == 0) continue;
+      while (!mbar_try_wait(&full[sl], (uint32_t)(n - 1) & 1u))
+        if (globaltimer() - t0 > kDrainNs) break;
     }
     if (trace) trace[1] = globaltimer();
   }
@@ -1144,6 +1172,8 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
   p.n_layers = m.n_layers;
   p.max_ctx = s.max_ctx;
   p.kv_layer_stride = (int)s.kv_layer_stride();
+  p.wait_ns = a.wait_ns;
+  p.stall_site = a.stall_site;
   if (int rc = cuda_status(cudaFuncSetAttribute(k_decode_fused,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 kSmemBytes),

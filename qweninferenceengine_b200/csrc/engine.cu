@@ -315,6 +315,10 @@ int QwenEngine::init(const qwen_engine_config& cfg) {
   if (cfg.kernels != QWEN_KERNELS_FUSED && cfg.kernels != QWEN_KERNELS_OPS &&
       cfg.kernels != QWEN_KERNELS_TC)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "unknown kernels mode %d", cfg.kernels);
+  if (cfg.prefill_mode != QWEN_PREFILL_CHUNKED && cfg.prefill_mode != QWEN_PREFILL_STEPS)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "unknown prefill mode %d", cfg.prefill_mode);
+  if (cfg.ctx_overflow != QWEN_CTX_CLAMP && cfg.ctx_overflow != QWEN_CTX_ERROR)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "unknown ctx_overflow mode %d", cfg.ctx_overflow);
   if (cfg.kernels == QWEN_KERNELS_OPS && cfg.batch != 1)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "the per-op kernel path decodes one sequence");
   int ndev = 0;
@@ -345,9 +349,16 @@ int QwenEngine::load_weights(const std::string& dir) {
   return QWEN_OK;
 }
 
+// The fused engine keeps the tensor-core layout too when it prefills on the
+// tensor cores (both fit in HBM many times over: 1.2 GB each).
+bool QwenEngine::uses_tc_layout() const {
+  return cfg_.kernels == QWEN_KERNELS_TC ||
+         (cfg_.kernels == QWEN_KERNELS_FUSED && cfg_.prefill_mode == QWEN_PREFILL_CHUNKED);
+}
+
 int QwenEngine::build_step_weights() {
   if (cfg_.kernels == QWEN_KERNELS_FUSED) QWEN_TRY(build_fused_weights(model_, cfg_.max_ctx, stream_));
-  if (cfg_.kernels == QWEN_KERNELS_TC) QWEN_TRY(build_tc_weights(model_, cfg_.max_ctx, stream_));
+  if (uses_tc_layout()) QWEN_TRY(build_tc_weights(model_, cfg_.max_ctx, stream_));
   return QWEN_OK;
 }
 
@@ -417,7 +428,7 @@ int QwenEngine::enqueue_step_fused(cudaEvent_t* ev) {
   k_step_begin<<<s.batch, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
                                         s.max_ctx, cfg_.seed, s.err, s.epoch);
   if (ev) cudaEventRecord(ev[1], st);
-  FusedStepArgs a{&model_, &state_, model_.n_layers, sm_count_};
+  FusedStepArgs a{&model_, &state_, model_.n_layers, sm_count_, wait_ns_, stall_site_};
   QWEN_TRY(enqueue_fused_step(a, st));
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
@@ -461,7 +472,7 @@ int QwenEngine::ensure_graph() {
     QWEN_CUDA(cudaMemset(state_.fused_scratch, 0, bytes), "cudaMemset");
     state_.fused_scratch_bytes = bytes;
   }
-  if (cfg_.kernels == QWEN_KERNELS_TC) QWEN_TRY(tc_state_allocate(state_, sm_count_));
+  if (uses_tc_layout()) QWEN_TRY(tc_state_allocate(state_, sm_count_));
   sampler_prepare();
   QWEN_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "BeginCapture");
   const int rc = enqueue_step(nullptr);
@@ -524,6 +535,9 @@ int QwenEngine::forward(int32_t token, int32_t position, int32_t* next) {
   if (state_.batch != 1) return set_error(QWEN_ERR_INVALID_ARGUMENT, "forward() drives a batch-1 engine");
   if (position < 0) return set_error(QWEN_ERR_INVALID_ARGUMENT, "negative position");
   if (token < 0 || token >= kVocab) return set_error(QWEN_ERR_INVALID_ARGUMENT, "token id %d out of range", token);
+  if (cfg_.ctx_overflow == QWEN_CTX_ERROR && position >= state_.max_ctx)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "position %d past the context window (%d)", position,
+                     state_.max_ctx);
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_TRY(ensure_graph());
   // One step that reads `token` as a prompt token at `position`; positions
@@ -558,11 +572,37 @@ int QwenEngine::set_trace(int enable) {
     cudaFree(state_.trace);
     state_.trace = nullptr;
   }
-  // the captured step graph bakes in the trace pointer: rebuild it
+  drop_graph();  // the captured step graph bakes in the trace pointer
+  return QWEN_OK;
+}
+
+void QwenEngine::drop_graph() {
   if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
   if (graph_) cudaGraphDestroy(graph_);
   graph_exec_ = nullptr;
   graph_ = nullptr;
+}
+
+int QwenEngine::set_wait_timeout(uint64_t ns) {
+  if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
+  if (ns < 1000000ull || ns > 60000000000ull)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "wait timeout %llu ns outside [1 ms, 60 s]",
+                     (unsigned long long)ns);
+  QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
+  QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
+  wait_ns_ = ns;
+  drop_graph();  // the limit is a parameter of the captured launch
+  return QWEN_OK;
+}
+
+int QwenEngine::test_stall(int site) {
+  if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
+  if (site != 0 && site != kFusedStallH)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "no stall hook for wait site %d", site);
+  QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
+  QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
+  stall_site_ = site;
+  drop_graph();
   return QWEN_OK;
 }
 
@@ -658,8 +698,7 @@ int QwenEngine::prefill(const int32_t* ids, int32_t n) {
   if (n < 1) return set_error(QWEN_ERR_INVALID_ARGUMENT, "empty prompt");
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_TRY(ensure_graph());
-  if (cfg_.kernels == QWEN_KERNELS_TC && state_.batch == 1 && n > 1 && state_.tc_px)
-    return prefill_chunked(ids, n);
+  if (cfg_.prefill_mode == QWEN_PREFILL_CHUNKED && state_.tc_px && n > 1) return prefill_chunked(ids, n);
   QWEN_TRY(upload_prompt(ids, n, 0));
   std::vector<SeqCtl> c(state_.batch);
   for (auto& x : c) {
@@ -672,40 +711,49 @@ int QwenEngine::prefill(const int32_t* ids, int32_t n) {
   return check_device_error();
 }
 
-// Batch-1 prefill on the tensor cores: the prompt's positions go through the
-// model kTcPrefillRows at a time as the rows of one batched step (each row
-// attends to positions 0 .. its own, the rows before it in the chunk included,
-// since their K/V rows are written before attention runs).  The logits of the
-// last position are then sampled exactly as the sequential loop's last prompt
-// step samples them (InferenceEngine.swift:29-52): same uniform, same record.
+// Prefill on the tensor cores: the prompt positions of every sequence go
+// through the model as the rows of batched steps, a chunk of positions at a
+// time (kTcPrefillRows positions of a batch-1 engine, or as many positions as
+// fit kTcMaxNb rows).  Each row attends to positions 0 .. its own, the rows
+// before it in the chunk included, since the chunk's K/V rows are written
+// before its attention runs.  Only the last chunk runs the LM head, and only
+// each sequence's last position is sampled -- exactly as the sequential loop's
+// last prompt step samples it (InferenceEngine.swift:29-52): same uniform,
+// same record.  The reference's earlier prompt steps also sample, but their
+// ids are discarded (:34-36).
 int QwenEngine::prefill_chunked(const int32_t* ids, int32_t n) {
   InferenceManager& s = state_;
   cudaStream_t st = stream_;
   QWEN_TRY(upload_prompt(ids, n, 0));
-  const int C = s.tc_rows;
-  int last_rows = 0;
+  const int B = s.batch;
+  const int C = std::max(1, s.tc_rows / B);  // positions per chunk
+  int last = 0;
   for (int p0 = 0; p0 < n; p0 += C) {
-    const int rows = std::min(C, n - p0);
-    const bool final = p0 + rows == n;
-    QWEN_TRY(launch_prefill_rows(s, model_.embed, p0, rows, st));
-    const TcRows v{rows, s.tc_px, s.tc_pq, s.tc_row_len, 1, s.tc_row_seq, s.tc_pattn, s.tc_psplits,
+    const int np = std::min(C, n - p0);
+    const bool final = p0 + np == n;
+    QWEN_TRY(launch_prefill_rows(s, model_.embed, p0, np, st));
+    const TcRows v{B * np, s.tc_px, s.tc_pq, s.tc_row_len, 1, s.tc_row_seq, s.tc_pattn, s.tc_psplits,
                    final ? s.tc_plogits : nullptr};
     QWEN_TRY(enqueue_tc_model(model_, s, v, sm_count_, st));
-    last_rows = rows;
+    last = np;
   }
-  SeqCtl c;
-  std::memset(&c, 0, sizeof(c));
-  c.pos = n - 1;
-  c.n_prompt = n;
-  QWEN_CUDA(cudaMemcpyAsync(s.ctl, &c, sizeof(c), cudaMemcpyHostToDevice, st), "memcpy ctl");
-  k_step_begin<<<1, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_,
-                                  s.max_ctx, cfg_.seed, s.err, s.epoch);
-  QWEN_CUDA(cudaMemcpyAsync(s.logits, s.tc_plogits + (size_t)(last_rows - 1) * kVocab, kVocab * 2,
-                            cudaMemcpyDeviceToDevice, st), "memcpy logits");
-  if (launch_sample(s.logits, 1, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
+  std::vector<SeqCtl> c(B);
+  for (auto& x : c) {
+    std::memset(&x, 0, sizeof(x));
+    x.pos = n - 1;
+    x.n_prompt = n;
+  }
+  QWEN_CUDA(cudaMemcpyAsync(s.ctl, c.data(), sizeof(SeqCtl) * B, cudaMemcpyHostToDevice, st), "memcpy ctl");
+  k_step_begin<<<B, 256, 0, st>>>(s.ctl, s.prompt, s.max_ctx, model_.embed, s.x, s.u24_, s.max_ctx,
+                                  cfg_.seed, s.err, s.epoch);
+  // each sequence's last row of the final chunk: row b * last + last - 1
+  QWEN_CUDA(cudaMemcpy2DAsync(s.logits, (size_t)kVocab * 2, s.tc_plogits + (size_t)(last - 1) * kVocab,
+                              (size_t)last * kVocab * 2, (size_t)kVocab * 2, B, cudaMemcpyDeviceToDevice,
+                              st), "memcpy logits");
+  if (launch_sample(s.logits, B, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
                     s.sampled, nullptr, s.err, st) != 0)
     return launch_status("sample");
-  k_step_end<<<1, 1, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
+  k_step_end<<<1, B, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   QWEN_TRY(launch_status("chunked prefill"));
   QWEN_CUDA(cudaStreamSynchronize(st), "sync");
   return check_device_error();
@@ -723,6 +771,11 @@ int QwenEngine::decode(int32_t n_steps, int32_t* out) {
     for (auto& x : c)
       if (x.n_out + n_steps > state_.max_out)
         return set_error(QWEN_ERR_INVALID_ARGUMENT, "decode: %d more tokens exceed the output buffer", n_steps);
+  if (cfg_.ctx_overflow == QWEN_CTX_ERROR)
+    for (auto& x : c)
+      if (x.pos + n_steps > state_.max_ctx)
+        return set_error(QWEN_ERR_INVALID_ARGUMENT, "decode: %d more steps from position %d pass the "
+                         "context window (%d)", n_steps, x.pos, state_.max_ctx);
   QWEN_TRY(run_steps(n_steps));
   QWEN_TRY(check_device_error());
   if (out) {
@@ -739,6 +792,9 @@ int QwenEngine::generate(const int32_t* ids, int32_t n_prompt, int32_t max_token
                          int32_t* n_out) {
   if (max_tokens < 1) return set_error(QWEN_ERR_INVALID_ARGUMENT, "max_tokens must be >= 1");
   if (max_tokens > state_.max_out) return set_error(QWEN_ERR_INVALID_ARGUMENT, "max_tokens too large");
+  if (cfg_.ctx_overflow == QWEN_CTX_ERROR && (int64_t)n_prompt + max_tokens - 1 > state_.max_ctx)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "generate: %d prompt + %d generated positions pass the "
+                     "context window (%d)", n_prompt, max_tokens - 1, state_.max_ctx);
   QWEN_TRY(prefill(ids, n_prompt));
   // The reference runs maxTokens decode forwards and prints the token before
   // each one (InferenceEngine.swift:40-50); the last forward's result is never
@@ -776,6 +832,20 @@ int QwenEngine::get_kv(int32_t seq, int32_t layer, int32_t n_pos, uint16_t* hk, 
   return QWEN_OK;
 }
 
+int QwenEngine::set_kv(int32_t seq, int32_t layer, int32_t n_pos, const uint16_t* hk,
+                       const uint16_t* hv) {
+  if (seq < 0 || seq >= state_.batch || layer < 0 || layer >= state_.n_layers || n_pos < 0 ||
+      n_pos > state_.max_ctx)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "set_kv: bad arguments");
+  QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
+  const size_t off = (size_t)layer * state_.kv_layer_stride() + (size_t)seq * state_.kv_seq_stride();
+  const size_t bytes = (size_t)n_pos * kKVDim * 2;
+  if (hk) QWEN_CUDA(cudaMemcpyAsync(state_.kc + off, hk, bytes, cudaMemcpyHostToDevice, stream_), "memcpy");
+  if (hv) QWEN_CUDA(cudaMemcpyAsync(state_.vc + off, hv, bytes, cudaMemcpyHostToDevice, stream_), "memcpy");
+  QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
+  return QWEN_OK;
+}
+
 int QwenEngine::position(int32_t seq, int32_t* pos) {
   if (seq < 0 || seq >= state_.batch) return set_error(QWEN_ERR_INVALID_ARGUMENT, "bad sequence %d", seq);
   SeqCtl c;
@@ -807,6 +877,8 @@ void qwen_engine_config_default(qwen_engine_config* c) {
   c->top_p = 0.8f;
   c->seed = 0;
   c->stop_on_eos = 1;
+  c->ctx_overflow = QWEN_CTX_CLAMP;
+  c->prefill_mode = QWEN_PREFILL_CHUNKED;
 }
 
 int qwen_engine_create(const qwen_engine_config* cfg, qwen_engine** out) {
@@ -874,6 +946,11 @@ int qwen_engine_get_kv(qwen_engine* e, int32_t seq, int32_t layer, int32_t n_pos
   ENGINE_OR_FAIL(e);
   return e->impl.get_kv(seq, layer, n_pos, hk, hv);
 }
+int qwen_engine_set_kv(qwen_engine* e, int32_t seq, int32_t layer, int32_t n_pos,
+                       const uint16_t* hk, const uint16_t* hv) {
+  ENGINE_OR_FAIL(e);
+  return e->impl.set_kv(seq, layer, n_pos, hk, hv);
+}
 int qwen_engine_position(qwen_engine* e, int32_t seq, int32_t* pos) {
   ENGINE_OR_FAIL(e);
   if (!pos) return set_error(QWEN_ERR_INVALID_ARGUMENT, "null output");
@@ -908,6 +985,14 @@ int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n)
   const int rc = e->impl.profile_step(ms, cap, &v);
   *n = v;
   return rc;
+}
+int qwen_engine_set_wait_timeout(qwen_engine* e, uint64_t timeout_ns) {
+  ENGINE_OR_FAIL(e);
+  return e->impl.set_wait_timeout(timeout_ns);
+}
+int qwen_engine_test_stall(qwen_engine* e, int32_t site) {
+  ENGINE_OR_FAIL(e);
+  return e->impl.test_stall(site);
 }
 int qwen_engine_stream(qwen_engine* e, void** stream) {
   ENGINE_OR_FAIL(e);

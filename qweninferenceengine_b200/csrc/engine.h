@@ -153,11 +153,11 @@ class InferenceManager {
   float* tc_part = nullptr;      // fp32 split-K partials
   int tc_rows = 0;               // activation rows the buffers hold
   int tc_nb = 0;                 // tc_rows padded to 16
-  // chunked prefill of a batch-1 engine (rows = consecutive positions)
+  // chunked prefill (rows = (sequence, position) pairs of a chunk)
   __half *tc_px = nullptr, *tc_pq = nullptr;  // [tc_rows][1536]
   __half* tc_plogits = nullptr;  // [tc_rows][151936]
   uint32_t* tc_row_len = nullptr;  // [tc_rows] position + 1 of each row
-  int32_t* tc_row_seq = nullptr;   // [tc_rows] KV sequence of each row (0)
+  int32_t* tc_row_seq = nullptr;   // [tc_rows] KV sequence of each row
   void* tc_pattn = nullptr;      // attention scratch for tc_rows rows
   int tc_psplits = 0;
 
@@ -186,12 +186,15 @@ class QwenEngine {
                int32_t* n_out);
   int get_logits(int32_t seq, uint16_t* host);
   int get_kv(int32_t seq, int32_t layer, int32_t n_pos, uint16_t* hk, uint16_t* hv);
+  int set_kv(int32_t seq, int32_t layer, int32_t n_pos, const uint16_t* hk, const uint16_t* hv);
   int position(int32_t seq, int32_t* pos);
   int kernels_per_step(int* n) const;
   int set_trace(int enable);
   int get_trace(unsigned long long* host, size_t n, size_t* needed);
   int time_steps(int n, float* ms_step, float* ms_model);
   int profile_step(float* ms, int cap, int* n);
+  int set_wait_timeout(uint64_t ns);
+  int test_stall(int site);
   cudaStream_t stream() const { return stream_; }
 
  private:
@@ -206,6 +209,7 @@ class QwenEngine {
   int prefill_chunked(const int32_t* prompt_ids, int32_t n_prompt);
   int enqueue_step(cudaEvent_t* ev);
   int build_step_weights();
+  bool uses_tc_layout() const;
   int upload_prompt(const int32_t* prompt_ids, int32_t n_prompt, int32_t start_pos);
 
   qwen_engine_config cfg_{};
@@ -216,6 +220,9 @@ class QwenEngine {
   cudaGraph_t graph_ = nullptr;
   bool initialised_ = false;
   int sm_count_ = 0;
+  uint64_t wait_ns_ = 2000000000ull;  // device wait limit of the fused step
+  int stall_site_ = 0;                // test hook of the fused step
+  void drop_graph();
   struct HostStaging {
     int32_t token;
     SeqCtl ctl;
@@ -231,7 +238,11 @@ struct FusedStepArgs {
   InferenceManager* state;
   int n_layers;
   int sm_count;
+  unsigned long long wait_ns;  // device wait limit
+  int stall_site;              // test hook (0: none)
 };
+// Wait site of the fused step's h poll (down phase), for the stall test hook.
+constexpr int kFusedStallH = 9;
 int fused_scratch_bytes(int batch, int max_ctx, int sm_count, size_t* bytes);
 int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st);
 int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st);
@@ -258,9 +269,10 @@ TcRows tc_decode_rows(InferenceManager& s);
 // marks (optional): an event is recorded after every launch, (*n_marks)++.
 int enqueue_tc_model(QwenModel& m, InferenceManager& s, const TcRows& v, int sm_count,
                      cudaStream_t st, cudaEvent_t* marks = nullptr, int* n_marks = nullptr);
-// Rows for positions p0 .. p0+rows-1 of sequence 0: embeddings of its prompt
-// ids and lengths, on the device.
-int launch_prefill_rows(InferenceManager& s, const __half* embed, int p0, int rows,
+// Rows for positions p0 .. p0+n_pos-1 of every sequence of the batch (row
+// b * n_pos + j: sequence b, position p0 + j): embeddings of the prompt ids,
+// lengths and KV sequences, on the device.
+int launch_prefill_rows(InferenceManager& s, const __half* embed, int p0, int n_pos,
                         cudaStream_t st);
 int tc_kernels_per_step(int n_layers);
 constexpr int kTcPrefillRows = 128;  // positions per chunk of a batch-1 prefill

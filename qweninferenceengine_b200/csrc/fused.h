@@ -143,6 +143,8 @@ struct FusedParams {
   int n_layers;
   int max_ctx;
   int kv_layer_stride;        // elements between layers of kc / vc
+  unsigned long long wait_ns; // a dependency wait gives up after this long
+  int stall_site;             // test hook: a wait site made to run out (0: none)
 };
 
 }  // namespace qwen

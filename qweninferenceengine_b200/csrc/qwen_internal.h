@@ -7,7 +7,24 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace qwen {
+
+// ------------------------------------------------- __device__ symbols ----
+// Per-device cache of a __device__ symbol's address, keyed on the CUDA
+// context it was looked up in (a reset device gets a new lookup).
+struct DeviceSymbolCache {
+  static constexpr int kMaxDevices = 64;
+  std::mutex mu;
+  void* ctx[kMaxDevices] = {};
+  void* addr[kMaxDevices] = {};
+};
+// lookup: cudaGetSymbolAddress of the symbol, called in the symbol's own file.
+int symbol_address_cached(DeviceSymbolCache& cache, int (*lookup)(void**), void** out);
+// Device address of the operator status word (ops_status.cu) on the current
+// device: int[4], [0] the first DeviceError recorded by an operator kernel.
+int ops_status_word(int** out);
 
 // ---------------------------------------------------------- attention ----
 struct AttnParams {

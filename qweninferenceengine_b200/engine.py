@@ -8,7 +8,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (QWEN_KERNELS_FUSED, QWEN_KERNELS_OPS, QWEN_KERNELS_TC, EngineConfig, check,
+from ._lib import (QWEN_CTX_CLAMP, QWEN_CTX_ERROR, QWEN_KERNELS_FUSED, QWEN_KERNELS_OPS,
+                   QWEN_KERNELS_TC, QWEN_PREFILL_CHUNKED, QWEN_PREFILL_STEPS, EngineConfig, check,
                    lib)
 
 STOP_TOKENS = (151645, 151643)  # InferenceEngine.swift:41
@@ -35,6 +36,8 @@ class QwenConfig:
     device: int = 0
     kernels: str = "fused"   # "fused", "ops" or "tc" (tensor-core batched step)
     stop_on_eos: bool = True
+    ctx_overflow: str = "clamp"  # "clamp" (InferenceEngine.swift:55) or "error"
+    prefill: str = "chunked"     # "chunked" (tensor cores) or "steps" (InferenceEngine.swift:34-36)
 
 
 class QwenEngine:
@@ -60,6 +63,8 @@ class QwenEngine:
         cfg.top_p = c.top_p
         cfg.seed = c.seed
         cfg.stop_on_eos = 1 if c.stop_on_eos else 0
+        cfg.ctx_overflow = {"clamp": QWEN_CTX_CLAMP, "error": QWEN_CTX_ERROR}[c.ctx_overflow]
+        cfg.prefill_mode = {"chunked": QWEN_PREFILL_CHUNKED, "steps": QWEN_PREFILL_STEPS}[c.prefill]
         h = ctypes.c_void_p()
         check(lib().qwen_engine_create(ctypes.byref(cfg), ctypes.byref(h)))
         self._h = h
@@ -156,6 +161,15 @@ class QwenEngine:
                                        v.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16))))
         return k.view(np.float16), v.view(np.float16)
 
+    def set_kv(self, seq: int, layer: int, k: np.ndarray, v: np.ndarray) -> None:
+        """Writes positions [0, len(k)) of one layer's KV cache (fp16 [n][256])."""
+        k = np.ascontiguousarray(k, np.float16).view(np.uint16)
+        v = np.ascontiguousarray(v, np.float16).view(np.uint16)
+        assert k.shape == v.shape and k.ndim == 2 and k.shape[1] == 256
+        check(lib().qwen_engine_set_kv(self._h, seq, layer, k.shape[0],
+                                       k.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)),
+                                       v.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16))))
+
     def position(self, seq: int = 0) -> int:
         out = ctypes.c_int32()
         check(lib().qwen_engine_position(self._h, seq, ctypes.byref(out)))
@@ -196,6 +210,14 @@ class QwenEngine:
         check(lib().qwen_engine_get_trace(self._h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
                                           out.size, ctypes.byref(need)))
         return out
+
+    def set_wait_timeout(self, ns: int) -> None:
+        """Device wait limit of the fused step (qwen_engine_set_wait_timeout)."""
+        check(lib().qwen_engine_set_wait_timeout(self._h, int(ns)))
+
+    def test_stall(self, site: int) -> None:
+        """Test hook: make the fused step's waits at `site` run out (0: off)."""
+        check(lib().qwen_engine_test_stall(self._h, site))
 
     def stream(self) -> int:
         s = ctypes.c_void_p()

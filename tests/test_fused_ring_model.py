@@ -182,3 +182,125 @@ def test_model_catches_a_missing_slot_tag_check():
         except AssertionError:
             caught += 1
     assert caught > 0
+
+
+def simulate_abort(n_layers, n_gu, n_lm_tiles, seed, propagate=True, drain_by_count=True):
+    """The ring when another CTA gives up part way (the global error word is set
+    at a random moment).  From then on a warp's wait returns false as soon as it
+    looks (skipping the read) and the warp still releases its share, as the
+    kernel does.  With `propagate` the warp that sees the error raises the
+    CTA's own abort flag first, and a completed release refills only while that
+    flag is clear; without it (the kernel before the fix) only the CTA that timed
+    out stops refilling.  At exit thread 0 drains: per slot it waits (bounded)
+    on the phase of the slot's last copy -- by the count of copies issued into
+    the slot, or (the old way) by the last item's index.  Returns the problems
+    seen: a second copy put in flight into a slot, or a copy still in flight
+    when the CTA exits."""
+    rnd = random.Random(seed)
+    items, shares, phase_of, n_phases = plan(n_layers, n_gu, n_lm_tiles)
+    n = len(items)
+    slot_item = [-1] * KNS
+    issued = [0] * KNS
+    rel_cnt = [0] * KNS
+    completed = [0] * KNS
+    inflight = []
+    problems = []
+    err = [False]
+    local_abort = [False]
+    strike = rnd.randrange(50, 4000)
+    at_barrier = [0] * n_phases
+
+    def issue(i):
+        s = i % KNS
+        if any(j % KNS == s for j in inflight):
+            problems.append(("second copy in flight", s))
+        slot_item[s] = i
+        issued[s] += 1
+        inflight.append(i)
+
+    for i in range(min(KNS, n)):
+        issue(i)
+
+    def aborted():
+        if local_abort[0]:
+            return True
+        if err[0]:
+            if propagate:
+                local_abort[0] = True
+            return True
+        return False
+
+    def warp(w):
+        for ph in range(n_phases):
+            for i in range(n):
+                if phase_of[i] != ph or w not in shares[i]:
+                    continue
+                ok = True
+                while slot_item[i % KNS] != i:
+                    if aborted():
+                        ok = False
+                        break
+                    yield
+                if ok:
+                    parity = (i // KNS) & 1
+                    while (completed[i % KNS] & 1) == parity:
+                        if aborted():
+                            ok = False
+                            break
+                        yield
+                yield
+                s = i % KNS
+                rel_cnt[s] += shares[i][w]
+                if rel_cnt[s] == WARPS:
+                    rel_cnt[s] = 0
+                    if i + KNS < n and not local_abort[0]:
+                        issue(i + KNS)
+            at_barrier[ph] += 1
+            while at_barrier[ph] < WARPS:
+                yield
+
+    def copy_engine():
+        while True:
+            if inflight and rnd.random() < 0.4:
+                i = inflight.pop(rnd.randrange(len(inflight)))
+                completed[i % KNS] += 1
+            yield
+
+    eng = copy_engine()
+    alive = [warp(w) for w in range(WARPS)]
+    steps = 0
+    while alive:
+        steps += 1
+        if steps == strike:
+            err[0] = True
+        a = rnd.choice(alive + [eng])
+        try:
+            next(a)
+        except StopIteration:
+            alive.remove(a)
+        assert steps < 3_000_000
+    for s in range(KNS):                       # the drain, a bounded wait per slot
+        if issued[s] == 0:
+            continue
+        parity = (issued[s] - 1) & 1 if drain_by_count else (slot_item[s] // KNS) & 1
+        for _ in range(2000):
+            if (completed[s] & 1) != parity:
+                break
+            next(eng)
+    if inflight:
+        problems.append(("copy in flight at exit", len(inflight)))
+    return problems
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_abort_path_leaves_no_copy_in_flight(seed):
+    assert simulate_abort(n_layers=1, n_gu=8, n_lm_tiles=30, seed=seed) == []
+
+
+def test_model_catches_the_unpropagated_abort():
+    """The kernel before the fix (a CTA kept refilling after another CTA's
+    timeout, and drained by item index) could exit with a copy in flight --
+    the model must show it."""
+    bad = sum(bool(simulate_abort(n_layers=1, n_gu=8, n_lm_tiles=30, seed=s, propagate=False,
+                                  drain_by_count=False)) for s in range(40))
+    assert bad > 0

@@ -80,38 +80,63 @@ def test_tc_batch_generate_greedy(cuda, oracle, small_model):
             assert margins[diff[0]] < LOGIT_ABS, f"seq {b} parts at step {diff[0]}"
 
 
-def test_tc_chunked_prefill_matches_sequential_oracle(cuda, oracle, small_model):
-    # batch 1 on the tensor-core path prefills 128 positions per batched step;
-    # 300 positions = chunks of 128, 128, 44.  The result must match the
-    # reference's one-token-at-a-time loop (InferenceEngine.swift:29-52).
+@pytest.mark.parametrize("kernels,B", [("tc", 1), ("fused", 1), ("tc", 4)])
+def test_chunked_prefill_matches_sequential_oracle(cuda, oracle, small_model, kernels, B):
+    """The tensor-core prefill (a batch-1 engine: 128 positions per chunk, 300
+    positions = chunks of 128, 128, 44; a batch of 4: 64 positions of every
+    sequence per chunk of 256 rows) must match the reference's
+    one-token-at-a-time loop (InferenceEngine.swift:29-52) for every sequence:
+    logits of the last prompt position, the K/V cache, and the greedy
+    continuation decoded by the engine's own step (fused or tensor-core)."""
     n, gen = 300, 6
-    prompt = np.random.default_rng(23).integers(0, 151936, size=n).astype(np.int32)
-    cfg = QwenConfig(num_layers=2, max_context_window=512, temperature=0.0, kernels="tc",
-                     stop_on_eos=False)
+    prompts = np.stack([np.random.default_rng(23 + b).integers(0, 151936, size=n)
+                        for b in range(B)]).astype(np.int32)
+    cfg = QwenConfig(num_layers=2, max_context_window=512, temperature=0.0, kernels=kernels,
+                     batch=B, stop_on_eos=False)
     eng = QwenEngine(small_model, cfg)
-    eng.prefill(prompt)
-    got = eng.logits()
-    om = OracleModel(oracle, small_model, 2, 512)
-    for i in range(n - 1):
-        om.forward(int(prompt[i]), i, want_logits=False)
-    ref = om.forward(int(prompt[-1]), n - 1)
-    check_logits(got, ref)
-    k, v = eng.kv(0, 1, n)
-    assert np.abs(k.astype(np.float32) - om.k_cache(1)[:n].astype(np.float32)).max() < 2e-2
-    assert np.abs(v.astype(np.float32) - om.v_cache(1)[:n].astype(np.float32)).max() < 2e-2
-    assert eng.position() == n
-    # greedy continuation from the chunked prefill
-    out = eng.decode(gen - 1)[0].tolist()
-    first = oracle.sample_greedy(ref)
-    ref_ids, margins, lg, cur = [first], [top2_margin(ref)], ref, first
-    for j in range(gen - 1):
-        lg = om.forward(cur, n + j)
-        cur = oracle.sample_greedy(lg)
-        ref_ids.append(cur)
-        margins.append(top2_margin(lg))
-    om.close()
+    eng.prefill(prompts)
+    got = [eng.logits(b) for b in range(B)]
+    kv = [eng.kv(b, 1, n) for b in range(B)]
+    assert all(eng.position(b) == n for b in range(B))
+    out = eng.decode(gen - 1)
     eng.close()
-    assert len(out) == gen - 1
-    diff = [j for j in range(gen - 1) if out[j] != ref_ids[j + 1]]
-    if diff:
-        assert margins[diff[0] + 1] < LOGIT_ABS
+    for b in range(B):
+        om = OracleModel(oracle, small_model, 2, 512)
+        for i in range(n - 1):
+            om.forward(int(prompts[b, i]), i, want_logits=False)
+        ref = om.forward(int(prompts[b, -1]), n - 1)
+        check_logits(got[b], ref)
+        k, v = kv[b]
+        assert np.abs(k.astype(np.float32) - om.k_cache(1)[:n].astype(np.float32)).max() < 2e-2
+        assert np.abs(v.astype(np.float32) - om.v_cache(1)[:n].astype(np.float32)).max() < 2e-2
+        # greedy continuation from the chunked prefill
+        first = oracle.sample_greedy(ref)
+        ref_ids, margins, lg, cur = [first], [top2_margin(ref)], ref, first
+        for j in range(gen - 1):
+            lg = om.forward(cur, n + j)
+            cur = oracle.sample_greedy(lg)
+            ref_ids.append(cur)
+            margins.append(top2_margin(lg))
+        om.close()
+        seq = out[b].tolist()
+        assert len(seq) == gen - 1
+        diff = [j for j in range(gen - 1) if seq[j] != ref_ids[j + 1]]
+        if diff:
+            assert margins[diff[0] + 1] < LOGIT_ABS, f"seq {b} parts at step {diff[0] + 1}"
+
+
+def test_prefill_modes_agree_on_the_fused_engine(cuda, oracle, small_model):
+    """QWEN_PREFILL_STEPS (the reference's loop on the fused step) and the
+    default chunked prefill leave logits within the oracle tolerance of each
+    other, and the same greedy next token where the margin allows."""
+    n = 150
+    prompt = np.random.default_rng(31).integers(0, 151936, size=n).astype(np.int32)
+    res = {}
+    for mode in ("steps", "chunked"):
+        eng = QwenEngine(small_model, QwenConfig(num_layers=2, max_context_window=256,
+                                                  temperature=0.0, prefill=mode,
+                                                  stop_on_eos=False))
+        eng.prefill(prompt)
+        res[mode] = eng.logits()
+        eng.close()
+    check_logits(res["chunked"], res["steps"])

@@ -3,9 +3,16 @@
 oracle through the reference's generate loop (InferenceEngine.swift:29-52);
 fixture and generator in tests/golden/ (make_config3.py).
 
-The engine computes in a different summation order than the oracle, so a
-greedy pick may flip where the oracle's two best logits are closer than the
-logit tolerance; the test allows the sequences to part only at such a step.
+The engine sums in a different order than the oracle, so a greedy pick may
+flip where the oracle's two best logits are closer than the logit tolerance;
+after such a flip the free-running sequences go their own ways.  So the test
+runs the engine twice:
+  * free-running (generate): it may part from the golden ids only at a step
+    whose oracle top-2 margin is below the tolerance;
+  * teacher-forced: every step is fed the golden token of the previous step
+    (forward(token, position), InferenceEngine.swift:54-271), so all 256 steps
+    are compared; the engine's pick must equal the oracle's at every step whose
+    margin is at least the tolerance.
 """
 import json
 import os
@@ -33,20 +40,33 @@ def model_dir(oracle, golden):
     return make_weight_dir(oracle, 28, golden["weight_seed"])
 
 
-@pytest.mark.parametrize("kernels", ["fused", "ops"])
+@pytest.mark.parametrize("kernels", ["fused", "ops", "tc"])
 def test_full_model_greedy_256(cuda, golden, model_dir, kernels):
+    n_prompt = golden["n_prompt"]
     prompt = np.random.default_rng(golden["prompt_seed"]).integers(
-        0, 151936, size=golden["n_prompt"]).astype(np.int32)
-    want = golden["tokens"]
+        0, 151936, size=n_prompt).astype(np.int32)
+    want, margin = golden["tokens"], golden["top2_margin"]
     cfg = QwenConfig(num_layers=28, max_context_window=512, temperature=0.0, kernels=kernels,
                      stop_on_eos=False)
     eng = QwenEngine(model_dir, cfg)
     got = eng.generate(prompt.tolist(), max_tokens=len(want))
-    eng.close()
     assert len(got) == len(want)
     diff = [i for i in range(len(want)) if got[i] != want[i]]
     if diff:
         j = diff[0]
-        assert golden["top2_margin"][j] < LOGIT_ABS, (
+        assert margin[j] < LOGIT_ABS, (
             f"greedy ids part at step {j} ({got[j]} vs {want[j]}) with oracle top-2 margin "
-            f"{golden['top2_margin'][j]:.4f}")
+            f"{margin[j]:.4f}")
+
+    # Teacher-forced: step j + 1 reads the golden token of step j at its position.
+    pred = [got[0]]
+    for j in range(len(want) - 1):
+        pred.append(eng.forward(want[j], n_prompt + j))
+    eng.close()
+    limited = [j for j in range(len(want)) if margin[j] < LOGIT_ABS]
+    wrong = [j for j in range(len(want)) if pred[j] != want[j]]
+    print(f"{kernels}: free run parts at step {diff[0] if diff else None}; "
+          f"{len(limited)} margin-limited steps; teacher-forced mismatches at {wrong}")
+    bad = [j for j in wrong if margin[j] >= LOGIT_ABS]
+    assert not bad, [(j, pred[j], want[j], margin[j]) for j in bad]
+    assert len(wrong) <= len(limited)

@@ -15,7 +15,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-from qweninferenceengine_b200._lib import QWEN_OK, lib  # noqa: E402
+from qweninferenceengine_b200._lib import QWEN_ERR_INVALID_ARGUMENT, QWEN_OK, lib  # noqa: E402
 from test_gpu_ops import assert_close16  # noqa: E402
 
 
@@ -31,9 +31,13 @@ def test_noalloc_matches_allocating_entry_point(cuda):
     L = lib()
     L.qwen_attention_decode_noalloc.restype = ctypes.c_int
     L.qwen_attention_decode_noalloc.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_uint32, ctypes.c_void_p]
+    L.qwen_ops_status.restype = ctypes.c_int
+    L.qwen_ops_status.argtypes = [ctypes.c_void_p]
     rng = np.random.default_rng(99)
-    # two calls in a row with different lengths: the second reuses the array the first left behind
-    for L_ctx, max_ctx in ((777, 1024), (40, 1024)):
+    # calls in a row that each reuse the array the one before left behind, with
+    # different lengths and split counts: 13 of 16, 1, 32 of 32 (the split count
+    # that sizes the array, max_ctx >= 2048), then 16 of 32 and 1 of 1 again
+    for L_ctx, max_ctx in ((777, 1024), (40, 1024), (4000, 4096), (1000, 4096), (50, 64)):
         q = torch.from_numpy(rng.standard_normal(1536).astype(np.float16)).cuda()
         kc = torch.from_numpy(rng.standard_normal((max_ctx, 256)).astype(np.float16)).cuda()
         vc = torch.from_numpy(rng.standard_normal((max_ctx, 256)).astype(np.float16)).cuda()
@@ -44,6 +48,32 @@ def test_noalloc_matches_allocating_entry_point(cuda):
         _call(L.qwen_attention_decode_noalloc, q, kc, vc, got, sl, max_ctx)
         torch.cuda.synchronize()
         assert_close16(got.cpu().numpy(), want.cpu().numpy())
+    assert L.qwen_ops_status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == QWEN_OK
+
+
+def test_noalloc_reports_a_length_beyond_max_ctx(cuda):
+    """A device-side length the kernel rejects (L > max_ctx) is recorded in the
+    operator status word -- no allocation needed -- and qwen_ops_status reports
+    it once; the output is left untouched and the next call works."""
+    L = lib()
+    L.qwen_attention_decode_noalloc.restype = ctypes.c_int
+    L.qwen_attention_decode_noalloc.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_uint32, ctypes.c_void_p]
+    L.qwen_ops_status.restype = ctypes.c_int
+    L.qwen_ops_status.argtypes = [ctypes.c_void_p]
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    q = torch.zeros(1536, dtype=torch.float16, device="cuda")
+    kc = torch.zeros((64, 256), dtype=torch.float16, device="cuda")
+    out = torch.full((1536,), 7.0, dtype=torch.float16, device="cuda")
+    sl = torch.tensor([65], dtype=torch.int32, device="cuda")
+    _call(L.qwen_attention_decode_noalloc, q, kc, kc, out, sl, 64)
+    assert L.qwen_ops_status(stream) == QWEN_ERR_INVALID_ARGUMENT
+    assert b"out-of-range" in L.qwen_last_error()
+    assert bool((out == 7.0).all())
+    assert L.qwen_ops_status(stream) == QWEN_OK          # reported once
+    sl.fill_(64)
+    _call(L.qwen_attention_decode_noalloc, q, kc, kc, out, sl, 64)
+    assert L.qwen_ops_status(stream) == QWEN_OK
+    assert bool((out == 0.0).all())                       # zero V rows: zero output
 
 
 def test_noalloc_rejects_oversized_request(cuda):
