@@ -307,12 +307,12 @@ int qwen_engine_profile_step(qwen_engine* e, float* ms, int32_t cap, int32_t* n)
  * %globaltimer stamps: [0] producer start, [1] producer done, [2] consumer
  * start, then 10 per layer at [3 + 10*layer + k]: k = 0 layer start, 1 x ready,
  * 2 QKV done, 3 attention done, 4 attention output ready, 5 O done, 6 gate/up
- * input ready, 7 gate/up done, 8 h ready, 9 down done; then LM-head start and
+ * input ready, 7 gate/up done (h fragments ready), 8 the CTA's down partial
+ * sums written, 9 its rows of the layer output written; then LM-head start and
  * consumer end; then 7 stamps inside the attention unit of layer n_layers/2
  * (unit start, q/k/v in, warp 0's positions done, the unit's warps merged,
  * partials written, all splits' partials in, output slice written; zero on
- * CTAs without a unit), then warp 0's nanoseconds spent waiting for weight
- * slots in that layer's gate/up and down phases; stride 3 + 10*n_layers + 2 + 9.
+ * CTAs without a unit); stride 3 + 10*n_layers + 2 + 7.
  * qwen_engine_get_trace copies the last step's stamps ([grid][stride]) when
  * n >= *needed, and always reports *needed. */
 int qwen_engine_trace(qwen_engine* e, int32_t enable);
@@ -325,11 +325,11 @@ int qwen_engine_get_trace(qwen_engine* e, uint64_t* host, size_t n, size_t* need
  * without limit: commandBuffer.waitUntilCompleted, InferenceEngine.swift:266-268.) */
 int qwen_engine_set_wait_timeout(qwen_engine* e, uint64_t timeout_ns);
 
-/* Test hook, no reference counterpart: site 9 makes every down-phase wait of
- * the fused step expect data that nothing writes, so the waits run out and
- * the timeout path runs; site 0 turns the hook off. */
+/* Test hook, no reference counterpart: site 9 makes the fused step's waits for
+ * the down projection's partial sums expect data that nothing writes, so the
+ * waits run out and the timeout path runs; site 0 turns the hook off. */
 #define QWEN_STALL_NONE 0
-#define QWEN_STALL_FUSED_H 9
+#define QWEN_STALL_FUSED_DOWN 9
 int qwen_engine_test_stall(qwen_engine* e, int32_t site);
 
 /* Device and stream the engine runs on (for callers that time it). */

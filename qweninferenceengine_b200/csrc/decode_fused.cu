@@ -42,6 +42,14 @@ namespace qwen {
 namespace {
 
 constexpr int kNS = 14;                    // ring slots
+// The down strip: kWarpsPerDownItem warps share each of the kDownItems items.
+constexpr int kWarpsPerDownItem = kConsumerWarps / kDownItems;                 // 2
+constexpr int kDownRowTilesPerWarp = kDownItemTiles / kWarpsPerDownItem;       // 12
+static_assert(kWarpsPerDownItem * kDownItems == kConsumerWarps, "warps per down item");
+static_assert(kDownRowTilesPerWarp % 6 == 0, "down row tiles a warp: groups of three, stores by pairs");
+// Rows of the layer output each CTA finishes, and the partial sums it reads.
+constexpr int kMaxReduceRows = (kHidden + kMlpUnits - 1) / kMlpUnits + 1;   // grid >= kMlpUnits
+constexpr int kReducePerThread = (kMaxReduceRows * kMlpUnits + kFusedThreads - 1) / kFusedThreads;
 constexpr int kUnionBytes = 20480;         // x fragments + corrections / attention buffers
 constexpr int kMaxXFrags = kInter / 8;     // 1120 fragment units (K = 8960)
 static_assert(kMaxXFrags * 16 <= kUnionBytes, "x fragments exceed the union");
@@ -57,8 +65,14 @@ constexpr int kOffRed = kOffXn + kHidden * 2;
 constexpr int kOffRed2 = kOffRed + kConsumerWarps * 16 * 4;
 constexpr int kOffBars = kOffRed2 + 64;
 constexpr int kOffMisc = kOffBars + 2 * kNS * 8;
-constexpr int kOffItems = kOffMisc + 128;
-constexpr int kSmemBytes = kOffItems + kMaxItemsPerCta * 8;
+constexpr int kMiscBytes = 128;
+constexpr int kOffItems = kOffMisc + kMiscBytes;
+// Trace stamps of this CTA (when tracing), kept in shared memory during the
+// step and copied out at exit: a global store would make the next release's
+// block-scope fence wait for it and distort what it measures.
+constexpr int kMaxTraceStride = 3 + kLayers * kTraceStampsPerLayer + 2 + kAttnTraceStamps;
+constexpr int kOffTrace = kOffItems + kMaxItemsPerCta * 8;
+constexpr int kSmemBytes = kOffTrace + kMaxTraceStride * 8;
 
 // attention buffers inside the union region
 constexpr int kAVs = 0;                                   // [4][16][272] V rows
@@ -68,6 +82,11 @@ constexpr int kAWl = kAWm + kAttnWarpsFused * 8 * 4;
 constexpr int kAKnew = kAWl + kAttnWarpsFused * 8 * 4;    // [128] fp16 new k
 constexpr int kAVnew = kAKnew + 256;                      // [128] fp16 new v
 static_assert(kAVnew + 256 <= kUnionBytes, "attention buffers exceed the union region");
+// MLP buffers inside the union region, after the gate/up x fragments (K = 1536).
+constexpr int kOffHFrag = kHidden / 8 * 16;                  // [8] uint4: the unit's h fragments
+constexpr int kOffMlpStage = kOffHFrag + kGUTilesPerUnit * 16;  // [rows][140] fp32 partials
+static_assert(kOffMlpStage + kMaxReduceRows * kMlpUnits * 4 <= kUnionBytes,
+              "MLP buffers exceed the union region");
 // Merge factors, after the warp merge buffer (which aliases the dead V rows).
 constexpr int kAFac = kAVs + kAttnWarpsFused * 6 * 128 * 4;  // 36 floats
 constexpr int kACFac = kAFac + 256;                           // [74][2] + [6] floats
@@ -84,7 +103,7 @@ struct Misc {
   int last_rel[8];      // last item index each consumer warp released (diagnostics)
 };
 
-static_assert(sizeof(Misc) <= 128, "Misc exceeds its shared-memory region");
+static_assert(sizeof(Misc) <= kMiscBytes, "Misc exceeds its shared-memory region");
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void abar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
@@ -149,10 +168,10 @@ __device__ __forceinline__ void fail(volatile Misc* m, int* err, int site) {
 // Wait sites (x 100 + layer) reported by fail().
 enum WaitSite : int {
   kSiteEmpty = 1, kSiteFull = 2, kSiteXIn = 3, kSiteQ = 4, kSiteKV = 5, kSiteCombine = 6,
-  kSiteAttnOut = 7, kSiteXMid = 8, kSiteH = 9, kSiteXFinal = 10
+  kSiteAttnOut = 7, kSiteXMid = 8, kSiteDownPart = 9, kSiteXFinal = 10
 };
 
-static_assert(kSiteH == kFusedStallH, "the stall hook's site is the h poll");
+static_assert(kSiteDownPart == kFusedStallDownPart, "the stall hook's site is the partials poll");
 
 // Polls units of 8 consecutive tagged fp16 words: unit u covers words
 // [8u, 8u+8).  Thread `tid` of `nthr` owns units tid, tid+nthr, ... (at most
@@ -652,7 +671,7 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
 // overwrite it; slot_item tells waiters the slot now holds item i.
 __device__ __noinline__ void issue_item(int i, const FusedItem* items, const FusedParams& p,
                                         int lm_phase, uint8_t* ring, uint64_t* full,
-                                        volatile int* slot_item, volatile int* issued) {
+                                        volatile int* slot_item, volatile Misc* misc) {
   const int slot = i % kNS;
   const ItemFields it = unpack_item(items[i]);
   size_t off;
@@ -664,7 +683,7 @@ __device__ __noinline__ void issue_item(int i, const FusedItem* items, const Fus
   bulk_g2s_stream(ring + slot * kSlotBytes, src, bytes, &full[slot], policy_evict_first());
   __threadfence_block();
   slot_item[slot] = i;
-  issued[slot] = issued[slot] + 1;
+  misc->issued[slot] = misc->issued[slot] + 1;
 }
 
 }  // namespace
@@ -707,10 +726,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   }
   __syncthreads();
 
-  unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
+  unsigned long long* trace_out = p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
+  unsigned long long* trace =
+      trace_out ? reinterpret_cast<unsigned long long*>(smem + kOffTrace) : nullptr;
+  if (trace)
+    for (int i = threadIdx.x; i < p.trace_stride; i += blockDim.x) trace[i] = 0;
+  __syncthreads();
   if (threadIdx.x == 0) {
     if (trace) trace[0] = globaltimer();
-    for (int i = 0; i < kNS && i < n_items; ++i) issue_item(i, items, p, lm_phase, ring, full, slot_item, misc->issued);
+    for (int i = 0; i < kNS && i < n_items; ++i) issue_item(i, items, p, lm_phase, ring, full, slot_item, misc);
   }
   {
     // ------------------------------------------------------------ consumers
@@ -733,7 +757,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         // (the shared abort flag only: a global read here would sit on the
         // issuing warp's path at every refill)
         if (i + kNS < n_items && !misc->abort)
-          issue_item(i + kNS, items, p, lm_phase, ring, full, slot_item, misc->issued);
+          issue_item(i + kNS, items, p, lm_phase, ring, full, slot_item, misc);
       }
       misc->last_rel[warp] = i;
     };
@@ -744,17 +768,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     };
     // K-split processing of items [cur, e): warp w takes block pairs w, w+8, ...
     // of every chunk; the tile's 16 sums meet in shared memory at its last chunk.
-    // Trace: warp 0's time waiting for weight slots in the gate/up ([0]) and
-    // down ([1]) phases of the middle layer.
-    unsigned long long* wtrace =
-        trace ? trace + 3 + p.n_layers * kTraceStampsPerLayer + 2 + 7 : nullptr;
-    int wsel = -1;
     auto timed_wait = [&](int i, int site) {
-      if (!wtrace || ct != 0 || wsel < 0) return item_wait(i, full, slot_item, misc, p.err, site);
-      const uint64_t t0 = globaltimer();
-      const bool ok = item_wait(i, full, slot_item, misc, p.err, site);
-      wtrace[wsel] += globaltimer() - t0;
-      return ok;
+      return item_wait(i, full, slot_item, misc, p.err, site);
     };
     auto ksplit = [&](int e, auto&& epilogue) {
       float acc_g = 0.f, acc_g8 = 0.f;
@@ -780,51 +795,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           }
           cbar();
         }
-      }
-      cur = e;
-    };
-    // Down tiles (K = 8960: kBp8960 block pairs in chunks of kDownChunkBp):
-    // each warp takes a contiguous 1/8 of the tile's block pairs, so it waits
-    // for and releases only the one or two chunks its range touches, found
-    // arithmetically, and streams its pairs back to back.  Striding every
-    // chunk over all warps cost each warp a slot wait, three block pairs and
-    // a release per chunk (~0.8 us per chunk).  A chunk's empty barrier still
-    // gets kConsumerWarps arrivals in all: the first warp touching it adds the
-    // share of the warps that do not.
-    auto ksplit_down = [&](int e, auto&& epilogue) {
-      constexpr int kChunks = (kBp8960 + kDownChunkBp - 1) / kDownChunkBp;
-      auto lo_of = [](int w) { return w * kBp8960 / kConsumerWarps; };
-      const int lo = lo_of(warp), hi = lo_of(warp + 1);
-      for (int a = cur; a + kChunks <= e; a += kChunks) {  // items [a, a + kChunks): one tile
-        float acc_g = 0.f, acc_g8 = 0.f;
-        for (int c = lo / kDownChunkBp; c <= (hi - 1) / kDownChunkBp; ++c) {
-          const int i = a + c;
-          const ItemFields it = unpack_item(items[i]);
-          const int i0 = it.k0, i1 = it.k0 + it.nk;
-          const int s0 = max(lo, i0), s1 = min(hi, i1);
-          int wfirst = -1, ntouch = 0;  // warps whose ranges meet this chunk
-          for (int w = 0; w < kConsumerWarps; ++w)
-            if (max(lo_of(w), i0) < min(lo_of(w + 1), i1)) {
-              if (wfirst < 0) wfirst = w;
-              ++ntouch;
-            }
-          const int slot = i % kNS;
-          if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
-            q4_chunk3(ring + slot * kSlotBytes, it.k0, s0 - i0, s1 - i0, 1, xf, lane, acc_g, acc_g8);
-          __syncwarp();
-          if (lane == 0) release(i, warp == wfirst ? (uint32_t)(kConsumerWarps - ntouch + 1) : 1u);
-        }
-        if (t == 0) {
-          red[warp * 16 + g] = acc_g;
-          red[warp * 16 + g + 8] = acc_g8;
-        }
-        cbar();
-        if (ct < 16) {
-          float sum = 0.f;
-          for (int w = 0; w < kConsumerWarps; ++w) sum += red[w * 16 + ct];
-          epilogue((int)unpack_item(items[a]).tile, ct, sum);
-        }
-        cbar();
       }
       cur = e;
     };
@@ -957,24 +927,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         }
       }
       lstamp(layer, kTsODone);
-      // ---- P4: x -> RMSNorm -> gate|up -> SwiGLU -> h (each warp owns whole tiles)
+      // ---- P4: x' -> RMSNorm -> gate|up -> SwiGLU -> h.  A CTA below
+      // kMlpUnits owns MLP unit u = blockIdx.x: gate/up tiles 8u .. 8u+7, one
+      // per warp (item cur + w has seq w), giving h[64u .. 64u+63].
       const uint4 gamma_post = gamma_prefetch(p.norms + (size_t)(2 * layer + 1) * kHidden, ct);
       poll_units<1>(p.x_ll, kHidden / 8, ct, 256, tagof(2 * layer + 1), misc, p.err,
                     kSiteXMid * 100 + layer, [&](int u, const __half* v) {
                       reinterpret_cast<uint4*>(xloc)[u] = *reinterpret_cast<const uint4*>(v);
                     });
       cbar();
+      uint4* hf = reinterpret_cast<uint4*>(uni + kOffHFrag);
       {
         const int e = phase_end(ph + kPhGU);
         rmsnorm_out(xloc, gamma_post, red2, xf, nullptr, ct);
         lstamp(layer, kTsGUReady);
-        wsel = layer == p.n_layers / 2 ? 0 : -1;
-        if (wtrace && ct == 0 && wsel >= 0) wtrace[0] = 0;
-        const uint16_t tg = (uint16_t)tagof(layer);
-        // One item per gate/up tile and item j of the phase has seq j, so warp
-        // w's tiles are items cur + w, cur + w + 8, ... (walking the whole list
-        // and skipping the other warps' items cost ~0.1 us per item).
-        for (int i = cur + warp; i < e; i += kConsumerWarps) {
+        const int i = cur + warp;
+        if (i < e) {
           const ItemFields it = unpack_item(items[i]);
           const int slot = i % kNS;
           float acc_g = 0.f, acc_g8 = 0.f;
@@ -982,57 +950,127 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
             q4_chunk(ring + slot * kSlotBytes, it.k0, 0, it.nk, 1, xf, lane, acc_g, acc_g8);
           __syncwarp();
           if (lane == 0) release(i, kConsumerWarps);
-          if (t == 0) {
-            // gate and up with the zero bias of InferenceEngine.swift:82-85, then
-            // half(silu(gate) * up) (activations.metal:14-26)
-            const __half gate = f2h(acc_g + 0.0f), up = f2h(acc_g8 + 0.0f);
-            st_tag16(p.h_ll + 8 * it.tile + g, tg, f2h(silu_ref(h2f(gate)) * h2f(up)));
-          }
+          // gate and up with the zero bias of InferenceEngine.swift:82-85, then
+          // half(silu(gate) * up) (activations.metal:14-26); every lane of
+          // group g holds row g's sums (the MMA's 8 columns are equal).
+          const __half gate = f2h(acc_g + 0.0f), up = f2h(acc_g8 + 0.0f);
+          const __half h = f2h(silu_ref(h2f(gate)) * h2f(up));
+          // h[8w .. 8w+7] of the unit is the down strip's x fragment for
+          // block w / 4, lane quad w % 4 (make_xfrag order): hf[w].
+          __half v[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            v[q] = __ushort_as_half((unsigned short)__shfl_sync(0xffffffffu, (unsigned)hbits(h), 4 * q));
+          if (lane == 0) hf[warp] = make_xfrag(v);
         }
         cur = e;
       }
       cbar();
       lstamp(layer, kTsGUDone);
-      // ---- P5: h -> down -> bias -> residual
+      // ---- P5: the unit's down strip: row tiles x block pair u, K-split
+      // partial sums of all 1536 outputs over this unit's 64 k.  Warps 2j and
+      // 2j+1 take item j (24 row tiles), 12 row tiles each: one slot wait and
+      // one release a warp.  The partial sums are stored after the release (a
+      // release's block-scope fence would otherwise wait for them).
       {
         const int e = phase_end(ph + kPhDown);
-        if (e > cur) {
-          const __half* db = p.down_bias + (size_t)layer * kHidden;
-          const int dtile = (int)unpack_item(items[cur]).tile;
-          const float dbias = ct < 16 ? h2f(db[16 * dtile + ct]) : 0.f;
-          // Each warp polls only the h units of its own K range (block pairs
-          // [w*140/8, (w+1)*140/8), the range ksplit_down gives it) and starts
-          // its GEMV once they are in: no CTA-wide wait for the last of the
-          // 1120 units.  (The cbar after gate/up ended every read of xf.)
-          {
-            const int blo = warp * kBp8960 / kConsumerWarps;
-            const int bhi = (warp + 1) * kBp8960 / kConsumerWarps;
-            // (test hook: with stall_site == kSiteH the poll expects a tag
-            // nothing writes, so the wait runs out)
-            const uint32_t htag = p.stall_site == kSiteH ? tagof(255) : tagof(layer);
-            poll_units<5>(p.h_ll + 64 * blo, 8 * (bhi - blo), lane, 32, htag, misc, p.err,
-                          kSiteH * 100 + layer, [&](int u, const __half* v) {
-                            __half tmp[8];
+        if (e - cur == kDownItems) {
+          const int i = cur + (warp >> 1);
+          const int slot = i % kNS;
+          const int b0 = kDownRowTilesPerWarp * (warp & 1);
+          float acc[kDownRowTilesPerWarp][2];
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) tmp[q] = v[q];
-                            xf[8 * blo + u] = make_xfrag(tmp);
-                          });
-            __syncwarp();
+          for (int j = 0; j < kDownRowTilesPerWarp; ++j) acc[j][0] = acc[j][1] = 0.f;
+          if (timed_wait(i, kSiteFull * 100 + (int)(items[i] & 0xFF) % 100)) {
+            const uint8_t* sb = ring + slot * kSlotBytes + b0 * kBpBytes;
+#pragma unroll
+            for (int j = 0; j < kDownRowTilesPerWarp; j += 3) {
+              q4_bp(sb + (j + 0) * kBpBytes, 0, 0, hf, lane, acc[j][0], acc[j][1]);
+              q4_bp(sb + (j + 1) * kBpBytes, 0, 0, hf, lane, acc[j + 1][0], acc[j + 1][1]);
+              q4_bp(sb + (j + 2) * kBpBytes, 0, 0, hf, lane, acc[j + 2][0], acc[j + 2][1]);
+            }
           }
-          lstamp(layer, kTsDownReady);
-          wsel = layer == p.n_layers / 2 ? 1 : -1;
-          if (wtrace && ct == 0 && wsel >= 0) wtrace[1] = 0;
-          const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
-          ksplit_down(e, [&](int tile, int r, float sum) {
-            const int row = 16 * tile + r;
-            const __half d = f2h(sum + (tile == dtile ? dbias : h2f(db[row])));
+          __syncwarp();
+          if (lane == 0) release(i, kConsumerWarps / kWarpsPerDownItem);
+          // The warp's 12 row tiles are 192 consecutive rows of the unit's
+          // partial vector, and every lane of group g holds rows g and g + 8 of
+          // each tile: lane (g, t) stores row 8t + g of a pair of tiles, one
+          // 256-byte store per pair.
+          const uint16_t tg = (uint16_t)tagof(layer);
+          const ItemFields it = unpack_item(items[i]);
+          unsigned long long* part = p.mlp_part + (size_t)it.tile * kHidden + 16 * (it.k0 + b0) + 8 * t + g;
+#pragma unroll
+          for (int m = 0; m < kDownRowTilesPerWarp / 2; ++m)
+            st_tag32(part + 32 * m, tg, t == 0 ? acc[2 * m][0] : t == 1 ? acc[2 * m][1]
+                                      : t == 2 ? acc[2 * m + 1][0] : acc[2 * m + 1][1]);
+        }
+        cur = e;
+      }
+      // All warps done before any polls: a warp spinning on global loads
+      // while others still stream their down items would queue its loads
+      // ahead of their shared-memory traffic.
+      cbar();
+      lstamp(layer, kTsPartialsOut);
+      // ---- P6: every CTA finishes rows [R0, R1) of the layer's output: the
+      // 140 units' partial sums in unit order, + bias, rounded (matmul.metal:71),
+      // + the residual x' (attention.metal:58-65).
+      {
+        const int R0 = (int)(blockIdx.x * kHidden / gridDim.x);
+        const int R1 = (int)((blockIdx.x + 1) * kHidden / gridDim.x);
+        const int n_rows = R1 - R0;
+        const int n_words = n_rows * kMlpUnits;
+        float* stage = reinterpret_cast<float*>(uni + kOffMlpStage);
+        // word w of the CTA's share: unit w / n_rows, row R0 + w % n_rows
+        auto word_src = [&](int w) {
+          return p.mlp_part + (size_t)(w / n_rows) * kHidden + R0 + w % n_rows;
+        };
+        auto word_dst = [&](int w) { return (w % n_rows) * kMlpUnits + w / n_rows; };
+        // (test hook: with stall_site == kSiteDownPart the poll expects a tag
+        // nothing writes, so the wait runs out)
+        const uint32_t ptag = p.stall_site == kSiteDownPart ? tagof(255) : tagof(layer);
+        uint32_t pending = 0;
+        unsigned long long v[kReducePerThread];
+#pragma unroll
+        for (int j = 0; j < kReducePerThread; ++j)
+          if (ct + j * kFusedThreads < n_words) pending |= 1u << j;
+        uint64_t t0 = 0;
+        for (uint32_t it = 0; pending; ++it) {
+#pragma unroll
+          for (int j = 0; j < kReducePerThread; ++j)
+            if (pending & (1u << j)) v[j] = ld_tag64(word_src(ct + j * kFusedThreads));
+#pragma unroll
+          for (int j = 0; j < kReducePerThread; ++j)
+            if ((pending & (1u << j)) && (uint32_t)(v[j] >> 32) == ptag) {
+              stage[word_dst(ct + j * kFusedThreads)] = __uint_as_float((uint32_t)v[j]);
+              pending &= ~(1u << j);
+            }
+          if (!pending) break;
+          if ((it & 63) == 0) {
+            if (aborted(misc, p.err)) break;
+            const uint64_t now = globaltimer();
+            if (it == 0) t0 = now;
+            else if (now - t0 > misc->wait_ns) {
+              fail(misc, p.err, kSiteDownPart * 100 + layer);
+              break;
+            }
+          }
+        }
+        cbar();
+        const __half* db = p.down_bias + (size_t)layer * kHidden;
+        const uint16_t tg = (uint16_t)tagof(2 * layer + 2);
+        for (int r = warp; r < n_rows; r += kConsumerWarps) {
+          float sum = 0.f;
+          for (int u = lane; u < kMlpUnits; u += 32) sum += stage[r * kMlpUnits + u];
+          sum = warp_sum(sum);
+          if (lane == 0) {
+            const int row = R0 + r;
+            const __half d = f2h(sum + h2f(db[row]));
             st_tag16(p.x_ll + row, tg, __hadd(xloc[row], d));
-          });
+          }
         }
       }
       cbar();
-      lstamp(layer, kTsDownDone);
-      wsel = -1;
+      lstamp(layer, kTsReduced);
     }
     // ---- final RMSNorm + LM head (each warp owns whole 16-row tiles)
     if (ct == 0) misc->cphase = lm_phase * 1000 + cur;
@@ -1100,12 +1138,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
     }
     if (trace) trace[1] = globaltimer();
   }
+  if (trace) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < p.trace_stride; i += blockDim.x) trace_out[i] = trace[i];
+  }
 }
 
 // ------------------------------------------------------------------ host --
 namespace {
 struct FusedScratchLayout {
-  size_t x_ll, q_ll, kv_ll, attn_part, attn_ll, h_ll, total;
+  size_t x_ll, q_ll, kv_ll, attn_part, attn_ll, mlp_part, total;
 };
 FusedScratchLayout fused_layout() {
   FusedScratchLayout l{};
@@ -1120,7 +1162,7 @@ FusedScratchLayout fused_layout() {
   l.kv_ll = take(512 * 4);
   l.attn_part = take((size_t)2 * kMaxAttnSplits * kAttnPartWords * 8);
   l.attn_ll = take(kHidden * 4);
-  l.h_ll = take(kInter * 4);
+  l.mlp_part = take((size_t)kHidden * kMlpUnits * 8);
   l.total = o;
   return l;
 }
@@ -1164,11 +1206,12 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
   p.kv_ll = reinterpret_cast<uint32_t*>(sc + lay.kv_ll);
   p.attn_part = reinterpret_cast<unsigned long long*>(sc + lay.attn_part);
   p.attn_ll = reinterpret_cast<uint32_t*>(sc + lay.attn_ll);
-  p.h_ll = reinterpret_cast<uint32_t*>(sc + lay.h_ll);
+  p.mlp_part = reinterpret_cast<unsigned long long*>(sc + lay.mlp_part);
   p.logits = s.logits;
   p.err = s.err;
   p.trace = s.trace;
   p.trace_stride = trace_stride_for(m.n_layers);
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
   p.n_layers = m.n_layers;
   p.max_ctx = s.max_ctx;
   p.kv_layer_stride = (int)s.kv_layer_stride();

@@ -597,7 +597,7 @@ int QwenEngine::set_wait_timeout(uint64_t ns) {
 
 int QwenEngine::test_stall(int site) {
   if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
-  if (site != 0 && site != kFusedStallH)
+  if (site != 0 && site != kFusedStallDownPart)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "no stall hook for wait site %d", site);
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");

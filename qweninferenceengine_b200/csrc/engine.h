@@ -241,8 +241,9 @@ struct FusedStepArgs {
   unsigned long long wait_ns;  // device wait limit
   int stall_site;              // test hook (0: none)
 };
-// Wait site of the fused step's h poll (down phase), for the stall test hook.
-constexpr int kFusedStallH = 9;
+// Wait site of the fused step's poll for the down partial sums, for the
+// stall test hook.
+constexpr int kFusedStallDownPart = 9;
 int fused_scratch_bytes(int batch, int max_ctx, int sm_count, size_t* bytes);
 int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st);
 int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st);

@@ -14,6 +14,12 @@
 // (RoPE pairs and gate/up pairs share a tile; see layout.cu).  The bytes are a
 // pure permutation of the reference's packed bytes and scales.
 //
+// The down projection (1536 x 8960) is stored block-pair-major instead: unit u
+// (block pair u, k = 64u .. 64u+63, u < 140) holds the 96 row tiles' block
+// pair u back to back (96 x 576 B), so the CTA that owns unit u -- the 64
+// SwiGLU outputs h[64u .. 64u+63], from gate/up tiles 8u .. 8u+7 -- streams
+// exactly the down weights those 64 h values multiply.
+//
 // fp16 LM-head tile layout: 16 vocabulary rows x 1536; per k16 step 512 B,
 // lane l = 4g + t holds W[g][16s+4t .. +3] then W[g+8][16s+4t .. +3].
 #pragma once
@@ -33,12 +39,20 @@ constexpr size_t kLayerOOff = kLayerQKVOff + (size_t)kQKVTiles * kTile1536Bytes;
 constexpr size_t kLayerGUOff = kLayerOOff + (size_t)kOTiles * kTile1536Bytes;
 constexpr size_t kLayerDownOff = kLayerGUOff + (size_t)kGUTiles * kTile1536Bytes;
 constexpr size_t kLayerBlobBytes = kLayerDownOff + (size_t)kDownTiles * kTile8960Bytes;  // 26,320,896
+// MLP units: unit u = gate/up tiles 8u .. 8u+7 (h[64u .. 64u+63]) and block
+// pair u of every down row tile, streamed as kDownItems items of
+// kDownItemTiles row tiles (one ring slot each).
+constexpr int kMlpUnits = kBp8960;              // 140
+constexpr int kGUTilesPerUnit = kGUTiles / kMlpUnits;  // 8
+constexpr int kDownItemTiles = 24;
+constexpr int kDownItems = kDownTiles / kDownItemTiles;  // 4
+static_assert(kGUTilesPerUnit * kMlpUnits == kGUTiles, "gate/up tiles per MLP unit");
+static_assert(kDownItems * kDownItemTiles == kDownTiles, "down items per MLP unit");
 
 constexpr int kLMTiles = 151936 / 16;           // 9496
 constexpr int kLMStepBytes = 512;               // one k16 step of a 16-row fp16 tile
 constexpr int kLMTileBytes = 96 * kLMStepBytes; // 49152
 constexpr int kLMChunkSteps = 24;               // 12288 B per streamed chunk
-constexpr int kDownChunkBp = 24;                // down tiles stream in chunks of 24 block pairs
 
 constexpr int kSlotBytes = kTile1536Bytes;      // ring slot
 constexpr int kConsumerWarps = 8;
@@ -51,27 +65,29 @@ enum FusedPhase : uint16_t { kPhQKV = 0, kPhAttn = 1, kPhO = 2, kPhGU = 3, kPhDo
 constexpr int kPhasesPerLayer = 5;
 // Trace stamps per CTA: [0] first weight items issued, [1] copies drained at
 // exit, [2] consumer start, then per layer kTraceStampsPerLayer stamps (see
-// TraceStamp), then LM start, consumer end.  kTsDownReady is warp 0's h range
-// in (each down warp polls its own range).
+// TraceStamp), then LM start, consumer end.  kTsPartialsOut: the CTA's down
+// partial sums written; kTsReduced: its rows of the layer output written.
 enum TraceStamp : int {
   kTsLayerStart = 0, kTsXReady, kTsQKVDone, kTsAttnDone, kTsOReady, kTsODone, kTsGUReady,
-  kTsGUDone, kTsDownReady, kTsDownDone, kTraceStampsPerLayer
+  kTsGUDone, kTsPartialsOut, kTsReduced, kTraceStampsPerLayer
 };
 // Per CTA: 3 head stamps, 10 per layer, 2 for the LM head, then 7 inside the
 // attention unit of the middle layer (start, q/k/v in, warp 0's positions
 // done, the unit's warps merged, partials written, partials of all splits in,
-// output slice written) on the CTAs that run one, then warp 0's nanoseconds
-// waiting for weight slots in the middle layer's gate/up and down phases.
-constexpr int kAttnTraceStamps = 9;
+// output slice written) on the CTAs that run one.  (Stamps go to shared memory
+// during the step; timing the waits of one warp measurably slowed that warp,
+// so nothing finer is recorded.)
+constexpr int kAttnTraceStamps = 7;
 inline int trace_stride_for(int n_layers) {
   return 3 + n_layers * kTraceStampsPerLayer + 2 + kAttnTraceStamps;
 }
 
 // One streamed unit of weights for one CTA, packed in 64 bits:
 //   bits  0..7   phase  (layer * 5 + FusedPhase, or n_layers * 5 for the LM head)
-//   bits  8..21  tile   (tile index inside its matrix)
-//   bits 22..29  k0     (first block pair (Q4) or k16 step (LM) of the chunk)
-//   bits 30..37  nk     (block pairs / k16 steps in the chunk)
+//   bits  8..21  tile   (tile index inside its matrix; for a down item: the MLP unit)
+//   bits 22..29  k0     (first block pair (Q4) or k16 step (LM) of the chunk;
+//                        for a down item: its first row tile)
+//   bits 30..37  nk     (block pairs / k16 steps / down row tiles in the chunk)
 //   bit  38      last   (the tile's last chunk)
 //   bits 39..46  seq    (index of the tile among this CTA's tiles of the phase)
 // The source offset and byte count follow from these fields (fused.h layouts).
@@ -106,12 +122,15 @@ __host__ __device__ inline void item_source(const ItemFields& f, int lm_phase, s
   }
   const int layer = f.phase / kPhasesPerLayer, k = f.phase % kPhasesPerLayer;
   size_t base = (size_t)layer * kLayerBlobBytes;
-  size_t tile_bytes = kTile1536Bytes;
   if (k == kPhQKV) base += kLayerQKVOff;
   else if (k == kPhO) base += kLayerOOff;
   else if (k == kPhGU) base += kLayerGUOff;
-  else { base += kLayerDownOff; tile_bytes = kTile8960Bytes; }
-  *off = base + (size_t)f.tile * tile_bytes + (size_t)f.k0 * kBpBytes;
+  else {
+    *off = base + kLayerDownOff + ((size_t)f.tile * kDownTiles + f.k0) * kBpBytes;
+    *bytes = (uint32_t)f.nk * kBpBytes;
+    return;
+  }
+  *off = base + (size_t)f.tile * kTile1536Bytes + (size_t)f.k0 * kBpBytes;
   *bytes = (uint32_t)f.nk * kBpBytes;
 }
 
@@ -135,7 +154,7 @@ struct FusedParams {
   uint32_t* kv_ll;            // [512]   new k | v of the step
   unsigned long long* attn_part;  // [2][kMaxAttnSplits][kAttnPartWords] tagged fp32 words
   uint32_t* attn_ll;          // [1536]
-  uint32_t* h_ll;             // [8960]
+  unsigned long long* mlp_part;  // [kMlpUnits][1536] tagged fp32 down partial sums
   __half* logits;             // [151936]
   int* err;
   unsigned long long* trace;  // optional [grid][trace_stride] %globaltimer stamps

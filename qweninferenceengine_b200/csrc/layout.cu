@@ -46,7 +46,10 @@ __device__ __forceinline__ void locate(const Q4Sources& s, int row, int& m, int&
   }
 }
 
-__global__ void k_repack_q4(Q4Sources src, int k, int n_tiles, int map, uint8_t* __restrict__ dst) {
+// bp_major: block pair p of tile `tile` goes to (p * n_tiles + tile) instead of
+// (tile * P + p) -- the MLP-unit order of the down projection (fused.h).
+__global__ void k_repack_q4(Q4Sources src, int k, int n_tiles, int map, int bp_major,
+                            uint8_t* __restrict__ dst) {
   const int P = k / 64;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)n_tiles * P * 32) return;
@@ -65,7 +68,7 @@ __global__ void k_repack_q4(Q4Sources src, int k, int n_tiles, int map, uint8_t*
   w.y = *reinterpret_cast<const uint32_t*>(rowg8 + 16 * (2 * p));
   w.z = *reinterpret_cast<const uint32_t*>(rowg + 16 * (2 * p + 1));
   w.w = *reinterpret_cast<const uint32_t*>(rowg8 + 16 * (2 * p + 1));
-  uint8_t* out = dst + ((size_t)tile * P + p) * kBpBytes;
+  uint8_t* out = dst + (bp_major ? (size_t)p * n_tiles + tile : (size_t)tile * P + p) * kBpBytes;
   reinterpret_cast<uint4*>(out)[lane] = w;
   if (t == 0) {
     const int nb = k / 32;
@@ -89,28 +92,33 @@ __global__ void k_repack_lm(const __half* __restrict__ w, uint8_t* __restrict__ 
   reinterpret_cast<uint4*>(dst + ((size_t)tile * 96 + s) * kLMStepBytes)[lane] = make_uint4(a.x, a.y, b.x, b.y);
 }
 
-static int repack(const Q4Sources& s, int k, int n_tiles, int map, uint8_t* dst, cudaStream_t st) {
+static int repack(const Q4Sources& s, int k, int n_tiles, int map, uint8_t* dst, cudaStream_t st,
+                  int bp_major = 0) {
   const long long n = (long long)n_tiles * (k / 64) * 32;
-  k_repack_q4<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s, k, n_tiles, map, dst);
+  k_repack_q4<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s, k, n_tiles, map, bp_major, dst);
   return launch_status("repack_q4");
 }
 
 // ------------------------------------------------------------ schedule ----
-// Greedy assignment of every streamed tile of a step to CTAs, balancing the
-// bytes each CTA streams over the whole step.  Phase order per layer:
-// QKV, (attention: no weights), O, gate/up, down; then the LM head.
-static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items,
+// Assignment of every streamed tile of a step to CTAs.  Phase order per
+// layer: QKV, (attention: no weights), O, gate/up, down; then the LM head.
+//   QKV: the first 128 CTAs, one tile each (the attention units use the last
+//        CTAs);
+//   O:   one tile per CTA, on the CTAs with the least bytes so far;
+//   MLP: unit u (gate/up tiles 8u .. 8u+7, then its down strip as kDownItems
+//        items) on CTA u, so every CTA below kMlpUnits owns one unit (the
+//        grid must have at least kMlpUnits CTAs);
+//   LM head: tile t on CTA t % grid, in chunks of kLMChunkSteps.
+// Returns false when the grid is too small for the MLP units.
+static bool build_schedule(int n_layers, int grid, std::vector<FusedItem>& items,
                            std::vector<uint32_t>& begin) {
+  items.clear();
+  begin.assign(grid + 1, 0);
+  if (grid < kMlpUnits) return false;
   std::vector<std::vector<FusedItem>> per(grid);
   std::vector<double> load(grid, 0.0);
-  auto least = [&](int lo, int hi) {
-    int best = lo;
-    for (int c = lo + 1; c < hi; ++c)
-      if (load[c] < load[best]) best = c;
-    return best;
-  };
   std::vector<std::vector<int>> tiles_in_phase(grid, std::vector<int>(n_layers * kPhasesPerLayer + 1, 0));
-  auto add_tile = [&](int cta, uint16_t phase, int tile, size_t, int n_k, int chunk_k, int unit_bytes) {
+  auto add_tile = [&](int cta, uint16_t phase, int tile, int n_k, int chunk_k, int unit_bytes) {
     const int seq = tiles_in_phase[cta][phase]++;
     for (int k0 = 0; k0 < n_k; k0 += chunk_k) {
       const int nk = std::min(chunk_k, n_k - k0);
@@ -119,47 +127,33 @@ static void build_schedule(int n_layers, int grid, std::vector<FusedItem>& items
     }
   };
   for (int l = 0; l < n_layers; ++l) {
-    const size_t lb = (size_t)l * kLayerBlobBytes;
     const uint16_t ph = (uint16_t)(l * kPhasesPerLayer);
-    // QKV: the first 128 CTAs, one tile each (attention units use the last CTAs).
-    for (int t = 0; t < kQKVTiles; ++t)
-      add_tile(t % grid, ph + kPhQKV, t, lb + kLayerQKVOff + (size_t)t * kTile1536Bytes, kBp1536,
-               kBp1536, kBpBytes);
-    // The least-loaded CTA that holds fewer than `cap` tiles of the phase: a
-    // phase lasts as long as its busiest CTA, so O and down tiles are spread
-    // one per CTA (without the cap the byte balance over the whole step gave
-    // ~52 CTAs two O tiles each, run back to back) and gate/up tiles one per
-    // consumer warp.
-    auto least_capped = [&](uint16_t phase, int cap) {
+    for (int t = 0; t < kQKVTiles; ++t) add_tile(t % grid, ph + kPhQKV, t, kBp1536, kBp1536, kBpBytes);
+    for (int t = 0; t < kOTiles; ++t) {
       int best = -1;
       for (int c = 0; c < grid; ++c)
-        if (tiles_in_phase[c][phase] < cap && (best < 0 || load[c] < load[best])) best = c;
-      return best;
-    };
-    const int o_cap = (kOTiles + grid - 1) / grid;
-    for (int t = 0; t < kOTiles; ++t)
-      add_tile(least_capped(ph + kPhO, o_cap), ph + kPhO, t,
-               lb + kLayerOOff + (size_t)t * kTile1536Bytes, kBp1536, kBp1536, kBpBytes);
-    const int gu_cap = (kGUTiles + grid - 1) / grid;
-    for (int t = 0; t < kGUTiles; ++t)
-      add_tile(least_capped(ph + kPhGU, gu_cap), ph + kPhGU, t,
-               lb + kLayerGUOff + (size_t)t * kTile1536Bytes, kBp1536, kBp1536, kBpBytes);
-    const int down_cap = (kDownTiles + grid - 1) / grid;
-    for (int t = 0; t < kDownTiles; ++t)
-      add_tile(least_capped(ph + kPhDown, down_cap), ph + kPhDown, t,
-               lb + kLayerDownOff + (size_t)t * kTile8960Bytes, kBp8960, kDownChunkBp, kBpBytes);
+        if (tiles_in_phase[c][ph + kPhO] == 0 && (best < 0 || load[c] < load[best])) best = c;
+      add_tile(best, ph + kPhO, t, kBp1536, kBp1536, kBpBytes);
+    }
+    for (int u = 0; u < kMlpUnits; ++u) {
+      for (int j = 0; j < kGUTilesPerUnit; ++j)
+        add_tile(u, ph + kPhGU, kGUTilesPerUnit * u + j, kBp1536, kBp1536, kBpBytes);
+      // the unit's down strip: kDownTiles row tiles of one block pair each
+      add_tile(u, ph + kPhDown, u, kDownTiles, kDownItemTiles, kBpBytes);
+    }
   }
   const uint16_t lm_phase = (uint16_t)(n_layers * kPhasesPerLayer);
-  for (int t = 0; t < kLMTiles; ++t)
-    add_tile(least(0, grid), lm_phase, t, (size_t)t * kLMTileBytes, 96, kLMChunkSteps, kLMStepBytes);
-  items.clear();
-  begin.assign(grid + 1, 0);
+  // The LM head is its own phase after the last layer (a ring slot holds one
+  // chunk, so it cannot be fetched much earlier): balance its tiles alone,
+  // not the bytes of the whole step.
+  for (int t = 0; t < kLMTiles; ++t) add_tile(t % grid, lm_phase, t, 96, kLMChunkSteps, kLMStepBytes);
   for (int c = 0; c < grid; ++c) {
     if (per[c].size() > (size_t)kMaxItemsPerCta) per[c].clear();  // reported by the caller
     begin[c] = (uint32_t)items.size();
     items.insert(items.end(), per[c].begin(), per[c].end());
   }
   begin[grid] = (uint32_t)items.size();
+  return true;
 }
 
 // RoPE cos/sin per position: theta = pos * 1e6^(-2i/128) in fp32 with libm,
@@ -211,7 +205,7 @@ int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
                  {kInter, kInter, 0}};
     QWEN_TRY(repack(gu, kHidden, kGUTiles, kMapGateUp, lb + kLayerGUOff, st));
     Q4Sources dn{{L.down.packed, nullptr, nullptr}, {L.down.scales, nullptr, nullptr}, {kHidden, 0, 0}};
-    QWEN_TRY(repack(dn, kInter, kDownTiles, kMapPlain, lb + kLayerDownOff, st));
+    QWEN_TRY(repack(dn, kInter, kDownTiles, kMapPlain, lb + kLayerDownOff, st, 1));
     QWEN_CUDA(cudaMemcpyAsync(f.norms + (size_t)(2 * l) * kHidden, L.input_norm, kHidden * 2,
                               cudaMemcpyDeviceToDevice, st), "memcpy");
     QWEN_CUDA(cudaMemcpyAsync(f.norms + (size_t)(2 * l + 1) * kHidden, L.post_attn_norm, kHidden * 2,
@@ -237,7 +231,9 @@ int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
   QWEN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "attr");
   std::vector<FusedItem> items;
   std::vector<uint32_t> begin;
-  build_schedule(m.n_layers, sms, items, begin);
+  if (!build_schedule(m.n_layers, sms, items, begin))
+    return set_error(QWEN_ERR_STATE, "the fused step needs at least %d SMs (device has %d)", kMlpUnits,
+                     sms);
   for (int c = 0; c < sms; ++c)
     if (begin[c + 1] == begin[c])
       return set_error(QWEN_ERR_STATE, "fused schedule: CTA %d has no work or more than %d items", c,
@@ -268,7 +264,7 @@ extern "C" long long qwen_fused_schedule(int n_layers, int grid, unsigned long l
   if (n_layers < 1 || n_layers > 64 || grid < 1 || grid > 1024 || !items_out || !begin_out) return -1;
   std::vector<qwen::FusedItem> items;
   std::vector<uint32_t> begin;
-  qwen::build_schedule(n_layers, grid, items, begin);
+  if (!qwen::build_schedule(n_layers, grid, items, begin)) return -1;
   if ((long long)items.size() > items_cap) return -1;
   std::copy(items.begin(), items.end(), items_out);
   std::copy(begin.begin(), begin.end(), begin_out);

@@ -22,7 +22,7 @@
         with an event after every kernel (qwen_engine_profile_step); prints the
         per-kernel device times and is the workload for ncu launch lists of it.
 
-    python -m qweninferenceengine_b200.profiling trace [--layers 28] [--ctx 512]
+    python -m qweninferenceengine_b200.profiling trace [--layers 28] [--ctx 512] [--save f.npy]
         Per-phase critical-path summary of one fused decode step from the
         kernel's %globaltimer stamps (qwen_engine_trace): for each traced layer,
         min / median / max over CTAs of every stamp relative to the layer start.
@@ -36,10 +36,10 @@ import numpy as np
 from .engine import QwenConfig, QwenEngine
 
 STAMPS = ["start", "x_ready", "qkv_done", "attn_done", "o_ready", "o_done", "gu_ready",
-          "gu_done", "h_ready", "down_done"]
+          "gu_done", "parts_out", "reduced"]
 ATTN_STAMPS = ["unit_start", "qkv_in", "warp0_done", "warps_merged", "partials_out",
                "splits_in", "output_out"]
-EXTRA_WORDS = 2  # warp 0's slot-wait ns in the middle layer's gate/up and down phases
+EXTRA_WORDS = 0
 
 
 def run_case(layers: int, steps: int) -> None:
@@ -97,7 +97,7 @@ def run_tcstep(batch: int, ctx: int, reps: int, layers: int = 28) -> list:
     return prof
 
 
-def run_trace(layers: int, ctx: int, show_layers) -> dict:
+def run_trace(layers: int, ctx: int, show_layers, save: str | None = None) -> dict:
     cfg = QwenConfig(num_layers=layers, max_context_window=max(1024, ctx + 64), temperature=0.7,
                      top_p=0.8, stop_on_eos=False)
     eng = QwenEngine(config=cfg, random_seed=5)
@@ -110,6 +110,8 @@ def run_trace(layers: int, ctx: int, show_layers) -> dict:
     tr = eng.get_trace().astype(np.int64)
     eng.trace(False)
     eng.close()
+    if save:
+        np.save(save, tr)
     k = len(STAMPS)
     grid = tr.size // (3 + k * layers + 2 + len(ATTN_STAMPS) + EXTRA_WORDS)
     tr = tr.reshape(grid, -1)
@@ -122,11 +124,6 @@ def run_trace(layers: int, ctx: int, show_layers) -> dict:
     periods = np.diff(np.nanmedian(ph[:, :, 0], axis=0))
     out["layer_period_us"] = float(np.median(periods)) if periods.size else None
     mid = layers // 2
-    waits = tr[:, 3 + k * layers + 2 + len(ATTN_STAMPS):].astype(np.float64) / 1000.0
-    out["slot_wait_us"] = {"gate_up": (float(waits[:, 0].min()), float(np.median(waits[:, 0])),
-                                       float(waits[:, 0].max())),
-                           "down": (float(waits[:, 1].min()), float(np.median(waits[:, 1])),
-                                    float(waits[:, 1].max()))}
     att = rel[:, 3 + k * layers + 2:3 + k * layers + 2 + len(ATTN_STAMPS)]
     have = ~np.isnan(att[:, 0])
     if have.any():
@@ -173,6 +170,7 @@ def main() -> None:
     t = sub.add_parser("trace")
     t.add_argument("--layers", type=int, default=28)
     t.add_argument("--ctx", type=int, default=512)
+    t.add_argument("--save", default=None, help="also write the raw stamps (.npy)")
     a = ap.parse_args()
     if a.cmd == "case":
         run_case(a.layers, a.steps)
@@ -195,12 +193,10 @@ def main() -> None:
         run_attention(a.batch, a.ctx, a.reps)
         print("ok")
         return
-    r = run_trace(a.layers, a.ctx, [1, a.layers // 2, a.layers - 1])
+    r = run_trace(a.layers, a.ctx, [1, a.layers // 2, a.layers - 1], a.save)
     print(f"step {r['ms_step']:.3f} ms, model kernels {r['ms_model']:.3f} ms, grid {r['grid']}, "
           f"median layer period {r['layer_period_us']:.2f} us, LM head from {r['lm_start_us']:.1f} "
           f"to {r['end_us']:.1f} us")
-    print("warp 0 waiting for weight slots, middle layer (us, min / med / max over CTAs): " +
-          ", ".join(f"{k} {lo:.2f} / {med:.2f} / {hi:.2f}" for k, (lo, med, hi) in r["slot_wait_us"].items()))
     if "attention_unit" in r:
         print(f"attention units of layer {a.layers // 2} (us from the layer's median start; min / med / max)")
         for name, (lo, med, hi) in r["attention_unit"].items():

@@ -10,10 +10,10 @@ a warp that runs ahead from taking the previous ring lap's phase for its own.
 
 Release shares per phase, as the kernel gives them:
   * k-split tiles (QKV, O): all 8 warps read every chunk, one share each;
-  * down tiles (6 chunks of 24 block pairs): warp w reads block pairs
-    [w*140/8, (w+1)*140/8); the first warp touching a chunk adds the shares of
-    the warps that do not touch it;
-  * gate/up tiles: one warp per tile (item j of the phase -> warp j % 8), 8 shares;
+  * the MLP unit's gate/up tiles: one warp per tile (item j of the phase ->
+    warp j), 8 shares;
+  * the unit's down strip (4 items of 24 row tiles): warps 2j and 2j+1 read
+    item j, 12 row tiles and 4 shares each;
   * LM head: tile t's chunks belong to warp t % 8, 8 shares each.
 All warps meet at a barrier between phases.
 
@@ -30,24 +30,17 @@ import pytest
 
 KNS = 14
 WARPS = 8
-BP8960, DOWN_CHUNK = 140, 24
+DOWN_ITEMS = 4
 
 
 def layer_items(n_gu):
-    """(phase, tile, chunk) items of one layer for one CTA, in stream order."""
+    """(phase, tile, chunk) items of one layer for one CTA, in stream order
+    (n_gu = 8 for a CTA that owns an MLP unit, 0 for one that does not)."""
     items = [("qkv", 0, 0), ("o", 0, 0)]
     items += [("gu", t, 0) for t in range(n_gu)]
-    n_chunks = (BP8960 + DOWN_CHUNK - 1) // DOWN_CHUNK
-    items += [("down", 0, c) for c in range(n_chunks)]
+    if n_gu:
+        items += [("down", 0, c) for c in range(DOWN_ITEMS)]
     return items
-
-
-def down_shares(c):
-    """{warp: shares} for down chunk c (the kernel's arithmetic)."""
-    lo_of = lambda w: w * BP8960 // WARPS  # noqa: E731
-    i0, i1 = c * DOWN_CHUNK, min(BP8960, (c + 1) * DOWN_CHUNK)
-    touch = [w for w in range(WARPS) if max(lo_of(w), i0) < min(lo_of(w + 1), i1)]
-    return {w: (WARPS - len(touch) + 1 if w == touch[0] else 1) for w in touch}
 
 
 def plan(n_layers, n_gu, n_lm_tiles, lm_chunks=4):
@@ -62,10 +55,10 @@ def plan(n_layers, n_gu, n_lm_tiles, lm_chunks=4):
                     continue
                 if k in ("qkv", "o"):
                     sh = {w: 1 for w in range(WARPS)}
-                elif k == "gu":
-                    sh = {t % WARPS: WARPS}
+                elif k == "down":
+                    sh = {2 * c: WARPS // 2, 2 * c + 1: WARPS // 2}
                 else:
-                    sh = down_shares(c)
+                    sh = {t % WARPS: WARPS}
                 items.append((k, t, c))
                 shares.append(sh)
                 phase_of.append(ph)
@@ -154,13 +147,7 @@ def simulate(n_layers, n_gu, n_lm_tiles, seed):
     assert not inflight
 
 
-def test_down_shares_sum_to_eight():
-    n_chunks = (BP8960 + DOWN_CHUNK - 1) // DOWN_CHUNK
-    for c in range(n_chunks):
-        assert sum(down_shares(c).values()) == WARPS
-
-
-@pytest.mark.parametrize("n_gu", [7, 8])
+@pytest.mark.parametrize("n_gu", [0, 8])
 @pytest.mark.parametrize("seed", range(4))
 def test_ring_protocol(n_gu, seed):
     simulate(n_layers=2, n_gu=n_gu, n_lm_tiles=20, seed=seed)

@@ -5,14 +5,18 @@ build_fused_weights uploads: each CTA's weight items in stream order, packed as
 fused.h describes (phase, tile, k0, nk, last, seq).  k_decode_fused relies on
 these properties of it:
 
-  * every tile of every matrix is covered over its whole K exactly once;
+  * every tile of every matrix is covered over its whole K exactly once; the
+    down projection is streamed by MLP unit: unit u's item covers block pair
+    u of all 96 row tiles, in 4 chunks of 24 row tiles (k0 / nk count row
+    tiles there);
   * a CTA's items are in stream order (phases ascending, a tile's chunks
-    consecutive and ascending in k, `last` on its final chunk);
+    consecutive and ascending, `last` on its final chunk);
   * QKV tiles sit on the first 128 CTAs, one each (the attention units use
-    the last CTAs), and a CTA holds at most one O tile, one down tile and
-    ceil(1120 / grid) gate/up tiles per layer;
-  * `seq` numbers a CTA's tiles within a phase 0, 1, 2, ...; a gate/up warp
-    takes items cur + w, cur + w + 8, ... directly, so a gate/up tile is one item;
+    the last CTAs); a CTA holds at most one O tile per layer;
+  * CTA u < 140 owns MLP unit u: gate/up tiles 8u .. 8u+7 (seq 0..7, one item
+    each, warp w takes item cur + w) and the down strip of unit u; the other
+    CTAs own none;
+  * `seq` numbers a CTA's tiles within a phase 0, 1, 2, ...;
   * an LM-head tile's chunks are 24 k16 steps (4 per tile), and tile ownership
     (seq % 8) gives every warp whole tiles;
   * no CTA exceeds the shared-memory item table (768 items) or is empty.
@@ -25,8 +29,9 @@ import pytest
 from qweninferenceengine_b200 import _lib
 
 PH_QKV, PH_ATTN, PH_O, PH_GU, PH_DOWN = range(5)
-TILES = {PH_QKV: 128, PH_O: 96, PH_GU: 1120, PH_DOWN: 96}
-KSTEPS = {PH_QKV: 24, PH_O: 24, PH_GU: 24, PH_DOWN: 140}   # block pairs (LM: k16 steps)
+TILES = {PH_QKV: 128, PH_O: 96, PH_GU: 1120, PH_DOWN: 140}   # down: MLP units
+KSTEPS = {PH_QKV: 24, PH_O: 24, PH_GU: 24, PH_DOWN: 96}   # block pairs (down: row tiles; LM: k16 steps)
+MLP_UNITS, DOWN_CHUNK = 140, 24
 LM_TILES, LM_STEPS, LM_CHUNK = 151936 // 16, 96, 24
 MAX_ITEMS = 768
 
@@ -60,9 +65,11 @@ def test_hook_rejects_bad_arguments():
     assert f(0, 148, items.ctypes.data, 16, begin.ctypes.data) == -1
     assert f(28, 148, items.ctypes.data, 16, begin.ctypes.data) == -1     # capacity too small
     assert f(28, 148, None, 16, begin.ctypes.data) == -1
+    big = np.zeros(200_000, np.uint64)
+    assert f(28, 132, big.ctypes.data, big.size, begin.ctypes.data) == -1   # fewer CTAs than MLP units
 
 
-@pytest.mark.parametrize("n_layers,grid", [(28, 148), (4, 148), (1, 148), (28, 132), (2, 160)])
+@pytest.mark.parametrize("n_layers,grid", [(28, 148), (4, 148), (1, 148), (28, 140), (2, 160)])
 def test_schedule_invariants(n_layers, grid):
     items, begin = schedule(n_layers, grid)
     lm_phase = n_layers * 5
@@ -70,7 +77,6 @@ def test_schedule_invariants(n_layers, grid):
     assert np.all(np.diff(begin.astype(np.int64)) >= 1), "a CTA has no work (or overflowed its table)"
     assert int(np.max(np.diff(begin.astype(np.int64)))) <= MAX_ITEMS
     cover = {}
-    gu_cap = -(-TILES[PH_GU] // grid)
     for c in range(grid):
         its = [unpack(w) for w in items[begin[c]:begin[c + 1]]]
         phases = [it[0] for it in its]
@@ -89,6 +95,9 @@ def test_schedule_invariants(n_layers, grid):
                 assert last == (k0 + nk == KSTEPS[kind])
                 if kind == PH_GU:
                     assert k0 == 0 and nk == KSTEPS[PH_GU], "a gate/up tile must be one item"
+                    assert tile // 8 == c and seq == tile % 8, "unit c's tiles 8c .. 8c+7 on CTA c"
+                if kind == PH_DOWN:
+                    assert tile == c and nk == DOWN_CHUNK and k0 % DOWN_CHUNK == 0
             # a tile's chunks are consecutive and ascending
             if prev is not None and (prev[0], prev[1]) == (ph, tile):
                 assert k0 == prev[2] + prev[3]
@@ -110,7 +119,7 @@ def test_schedule_invariants(n_layers, grid):
             elif kind in (PH_O, PH_DOWN):
                 assert len(tiles) <= 1
             elif kind == PH_GU:
-                assert len(tiles) <= gu_cap
+                assert c < MLP_UNITS and len(tiles) == 8
     # every tile covered over its whole K exactly once
     for layer in range(n_layers):
         for kind, n in TILES.items():

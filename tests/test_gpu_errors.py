@@ -166,13 +166,12 @@ def test_device_wait_runs_out_and_the_engine_recovers(cuda, oracle, one_layer):
     eng.forward(7, 0)
     om.forward(7, 0)
     eng.set_wait_timeout(20_000_000)                          # 20 ms
-    eng.test_stall(9)                                         # the down phase's h wait
+    eng.test_stall(9)                                         # the wait for the down partials
     with pytest.raises(QwenError) as ei:
         eng.forward(8, 1)
     assert ei.value.code == QWEN_ERR_DEVICE_TIMEOUT
-    # the first wait to give up is the stalled h wait (site 9) or, on a CTA
-    # without a down tile that began waiting earlier, the final x wait behind
-    # it (site 10)
+    # the first wait to give up is the stalled wait for the down partial sums
+    # (site 9) or the final x wait behind it (site 10)
     assert re.search(r"timed out \(site (9|10),", str(ei.value)), str(ei.value)
     eng.test_stall(0)
     eng.set_wait_timeout(2_000_000_000)
