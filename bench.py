@@ -44,15 +44,15 @@ def headline_config(world: int) -> dict:
 
 
 # DRAM traffic of one launch of the fused step kernel (dram__bytes_read.sum +
-# dram__bytes_write.sum from one ncu capture of the 28-layer model at context 6:
-# 1.006 x the algorithmic bytes there).  Weights and LM head are read once per
+# dram__bytes_write.sum from one ncu capture of the 28-layer model at context 8:
+# 1.004 x the algorithmic bytes there).  Weights and LM head are read once per
 # launch, so the traffic at another context adds the KV bytes of the extra
 # positions.
-FUSED_TRAFFIC_CTX6 = 1_212_492_544
+FUSED_TRAFFIC_CTX8 = 1_208_959_744
 
 
 def fused_traffic(ctx: float) -> float:
-    return FUSED_TRAFFIC_CTX6 + KV_BYTES_PER_POS * (ctx - 6)
+    return FUSED_TRAFFIC_CTX8 + KV_BYTES_PER_POS * (ctx - 8)
 
 
 def bytes_per_token(ctx: float) -> float:
@@ -686,7 +686,7 @@ def run_ours(args):
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": fused_traffic(ctx_prof) if args.kernels == "fused" else None,
-                         "traffic_source": "ncu dram bytes of one 28-layer launch at context 6, "
+                         "traffic_source": "ncu dram bytes of one 28-layer launch at context 8, "
                                            "plus the KV bytes of the extra positions",
                          "algorithmic_bytes": algo,
                          "ms_model": ms_model, "ms_step_unfused_launch": ms_step_prof},
