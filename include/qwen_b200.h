@@ -60,7 +60,11 @@ int qwen_ops_status(void* stream);
 /* gemv_q4_0, matmul.metal:9-73 (buffers 0..5 = packed, scales, x, y,
  * constants[K,..], bias).  packed: [n_rows][k/2] bytes, low nibble = even k;
  * scales: [n_rows][k/32] fp16; y[r] = half(sum_k ((q-8)*s) x_k + bias[r]).
- * bias may be NULL.  k must be a multiple of 32. */
+ * bias may be NULL.  k must be a multiple of 32.  For k <= 3072 with 16-byte
+ * aligned packed and x, the kernel is launched as a programmatic dependent of
+ * the previous kernel in the stream: it fetches packed and scales before
+ * waiting for that kernel (x after), so they must not be produced by a kernel
+ * that lets dependents start early (griddepcontrol.launch_dependents). */
 int qwen_gemv_q4_0(const uint8_t* packed, const uint16_t* scales, const uint16_t* x,
                    uint16_t* y, uint32_t k, const uint16_t* bias, uint32_t n_rows,
                    void* stream);

@@ -74,6 +74,87 @@ __global__ void __launch_bounds__(128) k_gemv_q4_rowmajor(const uint8_t* __restr
   }
 }
 
+// Same product for K up to kGemvTileMaxK, with the CTA's whole 16-row tile in
+// flight at once: every thread issues 16-byte cp.async copies of the tile's
+// packed rows into shared memory (rows padded by 16 bytes, so the fragment
+// reads of rows g and g + 8 hit distinct banks), then 8 warps take blocks
+// b = w, w + 8, ... from shared memory.  One kernel of ~560 CTAs keeps ~50 KB
+// of weights in flight per SM, where the per-block 4-byte loads of
+// k_gemv_q4_rowmajor kept one block per warp.  Launched as a programmatic
+// dependent: the weights and scales (which no earlier kernel writes) are
+// fetched before griddepcontrol.wait, x (which the previous kernel may have
+// produced) and y after it, so back-to-back projections overlap a kernel's
+// weight fetch with the previous one's tail.
+constexpr int kGemvTileMaxK = 3072;
+constexpr int kGemvTileThreads = 256;
+__host__ __device__ inline int gemv_tile_row_stride(int k) { return k / 2 + 16; }
+__host__ __device__ inline int gemv_tile_smem(int k) {
+  const int nblk = k / 32;
+  return 16 * gemv_tile_row_stride(k) + ((16 * nblk * 2 + 15) / 16) * 16 + nblk * 4 * 16;
+}
+
+__global__ void __launch_bounds__(kGemvTileThreads) k_gemv_q4_tile(const uint8_t* __restrict__ packed,
+                                                                  const __half* __restrict__ scales,
+                                                                  const __half* __restrict__ x,
+                                                                  __half* __restrict__ y,
+                                                                  const __half* __restrict__ bias,
+                                                                  int n_rows, int k) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float red[kGemvTileThreads / 32][16];
+  const int rb = k / 2, rs = gemv_tile_row_stride(k), nblk = k / 32;
+  uint8_t* wt = smem;                                                 // [16][rs]
+  __half* sc = reinterpret_cast<__half*>(smem + 16 * rs);              // [16][nblk]
+  uint4* xf = reinterpret_cast<uint4*>(smem + 16 * rs + ((16 * nblk * 2 + 15) / 16) * 16);  // [nblk][4]
+  const int row0 = blockIdx.x * 16;
+  const int rows = min(16, n_rows - row0);
+  const int chunks = rb / 16;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  for (int c = threadIdx.x; c < rows * chunks; c += kGemvTileThreads) {
+    const int r = c / chunks, j = c - r * chunks;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(wt + r * rs + 16 * j)),
+                 "l"(packed + (size_t)(row0 + r) * rb + 16 * j)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // scales (contiguous for the tile's rows) and the x fragments, meanwhile
+  for (int i = threadIdx.x; i < rows * nblk; i += kGemvTileThreads) sc[i] = scales[(size_t)row0 * nblk + i];
+  pdl_wait();
+  for (int i = threadIdx.x; i < nblk * 4; i += kGemvTileThreads) {
+    const int b = i >> 2, t = i & 3;
+    __half v[8];
+    *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(x + 32 * b + 8 * t);
+    xf[i] = make_xfrag(v);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  // rows past n_rows hold stale shared memory: their sums are never stored
+  const uint8_t* wg_row = wt + g * rs + 4 * t;
+  const uint8_t* wg8_row = wt + (g + 8) * rs + 4 * t;
+  float acc_g = 0.f, acc_g8 = 0.f;
+  for (int b = warp; b < nblk; b += kGemvTileThreads / 32) {
+    const uint32_t wg = *reinterpret_cast<const uint32_t*>(wg_row + 16 * b);
+    const uint32_t wg8 = *reinterpret_cast<const uint32_t*>(wg8_row + 16 * b);
+    float d[4];
+    q4_block_mma(wg, wg8, xf[b * 4 + t], d);
+    acc_g += __half2float(sc[g * nblk + b]) * d[0];
+    acc_g8 += __half2float(sc[(g + 8) * nblk + b]) * d[2];
+  }
+  if (t == 0) {
+    red[warp][g] = acc_g;
+    red[warp][g + 8] = acc_g8;
+  }
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGemvTileThreads / 32; ++w) s += red[w][threadIdx.x];
+    const int r = row0 + threadIdx.x;
+    if (bias) s += __half2float(bias[r]);
+    y[r] = f2h(s);
+  }
+}
+
 // ----------------------------------------------------------- fp16 GEMV ----
 // One CTA (4 warps) per 16-row tile, warp w takes k16 steps s = w, w+4, ...
 // Lane (g,t) feeds W[g][16s+4t..+3] and W[g+8][..] as its A fragment and
@@ -273,6 +354,22 @@ static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s)
 
 int launch_gemv_q4_rowmajor(const uint8_t* packed, const __half* scales, const __half* x,
                             __half* y, const __half* bias, int n_rows, int k, void* stream) {
+  // The tile kernel wants 16-byte aligned rows (k a multiple of 32 makes each
+  // row 16-byte sized) and an aligned x for its 16-byte fragment loads.
+  if (k <= kGemvTileMaxK && (reinterpret_cast<uintptr_t>(packed) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n_rows + 15) / 16);
+    cfg.blockDim = dim3(kGemvTileThreads);
+    cfg.dynamicSmemBytes = gemv_tile_smem(k);
+    cfg.stream = S(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_gemv_q4_tile, packed, scales, x, y, bias, n_rows, k) == cudaSuccess ? 0 : -1;
+  }
   const int smem = (k / 32) * 64;
   if (smem > 48 * 1024) {
     static bool attr_set = false;
