@@ -46,9 +46,13 @@ constexpr int kNS = 14;                    // ring slots
 constexpr int kWarpsPerDownItem = kConsumerWarps / kDownItems;                 // 2
 constexpr int kDownRowTilesPerWarp = kDownItemTiles / kWarpsPerDownItem;       // 12
 static_assert(kWarpsPerDownItem * kDownItems == kConsumerWarps, "warps per down item");
-static_assert(kDownRowTilesPerWarp % 6 == 0, "down row tiles a warp: groups of three, stores by pairs");
+// A round of the down strip: 6 row tiles, MMA chains in groups of three, stores by tile pairs.
+constexpr int kDownRound = 6;
+static_assert(kDownRowTilesPerWarp % kDownRound == 0, "down row tiles a warp: whole rounds");
 // Rows of the layer output each CTA finishes, and the partial sums it reads.
-constexpr int kMaxReduceRows = (kHidden + kMlpUnits - 1) / kMlpUnits + 1;   // grid >= kMlpUnits
+// (CTA b finishes rows [b*1536/grid, (b+1)*1536/grid): at most ceil(1536/grid)
+// <= ceil(1536/140) = 11 of them, as the grid has at least kMlpUnits CTAs.)
+constexpr int kMaxReduceRows = (kHidden + kMlpUnits - 1) / kMlpUnits;
 constexpr int kReducePerThread = (kMaxReduceRows * kMlpUnits + kFusedThreads - 1) / kFusedThreads;
 constexpr int kUnionBytes = 20480;         // x fragments + corrections / attention buffers
 constexpr int kMaxXFrags = kInter / 8;     // 1120 fragment units (K = 8960)
@@ -218,8 +222,11 @@ __device__ __forceinline__ void poll_units(const uint32_t* src, int n_units, int
   }
 }
 
-__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volatile Misc* m,
-                                          int* err, int site) {
+// The slow paths of the waits are out of line: the fast path (the data has
+// landed) is what every item takes, and the step's per-layer code has to stay
+// small enough for the SM's instruction cache.
+__device__ __noinline__ bool slot_wait_slow(uint64_t* bar, uint32_t parity, volatile Misc* m,
+                                            int* err, int site) {
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -234,14 +241,18 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volati
     }
   }
 }
+__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volatile Misc* m,
+                                          int* err, int site) {
+  return mbar_try_wait(bar, parity) || slot_wait_slow(bar, parity, m, err, site);
+}
 
 // Waits for item i of this CTA's list to land in its ring slot.  A slot's
 // mbarrier only tells the current phase from the previous one, so a warp
 // that runs ahead (one that owns every 8th tile) first waits until item i has
 // been issued into the slot (slot_item) -- from then on the slot's current
 // phase is item i's and the parity wait is exact.
-__device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile const int* slot_item,
-                                          volatile Misc* m, int* err, int site) {
+__device__ __noinline__ bool item_issue_wait_slow(int i, volatile const int* slot_item,
+                                                  volatile Misc* m, int* err, int site) {
   uint64_t t0 = 0;
   for (uint32_t it = 0; slot_item[i % kNS] != i; ++it) {
     if ((it & 63) == 0) {
@@ -255,6 +266,11 @@ __device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile const 
     }
     __nanosleep(32);
   }
+  return true;
+}
+__device__ __forceinline__ bool item_wait(int i, uint64_t* full, volatile const int* slot_item,
+                                          volatile Misc* m, int* err, int site) {
+  if (slot_item[i % kNS] != i && !item_issue_wait_slow(i, slot_item, m, err, site)) return false;
   return slot_wait(&full[i % kNS], (i / kNS) & 1, m, err, site);
 }
 
@@ -336,17 +352,17 @@ __device__ __forceinline__ void q4_chunk(const uint8_t* slot, int k0, int b_begi
 // each warp 3 strided block pairs, which q4_chunk runs as a pair then a tail,
 // two dependent rounds; the down ranges (17-18 pairs a warp) gain from the
 // third chain too now that registers do not spill.
-__device__ __forceinline__ void q4_chunk3(const uint8_t* slot, int k0, int b_begin, int b_end,
-                                          int b_step, const uint4* xf, int lane, float& acc_g,
-                                          float& acc_g8) {
+// Warp w's share of a whole-tile item (24 block pairs, K-split over the 8
+// warps): block pairs w, w + 8, w + 16, three MMA chains in flight.  Straight
+// code: the step's per-layer code has to stay small enough for the SM's
+// instruction cache, and a loop here unrolls into several copies.
+static_assert(kBp1536 == 3 * kConsumerWarps, "a whole-tile item is three block pairs a warp");
+__device__ __forceinline__ void q4_kslice3(const uint8_t* slot, int warp, const uint4* xf, int lane,
+                                           float& acc_g, float& acc_g8) {
   float ga = 0.f, g8a = 0.f, gb = 0.f, g8b = 0.f, gc = 0.f, g8c = 0.f;
-  int b = b_begin;
-  for (; b + 2 * b_step < b_end; b += 3 * b_step) {
-    q4_bp(slot, k0, b, xf, lane, ga, g8a);
-    q4_bp(slot, k0, b + b_step, xf, lane, gb, g8b);
-    q4_bp(slot, k0, b + 2 * b_step, xf, lane, gc, g8c);
-  }
-  for (; b < b_end; b += b_step) q4_bp(slot, k0, b, xf, lane, ga, g8a);
+  q4_bp(slot, 0, warp, xf, lane, ga, g8a);
+  q4_bp(slot, 0, warp + kConsumerWarps, xf, lane, gb, g8b);
+  q4_bp(slot, 0, warp + 2 * kConsumerWarps, xf, lane, gc, g8c);
   acc_g += ga + gb + gc;
   acc_g8 += g8a + g8b + g8c;
 }
@@ -766,35 +782,31 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       while (e < n_items && (int)(items[e] & 0xFF) == ph) ++e;
       return e;
     };
-    // K-split processing of items [cur, e): warp w takes block pairs w, w+8, ...
-    // of every chunk; the tile's 16 sums meet in shared memory at its last chunk.
+    // K-split processing of items [cur, e), each a whole 16-row tile: warp w
+    // takes block pairs w, w+8, w+16; the tile's 16 sums meet in shared memory.
+    // The warps release the item after the epilogue, off the path to it (the
+    // release that completes the slot issues the next copy).
     auto timed_wait = [&](int i, int site) {
       return item_wait(i, full, slot_item, misc, p.err, site);
     };
     auto ksplit = [&](int e, auto&& epilogue) {
-      float acc_g = 0.f, acc_g8 = 0.f;
       for (int i = cur; i < e; ++i) {
         const ItemFields it = unpack_item(items[i]);
-        const int slot = i % kNS;
+        float acc_g = 0.f, acc_g8 = 0.f;
         if (timed_wait(i, kSiteFull * 100 + it.phase % 100))
-          q4_chunk3(ring + slot * kSlotBytes, it.k0, warp, it.nk, kConsumerWarps, xf, lane, acc_g,
-                    acc_g8);
-        __syncwarp();
-        if (lane == 0) release(i, 1);
-        if (it.last) {
-          if (t == 0) {
-            red[warp * 16 + g] = acc_g;
-            red[warp * 16 + g + 8] = acc_g8;
-          }
-          acc_g = acc_g8 = 0.f;
-          cbar();
-          if (ct < 16) {
-            float sum = 0.f;
-            for (int w = 0; w < kConsumerWarps; ++w) sum += red[w * 16 + ct];
-            epilogue(it.tile, ct, sum);
-          }
-          cbar();
+          q4_kslice3(ring + (i % kNS) * kSlotBytes, warp, xf, lane, acc_g, acc_g8);
+        if (t == 0) {
+          red[warp * 16 + g] = acc_g;
+          red[warp * 16 + g + 8] = acc_g8;
         }
+        cbar();
+        if (ct < 16) {
+          float sum = 0.f;
+          for (int w = 0; w < kConsumerWarps; ++w) sum += red[w * 16 + ct];
+          epilogue(it.tile, ct, sum);
+        }
+        cbar();
+        if (lane == 0) release(i, 1);
       }
       cur = e;
     };
@@ -969,29 +981,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
       lstamp(layer, kTsGUDone);
       // ---- P5: the unit's down strip: row tiles x block pair u, K-split
       // partial sums of all 1536 outputs over this unit's 64 k.  Warps 2j and
-      // 2j+1 take item j (24 row tiles), 12 row tiles each: one slot wait and
-      // one release a warp.  The partial sums are stored after the release (a
-      // release's block-scope fence would otherwise wait for them).
+      // 2j+1 take item j (24 row tiles), 12 row tiles each, in two rounds of
+      // six (a loop, not straight code: the instruction cache): one slot wait
+      // and one release a warp.
       {
         const int e = phase_end(ph + kPhDown);
         if (e - cur == kDownItems) {
           const int i = cur + (warp >> 1);
-          const int slot = i % kNS;
           const int b0 = kDownRowTilesPerWarp * (warp & 1);
-          float acc[kDownRowTilesPerWarp][2];
-#pragma unroll
-          for (int j = 0; j < kDownRowTilesPerWarp; ++j) acc[j][0] = acc[j][1] = 0.f;
-          if (timed_wait(i, kSiteFull * 100 + (int)(items[i] & 0xFF) % 100)) {
-            const uint8_t* sb = ring + slot * kSlotBytes + b0 * kBpBytes;
-#pragma unroll
-            for (int j = 0; j < kDownRowTilesPerWarp; j += 3) {
-              q4_bp(sb + (j + 0) * kBpBytes, 0, 0, hf, lane, acc[j][0], acc[j][1]);
-              q4_bp(sb + (j + 1) * kBpBytes, 0, 0, hf, lane, acc[j + 1][0], acc[j + 1][1]);
-              q4_bp(sb + (j + 2) * kBpBytes, 0, 0, hf, lane, acc[j + 2][0], acc[j + 2][1]);
-            }
-          }
-          __syncwarp();
-          if (lane == 0) release(i, kConsumerWarps / kWarpsPerDownItem);
+          const bool landed = timed_wait(i, kSiteFull * 100 + (int)(items[i] & 0xFF) % 100);
+          const uint8_t* sb = ring + (i % kNS) * kSlotBytes + b0 * kBpBytes;
           // The warp's 12 row tiles are 192 consecutive rows of the unit's
           // partial vector, and every lane of group g holds rows g and g + 8 of
           // each tile: lane (g, t) stores row 8t + g of a pair of tiles, one
@@ -999,10 +998,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
           const uint16_t tg = (uint16_t)tagof(layer);
           const ItemFields it = unpack_item(items[i]);
           unsigned long long* part = p.mlp_part + (size_t)it.tile * kHidden + 16 * (it.k0 + b0) + 8 * t + g;
+#pragma unroll 1
+          for (int r = 0; r < kDownRowTilesPerWarp; r += kDownRound) {
+            float acc[kDownRound][2];
 #pragma unroll
-          for (int m = 0; m < kDownRowTilesPerWarp / 2; ++m)
-            st_tag32(part + 32 * m, tg, t == 0 ? acc[2 * m][0] : t == 1 ? acc[2 * m][1]
-                                      : t == 2 ? acc[2 * m + 1][0] : acc[2 * m + 1][1]);
+            for (int j = 0; j < kDownRound; ++j) acc[j][0] = acc[j][1] = 0.f;
+            if (landed) {
+#pragma unroll
+              for (int j = 0; j < kDownRound; j += 3) {
+                q4_bp(sb + (r + j + 0) * kBpBytes, 0, 0, hf, lane, acc[j][0], acc[j][1]);
+                q4_bp(sb + (r + j + 1) * kBpBytes, 0, 0, hf, lane, acc[j + 1][0], acc[j + 1][1]);
+                q4_bp(sb + (r + j + 2) * kBpBytes, 0, 0, hf, lane, acc[j + 2][0], acc[j + 2][1]);
+              }
+            }
+#pragma unroll
+            for (int m = 0; m < kDownRound / 2; ++m)
+              st_tag32(part + 16 * r + 32 * m, tg, t == 0 ? acc[2 * m][0] : t == 1 ? acc[2 * m][1]
+                                                 : t == 2 ? acc[2 * m + 1][0] : acc[2 * m + 1][1]);
+          }
+          __syncwarp();
+          if (lane == 0) release(i, kConsumerWarps / kWarpsPerDownItem);
         }
         cur = e;
       }
@@ -1018,21 +1033,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
         const int R0 = (int)(blockIdx.x * kHidden / gridDim.x);
         const int R1 = (int)((blockIdx.x + 1) * kHidden / gridDim.x);
         const int n_rows = R1 - R0;
-        const int n_words = n_rows * kMlpUnits;
         float* stage = reinterpret_cast<float*>(uni + kOffMlpStage);
-        // word w of the CTA's share: unit w / n_rows, row R0 + w % n_rows
+        // word w: unit w / kMaxReduceRows, row R0 + w % kMaxReduceRows (a
+        // constant divisor; rows past n_rows are not polled).  A warp's words
+        // are runs of consecutive rows of a unit: few L2 sectors a poll.
         auto word_src = [&](int w) {
-          return p.mlp_part + (size_t)(w / n_rows) * kHidden + R0 + w % n_rows;
+          return p.mlp_part + (size_t)(w / kMaxReduceRows) * kHidden + R0 + w % kMaxReduceRows;
         };
-        auto word_dst = [&](int w) { return (w % n_rows) * kMlpUnits + w / n_rows; };
+        auto word_dst = [&](int w) { return (w % kMaxReduceRows) * kMlpUnits + w / kMaxReduceRows; };
         // (test hook: with stall_site == kSiteDownPart the poll expects a tag
         // nothing writes, so the wait runs out)
         const uint32_t ptag = p.stall_site == kSiteDownPart ? tagof(255) : tagof(layer);
         uint32_t pending = 0;
         unsigned long long v[kReducePerThread];
 #pragma unroll
-        for (int j = 0; j < kReducePerThread; ++j)
-          if (ct + j * kFusedThreads < n_words) pending |= 1u << j;
+        for (int j = 0; j < kReducePerThread; ++j) {
+          const int w = ct + j * kFusedThreads;
+          if (w < kMaxReduceRows * kMlpUnits && w % kMaxReduceRows < n_rows) pending |= 1u << j;
+        }
         uint64_t t0 = 0;
         for (uint32_t it = 0; pending; ++it) {
 #pragma unroll

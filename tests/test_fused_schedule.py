@@ -12,7 +12,8 @@ these properties of it:
   * a CTA's items are in stream order (phases ascending, a tile's chunks
     consecutive and ascending, `last` on its final chunk);
   * QKV tiles sit on the first 128 CTAs, one each (the attention units use
-    the last CTAs); a CTA holds at most one O tile per layer;
+    the last CTAs); a CTA holds at most one O tile per layer; a QKV or O tile
+    is one item over its whole K (warp w takes block pairs w, w+8, w+16);
   * CTA u < 140 owns MLP unit u: gate/up tiles 8u .. 8u+7 (seq 0..7, one item
     each, warp w takes item cur + w) and the down strip of unit u; the other
     CTAs own none;
@@ -93,6 +94,8 @@ def test_schedule_invariants(n_layers, grid):
                 assert kind in TILES and tile < TILES[kind]
                 assert k0 + nk <= KSTEPS[kind]
                 assert last == (k0 + nk == KSTEPS[kind])
+                if kind in (PH_QKV, PH_O):
+                    assert k0 == 0 and nk == KSTEPS[kind], "a QKV / O tile must be one item"
                 if kind == PH_GU:
                     assert k0 == 0 and nk == KSTEPS[PH_GU], "a gate/up tile must be one item"
                     assert tile // 8 == c and seq == tile % 8, "unit c's tiles 8c .. 8c+7 on CTA c"
