@@ -161,7 +161,7 @@ __device__ __forceinline__ bool aborted(volatile Misc* m, const int* err) {
 }
 // Records the timeout and where it happened: err[1] = site, err[2] = CTA,
 // err[3] = thread (the first failure wins).
-__device__ __forceinline__ void fail(volatile Misc* m, int* err, int site) {
+__device__ __noinline__ void fail(volatile Misc* m, int* err, int site) {
   m->abort = 1;
   if (err && atomicCAS(err, 0, kDevWaitTimeout) == 0) {
     err[1] = site;
@@ -169,6 +169,31 @@ __device__ __forceinline__ void fail(volatile Misc* m, int* err, int site) {
     err[3] = threadIdx.x;
   }
 }
+// The abort flags and the time limit of a wait, looked at on one round in
+// kWaitCheckEvery and never on the first: the abort check reads global
+// memory, and a check on the first round would delay the round that sees the
+// data by an L2 round trip whenever it arrives just after the first look.
+// wait_check_slow returns the wait's start time (set at the first check) or
+// kWaitStop once the wait must end (another CTA failed, or the limit passed).
+constexpr uint32_t kWaitCheckEvery = 64;
+constexpr uint64_t kWaitStop = ~0ull;
+__device__ __noinline__ uint64_t wait_check_slow(uint64_t t0, volatile Misc* m, int* err, int site) {
+  if (aborted(m, err)) return kWaitStop;
+  const uint64_t now = globaltimer();
+  if (t0 == 0) return now;
+  if (now - t0 > m->wait_ns) {
+    fail(m, err, site);
+    return kWaitStop;
+  }
+  return t0;
+}
+__device__ __forceinline__ bool wait_check(uint32_t it, uint64_t& t0, volatile Misc* m, int* err,
+                                           int site) {
+  if (it % kWaitCheckEvery != kWaitCheckEvery - 1) return false;
+  t0 = wait_check_slow(t0, m, err, site);
+  return t0 == kWaitStop;
+}
+
 // Wait sites (x 100 + layer) reported by fail().
 enum WaitSite : int {
   kSiteEmpty = 1, kSiteFull = 2, kSiteXIn = 3, kSiteQ = 4, kSiteKV = 5, kSiteCombine = 6,
@@ -208,15 +233,7 @@ __device__ __forceinline__ void poll_units(const uint32_t* src, int n_units, int
         pending &= ~(1u << j);
       }
     if (!pending) break;
-    if ((it & 63) == 0) {
-      if (aborted(m, err)) return;
-      const uint64_t now = globaltimer();
-      if (it == 0) t0 = now;
-      else if (now - t0 > m->wait_ns) {
-        fail(m, err, site);
-        return;
-      }
-    }
+    if (wait_check(it, t0, m, err, site)) return;
     // no sleep between rounds: a hop is on the step's critical path, and a
     // 32 ns back-off measured 0.8% slower end to end
   }
@@ -230,15 +247,7 @@ __device__ __noinline__ bool slot_wait_slow(uint64_t* bar, uint32_t parity, vola
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 0) {
-      if (aborted(m, err)) return false;
-      const uint64_t now = globaltimer();
-      if (it == 0) t0 = now;
-      else if (now - t0 > m->wait_ns) {
-        fail(m, err, site);
-        return false;
-      }
-    }
+    if (wait_check(it, t0, m, err, site)) return false;
   }
 }
 __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, volatile Misc* m,
@@ -255,15 +264,7 @@ __device__ __noinline__ bool item_issue_wait_slow(int i, volatile const int* slo
                                                   volatile Misc* m, int* err, int site) {
   uint64_t t0 = 0;
   for (uint32_t it = 0; slot_item[i % kNS] != i; ++it) {
-    if ((it & 63) == 0) {
-      if (aborted(m, err)) return false;
-      const uint64_t now = globaltimer();
-      if (it == 0) t0 = now;
-      else if (now - t0 > m->wait_ns) {
-        fail(m, err, site);
-        return false;
-      }
-    }
+    if (wait_check(it, t0, m, err, site)) return false;
     __nanosleep(32);
   }
   return true;
@@ -436,41 +437,45 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
     }
   };
   const uint32_t first = p0 + warp * 16;
-  if (first < p1) issue_kv(first, false);
-  // q of the 6 heads of this kv group, and the step's new k / v rows.
-  poll_units<1>(p.q_ll + kvh * 768, 96, ct, 128, tag, misc, p.err, kSiteQ * 100 + layer, [&](int u, const __half* v) {
-    reinterpret_cast<uint4*>(qs)[u] = *reinterpret_cast<const uint4*>(v);
-  });
-  if (has_new) {
-    poll_units<1>(p.kv_ll, 64, ct, 128, tag, misc, p.err, kSiteKV * 100 + layer, [&](int u, const __half* v) {
-      const int w0 = 8 * u;  // words 0..255 = k, 256..511 = v
-      if (((w0 & 255) >> 7) != kvh) return;
-      __half* dst = (w0 < 256 ? knew : vnew) + (w0 & 127);
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(v);
-    });
-  }
-  abar();
-  astamp(1);
-  uint32_t qf[16];
-  {
-    const uint4* qp = reinterpret_cast<const uint4*>(qs + (g < 6 ? g : 0) * kHeadDim + 32 * t);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint4 v = g < 6 ? qp[j] : make_uint4(0, 0, 0, 0);
-      qf[4 * j] = v.x;
-      qf[4 * j + 1] = v.y;
-      qf[4 * j + 2] = v.z;
-      qf[4 * j + 3] = v.w;
-    }
-  }
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  for (uint32_t base = first; base < p1; base += kAttnWarpsFused * 16) {
-    if (base != first) {
-      issue_kv(base, true);
-    } else if (last >= base && last < base + 16) {
+  uint32_t qf[16];
+  // One copy of the sub-tile issue (the instruction cache): the first
+  // sub-tile is issued before the waits for q and the new k / v rows, which
+  // the first pass takes; a warp without positions only takes part in those.
+  for (uint32_t base = first;; base += kAttnWarpsFused * 16) {
+    if (base < p1) issue_kv(base, base != first);
+    if (base == first) {
+      // q of the 6 heads of this kv group, and the step's new k / v rows.
+      poll_units<1>(p.q_ll + kvh * 768, 96, ct, 128, tag, misc, p.err, kSiteQ * 100 + layer,
+                    [&](int u, const __half* v) {
+                      reinterpret_cast<uint4*>(qs)[u] = *reinterpret_cast<const uint4*>(v);
+                    });
+      if (has_new) {
+        poll_units<1>(p.kv_ll, 64, ct, 128, tag, misc, p.err, kSiteKV * 100 + layer,
+                      [&](int u, const __half* v) {
+                        const int w0 = 8 * u;  // words 0..255 = k, 256..511 = v
+                        if (((w0 & 255) >> 7) != kvh) return;
+                        __half* dst = (w0 < 256 ? knew : vnew) + (w0 & 127);
+                        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(v);
+                      });
+      }
+      abar();
+      astamp(1);
+      const uint4* qp = reinterpret_cast<const uint4*>(qs + (g < 6 ? g : 0) * kHeadDim + 32 * t);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = g < 6 ? qp[j] : make_uint4(0, 0, 0, 0);
+        qf[4 * j] = v.x;
+        qf[4 * j + 1] = v.y;
+        qf[4 * j + 2] = v.z;
+        qf[4 * j + 3] = v.w;
+      }
+    }
+    if (base >= p1) break;
+    if (base == first && last >= base && last < base + 16) {
       // patch the step's new row into the prefetched sub-tile
       const uint32_t pg = min(base + g, p1 - 1), pg8 = min(base + g + 8, p1 - 1);
       if (pg == last || pg8 == last) {
@@ -616,24 +621,35 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
   const uint32_t per_split = nz + 2 * nh;  // o slice, m[nh], l[nh]
   float* stage = reinterpret_cast<float*>(uni + kAVs);
   const uint32_t n_words = S_eff * per_split;
+  // word w of the slice: split w / per_split, entry w % per_split; the
+  // thread's words w0 + 128 j, their addresses computed once (128 = dq
+  // splits + dr entries).
+  const uint32_t dq = 128 / per_split, dr = 128 % per_split;
+  const unsigned long long* kv_part = p.attn_part + (size_t)kvh * kMaxAttnSplits * kAttnPartWords;
   for (uint32_t w0 = ct; w0 < n_words; w0 += 128 * 8) {
     unsigned long long v[8];
+    const unsigned long long* src[8];
     uint32_t pending = 0;
+    {
+      uint32_t sp = w0 / per_split, r = w0 % per_split;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (w0 + j * 128 < n_words) pending |= 1u << j;
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t word = r < nz ? z0 + r : r < nz + nh ? 768 + h0 + (r - nz) : 774 + h0 + (r - nz - nh);
+        src[j] = kv_part + (size_t)sp * kAttnPartWords + word;
+        if (w0 + j * 128 < n_words) pending |= 1u << j;
+        sp += dq;
+        r += dr;
+        if (r >= per_split) {
+          r -= per_split;
+          ++sp;
+        }
+      }
+    }
     uint64_t t0 = 0;
     for (uint32_t it = 0; pending; ++it) {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (pending & (1u << j)) {
-          const uint32_t w = w0 + j * 128, sp = w / per_split, r = w % per_split;
-          uint32_t word;
-          if (r < nz) word = z0 + r;
-          else if (r < nz + nh) word = 768 + h0 + (r - nz);
-          else word = 774 + h0 + (r - nz - nh);
-          v[j] = ld_tag64(p.attn_part + ((size_t)kvh * kMaxAttnSplits + sp) * kAttnPartWords + word);
-        }
+        if (pending & (1u << j)) v[j] = ld_tag64(src[j]);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if ((pending & (1u << j)) && (uint32_t)(v[j] >> 32) == tag) {
@@ -641,15 +657,7 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
           pending &= ~(1u << j);
         }
       if (!pending) break;
-      if ((it & 63) == 0) {
-        if (aborted(misc, p.err)) break;
-        const uint64_t now = globaltimer();
-        if (it == 0) t0 = now;
-        else if (now - t0 > misc->wait_ns) {
-          fail(misc, p.err, kSiteCombine * 100 + layer);
-          break;
-        }
-      }
+      if (wait_check(it, t0, misc, p.err, kSiteCombine * 100 + layer)) break;
     }
   }
   abar();
@@ -661,9 +669,11 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
   for (uint32_t hl = ct >> 5; hl < nh; hl += kAttnWarpsFused) {
     const uint32_t ln = ct & 31;
     float M = -INFINITY;
+#pragma unroll 1
     for (uint32_t sp = ln; sp < S_eff; sp += 32) M = fmaxf(M, stage[sp * per_split + nz + hl]);
     M = warp_max(M);
     float Ls = 0.f;
+#pragma unroll 1
     for (uint32_t sp = ln; sp < S_eff; sp += 32) {
       const float c = expf(stage[sp * per_split + nz + hl] - M);
       cfac[sp * nh + hl] = c;
@@ -676,6 +686,7 @@ __device__ __forceinline__ void attention_unit(const FusedParams& p, int layer, 
   for (uint32_t z = z0 + ct; z < z1; z += 128) {
     const uint32_t hl = z / kHeadDim - h0;
     float O = 0.f;
+#pragma unroll 2
     for (uint32_t sp = 0; sp < S_eff; ++sp) O += stage[sp * per_split + (z - z0)] * cfac[sp * nh + hl];
     st_tag16(p.attn_ll + kvh * 768 + z, tag, f2h(O / ctot[hl]));
   }
@@ -1063,15 +1074,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
               pending &= ~(1u << j);
             }
           if (!pending) break;
-          if ((it & 63) == 0) {
-            if (aborted(misc, p.err)) break;
-            const uint64_t now = globaltimer();
-            if (it == 0) t0 = now;
-            else if (now - t0 > misc->wait_ns) {
-              fail(misc, p.err, kSiteDownPart * 100 + layer);
-              break;
-            }
-          }
+          if (wait_check(it, t0, misc, p.err, kSiteDownPart * 100 + layer)) break;
         }
         cbar();
         const __half* db = p.down_bias + (size_t)layer * kHidden;
