@@ -406,9 +406,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (warp < 2) {  // warp hg: head group hg, lane = split
           const int hg = warp;
           const bool have = (uint32_t)lane < w.s_eff;
+          // the split's 6 (m, l) pairs in one go (48 bytes, 16-byte aligned)
+          float ml[12];
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            const float4 v = have ? __ldcg(reinterpret_cast<const float4*>(
+                                        all_ml + ((size_t)lane * 2 + hg) * 12) + q)
+                                  : make_float4(-INFINITY, 0.f, -INFINITY, 0.f);
+            ml[4 * q] = v.x;
+            ml[4 * q + 1] = v.y;
+            ml[4 * q + 2] = v.z;
+            ml[4 * q + 3] = v.w;
+          }
+#pragma unroll
           for (int head = 0; head < 6; ++head) {
-            const float m = have ? __ldcg(all_ml + ((size_t)lane * 2 + hg) * 12 + 2 * head) : -INFINITY;
-            const float l = have ? __ldcg(all_ml + ((size_t)lane * 2 + hg) * 12 + 2 * head + 1) : 0.f;
+            const float m = ml[2 * head];
+            const float l = ml[2 * head + 1];
             float M = m;
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
@@ -425,19 +438,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         consumers_sync();
-        for (int idx = ctid; idx < 2 * 6 * kHeadDim; idx += 256) {
-          const int hg = idx / (6 * kHeadDim), r = idx % (6 * kHeadDim), head = r / kHeadDim;
-          float part[kMaxSplits];
+        {
+          // The thread's six outputs (idx = ctid + 256 j), summed over the
+          // splits in split order; each split's six partials are loaded
+          // together, so the merge waits one L2 round trip per split rather
+          // than one per output.
+          constexpr int kPer = 2 * 6 * kHeadDim / 256;
+          static_assert(kPer * 256 == 2 * 6 * kHeadDim, "merge outputs per thread");
+          float O[kPer];
+          int hgj[kPer], rj[kPer];
 #pragma unroll
-          for (int sp = 0; sp < kMaxSplits; ++sp)
-            part[sp] = (uint32_t)sp < w.s_eff
-                           ? __ldcg(all_o + ((size_t)sp * 2 + hg) * (6 * kHeadDim) + r)
-                           : 0.f;
-          float O = 0.f;
+          for (int j = 0; j < kPer; ++j) {
+            const int idx = ctid + 256 * j;
+            hgj[j] = idx / (6 * kHeadDim);
+            rj[j] = idx % (6 * kHeadDim);
+            O[j] = 0.f;
+          }
+#pragma unroll 2
+          for (uint32_t sp = 0; sp < w.s_eff; ++sp) {
+            float v[kPer];
 #pragma unroll
-          for (int sp = 0; sp < kMaxSplits; ++sp)
-            if ((uint32_t)sp < w.s_eff) O += part[sp] * s.sc[hg][sp][head];
-          store_out(p, w.seq, (6 * hg) * kHeadDim + r, O / s.hsum[hg][head]);
+            for (int j = 0; j < kPer; ++j)
+              v[j] = __ldcg(all_o + ((size_t)sp * 2 + hgj[j]) * (6 * kHeadDim) + rj[j]);
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) O[j] += v[j] * s.sc[hgj[j]][sp][rj[j] / kHeadDim];
+          }
+#pragma unroll
+          for (int j = 0; j < kPer; ++j)
+            store_out(p, w.seq, (6 * hgj[j]) * kHeadDim + rj[j],
+                      O[j] / s.hsum[hgj[j]][rj[j] / kHeadDim]);
         }
         if (ctid == 0) p.counters[w.seq] = 0;  // re-arm for the next launch
       }
