@@ -125,6 +125,70 @@ struct Unit {
   int seq, split;
   uint32_t p0, p1, s_eff;
 };
+
+// q (qs, 12 heads x 128) and the step's new k | v rows (kvn: k of kv heads 0,
+// 1, then v) of sequence `seq` from the QKV partials, as the batched QKV
+// finish forms them: sum of the splits in split order, + bias, rounded to fp16,
+// RoPE on the 14 q / k heads at position pos (rope.metal:12-39), the v rows
+// rounded after the bias.  256 consumer threads: RoPE pairs ctid + 256 j
+// (head = pair / 64), v element ctid; every split's loads issued together.
+__device__ __forceinline__ void form_qkv(const AttnParams& p, int seq, uint32_t pos, __half* qs,
+                                         __half* kvn, int ctid) {
+  constexpr int kPairs = (kHeads + kKVHeads) * 64;   // 896
+  constexpr int kJobs = (kPairs + 255) / 256;          // 4
+  const size_t stride = (size_t)p.qkv_rows * kQKVRows;
+  const float* part = p.qkv_part + (size_t)seq * kQKVRows;
+  const float* cs = p.rope_cs + (size_t)pos * 128;
+  int i1[kJobs];
+  float s1[kJobs], s2[kJobs];
+  __half b1[kJobs], b2[kJobs];
+  float2 rot[kJobs];   // (cos, sin) of the pair
+#pragma unroll
+  for (int j = 0; j < kJobs; ++j) {   // biases and RoPE factors loaded with the partials
+    const int pr = ctid + 256 * j;
+    const int pc = pr < kPairs ? pr : 0;
+    i1[j] = (pc >> 6) * 128 + (pc & 63);
+    s1[j] = s2[j] = 0.f;
+    b1[j] = p.qkv_bias[i1[j]];
+    b2[j] = p.qkv_bias[i1[j] + 64];
+    rot[j] = reinterpret_cast<const float2*>(cs)[pc & 63];
+  }
+  const int iv = kHidden + kKVDim + ctid;   // v element (ctid < 256)
+  const __half bvh = p.qkv_bias[iv];
+  float sv = 0.f;
+#pragma unroll 4
+  for (int sp = 0; sp < p.qkv_splits; ++sp) {
+    const float* ps = part + (size_t)sp * stride;
+    float a[kJobs], b[kJobs];
+#pragma unroll
+    for (int j = 0; j < kJobs; ++j) {
+      a[j] = __ldcg(ps + i1[j]);
+      b[j] = __ldcg(ps + i1[j] + 64);
+    }
+    const float c = __ldcg(ps + iv);
+#pragma unroll
+    for (int j = 0; j < kJobs; ++j) {
+      s1[j] += a[j];
+      s2[j] += b[j];
+    }
+    sv += c;
+  }
+#pragma unroll
+  for (int j = 0; j < kJobs; ++j) {
+    const int pr = ctid + 256 * j;
+    if (pr >= kPairs) break;
+    const int head = pr >> 6, i0 = i1[j];
+    const float x1 = h2f(f2h(s1[j] + h2f(b1[j])));
+    const float x2 = h2f(f2h(s2[j] + h2f(b2[j])));
+    const float c = rot[j].x, sn = rot[j].y;
+    const __half r1 = f2h(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
+    const __half r2 = f2h(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, c)));
+    __half* dst = head < kHeads ? qs + i0 : kvn + (i0 - kHidden);
+    dst[0] = r1;
+    dst[64] = r2;
+  }
+  kvn[kKVDim + ctid] = f2h(sv + h2f(bvh));
+}
 // Unit u = (sequence u / max_s, split u % max_s): n_tiles = ceil(L/64) tiles
 // in S = min(max_s, n_tiles) near-equal runs; false if the split is empty.
 __device__ __forceinline__ bool unit_of(const AttnParams& p, int u, int max_s, Unit& w) {
@@ -209,12 +273,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       continue;
     }
+    // q (and in a decode step's fused mode the new k / v rows) in shared
+    // memory of the merge: q in wo (read into registers before the first tile;
+    // the merge writes wo after the last), the rows in sc (used by the last
+    // tile's patch; sc is written only after the merge's barriers).
+    const uint32_t pos = p.seq_len[(size_t)w.seq * p.seq_len_stride] - 1;
+    __half* qs = reinterpret_cast<__half*>(&s.wo[0][0][0]);
+    __half* kvn = reinterpret_cast<__half*>(&s.sc[0][0][0]);
+    static_assert(sizeof(s.sc) >= 2 * kKVDim * sizeof(__half), "new k / v rows exceed sc");
+    static_assert(sizeof(s.wo) >= kHidden * sizeof(__half), "q exceeds wo");
+    const bool fused_qkv = p.qkv_part != nullptr;
+    const bool owns_pos = fused_qkv && pos >= w.p0 && pos < w.p1;
+    if (fused_qkv) {
+      form_qkv(p, w.seq, pos, qs, kvn, ctid);
+      consumers_sync();
+      if (owns_pos && ctid < 64) {
+        // the new rows into the caches, for the steps after this one
+        const int kvs = p.row_seq ? p.row_seq[w.seq] : w.seq;
+        const size_t off = (size_t)kvs * p.kv_seq_stride + (size_t)pos * p.kv_pos_stride;
+        __half* dst = const_cast<__half*>(ctid < 32 ? p.k : p.v) + off;
+        reinterpret_cast<uint4*>(dst)[ctid & 31] = reinterpret_cast<const uint4*>(kvn)[ctid];
+      }
+    }
     // q fragments: lane (g,t) holds q[head 6h + g][32t .. 32t+31] (zero for g >= 6).
     uint32_t qf[16];
     {
       const bool hv = g < 6;
       const uint4* qp = reinterpret_cast<const uint4*>(
-          p.q + (size_t)w.seq * p.q_seq_stride + (size_t)(6 * h + (hv ? g : 0)) * kHeadDim + 32 * t);
+          (fused_qkv ? qs : p.q + (size_t)w.seq * p.q_seq_stride) + (size_t)(6 * h + (hv ? g : 0)) * kHeadDim +
+          32 * t);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint4 v = hv ? qp[j] : make_uint4(0, 0, 0, 0);
@@ -237,6 +324,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t base = tb + 16 * slice;
       const int r0 = 16 * slice;  // first row of this warp in the boxes
       bool zeroed = false;
+      if (ok && owns_pos && pos >= base && pos < base + 16) {
+        // The new position's k / v rows of this warp's head into the stage
+        // (the cache may not hold them yet): lane -> (k|v, 64-element box,
+        // 16-byte chunk), swizzled as the tensor map lays the box out.
+        const int r = (int)(pos - tb), kv = lane >> 4, half = (lane >> 3) & 1, ch = lane & 7;
+        uint8_t* box = kv ? s.v[st][2 * h + half] : s.k[st][2 * h + half];
+        *reinterpret_cast<uint4*>(box + swz(r, ch)) =
+            *reinterpret_cast<const uint4*>(kvn + kv * kKVDim + h * kHeadDim + half * 64 + ch * 8);
+        zeroed = true;   // generic stores into the stage: proxy fence before its release
+        __syncwarp();
+      }
       if (ok && base < w.p1) {
         // ---- S^T = K q^T: lane reads K[row g][32t..32t+31] and K[row g+8][..].
         float sv[4] = {0.f, 0.f, 0.f, 0.f};

@@ -285,7 +285,10 @@ int gemm(const uint8_t* blob, bool q4, const uint8_t* act, const InferenceManage
 
 }  // namespace
 
-int tc_kernels_per_step(int n_layers) { return 1 + 8 * n_layers + 1; }
+// Decode steps: 7 kernels a layer (the attention forms q and the new k / v
+// rows from the QKV partials itself); a chunked prefill launches the QKV
+// finish too (8 a layer).
+int tc_kernels_per_step(int n_layers) { return 1 + 7 * n_layers + 1; }
 
 int build_tc_weights(QwenModel& m, int max_ctx, cudaStream_t st) {
   TcWeights& t = m.tc;
@@ -396,6 +399,17 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, const TcRows& v, int sm_
   ap.row_seq = v.row_seq;
   ap.kv_n_seq = s.batch;
   ap.err = s.err;
+  // Decode rows: the attention forms q and the step's new k / v rows from the
+  // QKV partials (no finish kernel).  A chunked prefill's rows attend to each
+  // other's new rows, which must all be in the caches first: it keeps the
+  // QKV finish.
+  const bool fused_qkv = v.row_seq == nullptr;
+  if (fused_qkv) {
+    ap.qkv_part = s.tc_part;
+    ap.qkv_splits = p.qkv;
+    ap.qkv_rows = B;
+    ap.rope_cs = t.rope_cs;
+  }
   attn_bind_scratch(ap, v.attn_scratch, v.attn_splits, B);
 
   QWEN_TRY(launch_pdl(k_rms_to_act, dim3(B), dim3(512), st, v.x, m.layers[0].input_norm, s.act_h, nb));
@@ -411,10 +425,14 @@ int enqueue_tc_model(QwenModel& m, InferenceManager& s, const TcRows& v, int sm_
 
     QWEN_TRY(gemm(qkv, true, s.act_h, s, B, kQKVRows, kHidden, p.qkv, s.tc_part, nullptr, 0, st));
     mark();
-    QWEN_TRY(launch_pdl(k_qkv_finish, dim3(B, kHeads + kKVHeads + 1), dim3(64), st, s.tc_part,
-                        p.qkv, B, L.qkv_bias, t.rope_cs, v.seq_len, v.seq_len_stride, v.row_seq,
-                        s.max_ctx, v.q, kc, vc, s.kv_seq_stride()));
-    mark();
+    if (fused_qkv) {
+      ap.qkv_bias = L.qkv_bias;
+    } else {
+      QWEN_TRY(launch_pdl(k_qkv_finish, dim3(B, kHeads + kKVHeads + 1), dim3(64), st, s.tc_part,
+                          p.qkv, B, L.qkv_bias, t.rope_cs, v.seq_len, v.seq_len_stride, v.row_seq,
+                          s.max_ctx, v.q, kc, vc, s.kv_seq_stride()));
+      mark();
+    }
     ap.k = kc;
     ap.v = vc;
     if (launch_attention_decode(ap, v.attn_splits, B, st, true) != 0)

@@ -47,6 +47,17 @@ struct AttnParams {
   float* part_ml;           // scratch: [n_seq][2][max_splits][6][2]
   uint32_t* counters;       // scratch: [n_seq][2], zero between launches
   int* err;                 // device error word (may be null)
+  // Decode steps of the batched engine: q and the step's new k / v rows are
+  // formed here from the QKV projection's split-K partial sums (split order,
+  // + bias, fp16 rounding, RoPE at position seq_len - 1) instead of by a finish
+  // kernel: q never leaves the CTA, the new rows are patched into the tile
+  // that holds that position and appended to the caches by the unit that owns
+  // it.  qkv_part = null: q comes from `q` and the caches already hold the row.
+  const float* qkv_part;    // [splits][rows][2048] fp32
+  int qkv_splits;
+  int qkv_rows;             // rows of each split's block (the GEMM's batch)
+  const __half* qkv_bias;   // [2048] this layer's q | k | v biases
+  const float* rope_cs;     // [max_ctx][64][2] cos / sin
 };
 int attn_max_splits(int max_ctx, int n_seq);
 size_t attn_scratch_bytes(int max_splits, int n_seq);

@@ -194,7 +194,8 @@ class QwenEngine:
         ms = np.zeros(n.value, np.float32)
         check(lib().qwen_engine_profile_step(self._h, ms.ctypes.data_as(ctypes.c_void_p), n.value,
                                              ctypes.byref(n)))
-        per_layer = ["qkv_gemm", "qkv_finish", "attention", "o_gemm", "o_finish",
+        # a decode step: the attention forms q and the new k / v rows itself
+        per_layer = ["qkv_gemm", "attention_qkv", "o_gemm", "o_finish",
                      "gu_gemm_swiglu", "down_gemm", "down_finish"]
         names = ["rmsnorm"] + per_layer * ((n.value - 2) // len(per_layer)) + ["lm_gemm"]
         return list(zip(names, ms.tolist()))
