@@ -152,10 +152,14 @@ __device__ __forceinline__ void hist_clear(SS& s) {
 
 // Adds weight e at digit d to this warp's histogram for each lane that is a
 // member.  Zero weights change no sum, so callers pass them as non-members.
-// When every member of the warp falls in one digit (peaked distributions put
-// almost all weights in digit 0 of the later passes) the warp reduces first
-// and adds once.  (Partitioning the warp by digit with match.any before the
-// adds measured slower on flat distributions than the colliding atomics.)
+// The lanes of the first member's digit, and then those of digit 0, are
+// summed across the warp (two 32-bit halves, exact) and added once; the other
+// members add alone.  Digit 0 is where most weights of a flat distribution
+// fall (every weight below 2^-7 of the largest in the first pass), and a
+// warp's lanes all adding to one counter serialise: on random-init logits the
+// 64-sequence weight pass took 36 us, 13 us with the sums (gating them on two
+// or more lanes sharing the digit measured slower).  (Partitioning the
+// warp by digit with match.any measured slower on flat distributions.)
 template <class SS>
 __device__ __forceinline__ void hist_add(SS& s, bool member, uint32_t e, uint32_t d) {
   const int lane = threadIdx.x & 31, wid = (threadIdx.x >> 5) / SS::kWarpsPerHist;
@@ -163,15 +167,32 @@ __device__ __forceinline__ void hist_add(SS& s, bool member, uint32_t e, uint32_
   uint32_t* hhi = s.whist[wid][1];
   const uint32_t mm = __ballot_sync(0xffffffffu, member);
   if (mm == 0u) return;
-  const uint32_t d0 = __shfl_sync(0xffffffffu, d, __ffs(mm) - 1);
-  if (__all_sync(0xffffffffu, !member || d == d0)) {
-    const uint32_t lo = __reduce_add_sync(0xffffffffu, member ? (e & 0xFFFFu) : 0u);
-    const uint32_t hi = __reduce_add_sync(0xffffffffu, member ? (e >> 16) : 0u);
-    if (lane == 0) {
+  const int first = __ffs(mm) - 1;
+  const uint32_t d0 = __shfl_sync(0xffffffffu, d, first);
+  {
+    const bool in = member && d == d0;
+    const uint32_t lo = __reduce_add_sync(0xffffffffu, in ? (e & 0xFFFFu) : 0u);
+    const uint32_t hi = __reduce_add_sync(0xffffffffu, in ? (e >> 16) : 0u);
+    if (lane == first) {
       atomicAdd(&hlo[d0], lo);
       atomicAdd(&hhi[d0], hi);
     }
-  } else if (member) {
+    member = member && !in;
+  }
+  if (d0 != 0u) {
+    const bool in = member && d == 0u;
+    const uint32_t zm = __ballot_sync(0xffffffffu, in);
+    if (zm != 0u) {
+      const uint32_t lo = __reduce_add_sync(0xffffffffu, in ? (e & 0xFFFFu) : 0u);
+      const uint32_t hi = __reduce_add_sync(0xffffffffu, in ? (e >> 16) : 0u);
+      if (lane == __ffs(zm) - 1) {
+        atomicAdd(&hlo[0], lo);
+        atomicAdd(&hhi[0], hi);
+      }
+    }
+    member = member && !in;
+  }
+  if (member) {
     atomicAdd(&hlo[d], e & 0xFFFFu);
     atomicAdd(&hhi[d], e >> 16);
   }
@@ -296,10 +317,16 @@ __global__ void __launch_bounds__(kSampThreads)
   if (!(temperature > 0.0f)) {
     float best = -INFINITY;
     int idx = 0x7fffffff;
-#pragma unroll 4
+    __half lv[kSampPerThread];   // all loads in flight before the first compare
+#pragma unroll
+    for (int k = 0; k < kSampPerThread; ++k) {
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      lv[k] = i < n_local ? lg[lo + i] : __ushort_as_half((unsigned short)0x7e00u);
+    }
+#pragma unroll
     for (int k = 0; k < kSampPerThread; ++k) {   // increasing id: the first maximum is kept
       const int i = k * kSampThreads + (int)threadIdx.x;
-      const float v = i < n_local ? h2f(lg[lo + i]) : __int_as_float(0x7fc00000);
+      const float v = h2f(lv[k]);
       if (!isnan(v) && v > best) { best = v; idx = lo + i; }
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -351,11 +378,19 @@ __global__ void __launch_bounds__(kSampThreads)
       sc[k] = x;
     }
   } else {
-#pragma unroll 4
+    // every logit of the thread loaded before the first is used (the loads
+    // are the pass's latency: four in flight at a time cost ~10 us)
+    __half lv[kSampPerThread];
+#pragma unroll
+    for (int k = 0; k < kSampPerThread; ++k) {
+      const int i = k * kSampThreads + (int)threadIdx.x;
+      lv[k] = i < n_local ? lg[lo + i] : __ushort_as_half((unsigned short)0x7e00u);
+    }
+#pragma unroll
     for (int k = 0; k < kSampPerThread; ++k) {
       const int i = k * kSampThreads + (int)threadIdx.x;
       if (i < n_local) {
-        const float v = h2f(lg[lo + i]);
+        const float v = h2f(lv[k]);
         float x = 0.0f;
         if (!isnan(v)) {
           x = __fdiv_rn(v, temperature);
