@@ -6,25 +6,28 @@
 //   s_t = 0.088388 * q_h . K_t,   p_t = exp(s_t - max) / sum,   o_h = sum_t p_t V_t
 // evaluated as an online softmax over position chunks.
 //
-// Persistent grid (one CTA per SM) over work units = (sequence, split): a
-// split is a run of 64-position tiles of one sequence, covering both kv heads.
-//   warp 8      producer: per tile, one lane issues 8 TMA tile loads from 2-D
+// Persistent grid (one CTA per SM) over work units = (sequence, kv head,
+// split): a split is a run of 128-position tiles of one sequence and one kv
+// head (query heads 6h .. 6h+5).  The batch's sequences times the two kv heads
+// usually fill the machine with one split each, and a unit then holds a whole
+// head: no merge across CTAs.
+//   warp 8      producer: per tile, one lane issues 4 TMA tile loads from 2-D
 //               tensor maps over the K and V caches (rows = positions, 256
-//               fp16 per row): boxes of 64 positions x 64 elements with the
-//               128-byte swizzle, so the K fragment loads and the V
-//               ldmatrix.trans reads hit distinct banks; a 3-stage ring
-//               (192 KB in flight per SM);
+//               fp16 per row): the unit's head's two 64-element halves, boxes
+//               of 128 positions x 64 elements with the 128-byte swizzle, so
+//               the K fragment loads and the V ldmatrix.trans reads hit
+//               distinct banks; a 3-stage ring (192 KB in flight per SM);
 //               the ring runs on across units, so loads of the next unit
 //               overlap the merge of this one
-//   warps 0..7  warp w serves kv head w/4 (query heads 6h..6h+5) on positions
-//               16(w%4) .. +16 of every tile:
+//   warps 0..7  warp w takes positions 16w .. 16w+15 of every tile:
 //                 S^T[16 pos x 8 heads] = K[16 x 128] . q^T   (8 m16n8k16 MMAs)
 //                 o^T[128 x 8]        += V^T[128 x 16] . P^T  (V by
 //                     ldmatrix.trans; P split into fp16 hi + lo parts so the
 //                     product keeps ~22 bits)
-// The 4 warps of a head merge in shared memory; splits merge in a fixed order
-// by the last CTA of the sequence to finish (an atomic ticket -- nothing
-// waits), so results do not depend on scheduling.  Waits are bounded (2 s).
+// The 8 warps merge in shared memory; where a head has several splits they
+// merge in a fixed order by the last CTA of the (sequence, head) to finish (an
+// atomic ticket -- nothing waits), so results do not depend on scheduling.
+// Waits are bounded (2 s).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -37,13 +40,14 @@ namespace qwen {
 
 namespace {
 
-constexpr int kTilePos = 64;                        // positions per ring stage
+constexpr int kTilePos = 128;                       // positions per ring stage
 constexpr int kSub = 16;                            // positions per warp sub-tile
 constexpr int kConsumerWarps = 8;
 constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = 3;
-constexpr int kBoxBytes = kTilePos * 128;          // 64 positions x 64 fp16, swizzled
-constexpr int kBoxes = 4;                           // 256 fp16 per position: 2 heads x 2
+constexpr int kBoxBytes = kTilePos * 128;          // 128 positions x 64 fp16, swizzled
+constexpr int kBoxes = 2;                           // the unit's head: 2 x 64 fp16 per position
+static_assert(kConsumerWarps * kSub == kTilePos, "a tile is one sub-tile per consumer warp");
 constexpr int kMaxSplits = 32;                      // bounds the merge of a sequence
 constexpr int kUnitsPerSm = 1;                      // work units per SM to aim for (each costs a merge)
 constexpr unsigned long long kAttnWaitNs = 2000000000ull;
@@ -122,20 +126,21 @@ __device__ __forceinline__ void store_out(const AttnParams& p, int seq, int col,
 }
 
 struct Unit {
-  int seq, split;
+  int seq, kvh, split;
   uint32_t p0, p1, s_eff;
 };
 
-// q (qs, 12 heads x 128) and the step's new k | v rows (kvn: k of kv heads 0,
-// 1, then v) of sequence `seq` from the QKV partials, as the batched QKV
-// finish forms them: sum of the splits in split order, + bias, rounded to fp16,
-// RoPE on the 14 q / k heads at position pos (rope.metal:12-39), the v rows
-// rounded after the bias.  256 consumer threads: RoPE pairs ctid + 256 j
-// (head = pair / 64), v element ctid; every split's loads issued together.
-__device__ __forceinline__ void form_qkv(const AttnParams& p, int seq, uint32_t pos, __half* qs,
-                                         __half* kvn, int ctid) {
-  constexpr int kPairs = (kHeads + kKVHeads) * 64;   // 896
-  constexpr int kJobs = (kPairs + 255) / 256;          // 4
+// q of the unit's six query heads (qs, 6 x 128) and the step's new k | v rows
+// of its kv head (kvn: 128 k, then 128 v) of sequence `seq` from the QKV
+// partials, as the batched QKV finish forms them: sum of the splits in split
+// order, + bias, rounded to fp16, RoPE on the q / k heads at position pos
+// (rope.metal:12-39), the v row rounded after the bias.  256 consumer threads:
+// RoPE pairs ctid and ctid + 256 (pairs 0..383 the q heads, 384..447 the k
+// head), v element ctid < 128; every split's loads issued together.
+__device__ __forceinline__ void form_qkv(const AttnParams& p, int seq, int kvh, uint32_t pos,
+                                         __half* qs, __half* kvn, int ctid) {
+  constexpr int kQPairs = 6 * 64, kPairs = kQPairs + 64;   // 448
+  constexpr int kJobs = (kPairs + 255) / 256;               // 2
   const size_t stride = (size_t)p.qkv_rows * kQKVRows;
   const float* part = p.qkv_part + (size_t)seq * kQKVRows;
   const float* cs = p.rope_cs + (size_t)pos * 128;
@@ -147,13 +152,14 @@ __device__ __forceinline__ void form_qkv(const AttnParams& p, int seq, uint32_t 
   for (int j = 0; j < kJobs; ++j) {   // biases and RoPE factors loaded with the partials
     const int pr = ctid + 256 * j;
     const int pc = pr < kPairs ? pr : 0;
-    i1[j] = (pc >> 6) * 128 + (pc & 63);
+    i1[j] = pc < kQPairs ? (6 * kvh + (pc >> 6)) * 128 + (pc & 63)
+                         : kHidden + kvh * 128 + (pc - kQPairs);
     s1[j] = s2[j] = 0.f;
     b1[j] = p.qkv_bias[i1[j]];
     b2[j] = p.qkv_bias[i1[j] + 64];
     rot[j] = reinterpret_cast<const float2*>(cs)[pc & 63];
   }
-  const int iv = kHidden + kKVDim + ctid;   // v element (ctid < 256)
+  const int iv = kHidden + kKVDim + kvh * 128 + (ctid & 127);   // v element (ctid < 128)
   const __half bvh = p.qkv_bias[iv];
   float sv = 0.f;
 #pragma unroll 4
@@ -177,22 +183,23 @@ __device__ __forceinline__ void form_qkv(const AttnParams& p, int seq, uint32_t 
   for (int j = 0; j < kJobs; ++j) {
     const int pr = ctid + 256 * j;
     if (pr >= kPairs) break;
-    const int head = pr >> 6, i0 = i1[j];
     const float x1 = h2f(f2h(s1[j] + h2f(b1[j])));
     const float x2 = h2f(f2h(s2[j] + h2f(b2[j])));
     const float c = rot[j].x, sn = rot[j].y;
     const __half r1 = f2h(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
     const __half r2 = f2h(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, c)));
-    __half* dst = head < kHeads ? qs + i0 : kvn + (i0 - kHidden);
+    __half* dst = pr < kQPairs ? qs + (pr >> 6) * 128 + (pr & 63) : kvn + (pr - kQPairs);
     dst[0] = r1;
     dst[64] = r2;
   }
-  kvn[kKVDim + ctid] = f2h(sv + h2f(bvh));
+  if (ctid < 128) kvn[128 + ctid] = f2h(sv + h2f(bvh));
 }
-// Unit u = (sequence u / max_s, split u % max_s): n_tiles = ceil(L/64) tiles
-// in S = min(max_s, n_tiles) near-equal runs; false if the split is empty.
+// Unit u = (sequence u / (2 max_s), kv head (u / max_s) % 2, split u % max_s):
+// n_tiles = ceil(L/128) tiles in S = min(max_s, n_tiles) near-equal runs;
+// false if the split is empty.
 __device__ __forceinline__ bool unit_of(const AttnParams& p, int u, int max_s, Unit& w) {
-  w.seq = u / max_s;
+  w.seq = u / (2 * max_s);
+  w.kvh = (u / max_s) & 1;
   w.split = u % max_s;
   const uint32_t L = p.seq_len[(size_t)w.seq * p.seq_len_stride];
   if (L == 0 || L > p.max_ctx) return false;
@@ -244,9 +251,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             continue;  // aborting: keep the tile count, issue nothing
           mbar_arrive_expect_tx(&s.full[st], 2 * kBoxes * kBoxBytes);
 #pragma unroll
-          for (int b = 0; b < kBoxes; ++b) {
-            tma_load_2d(s.k[st][b], &tmk, 64 * b, row0 + (int)base, &s.full[st]);
-            tma_load_2d(s.v[st][b], &tmv, 64 * b, row0 + (int)base, &s.full[st]);
+          for (int b = 0; b < kBoxes; ++b) {   // the unit's head: elements 128 kvh + 64 b ..
+            tma_load_2d(s.k[st][b], &tmk, kHeadDim * w.kvh + 64 * b, row0 + (int)base, &s.full[st]);
+            tma_load_2d(s.v[st][b], &tmv, kHeadDim * w.kvh + 64 * b, row0 + (int)base, &s.full[st]);
           }
         }
       }
@@ -259,20 +266,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 
   // -------------------------------------------------------------- consumers --
-  const int h = warp >> 2, slice = warp & 3;     // kv head, 16-row slice of a tile
+  const int slice = warp;                        // 16-row slice of a tile
   const int g = lane >> 2, t = lane & 3;
   const int ctid = threadIdx.x;                  // 0..255
-  const int htid = ctid & 127;                   // thread within the head group
   uint32_t it = 0;
   for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
     Unit w;
     if (!unit_of(p, u, max_s, w)) {
-      if (ctid == 0 && u % max_s == 0) {
-        const uint32_t L = p.seq_len[(size_t)(u / max_s) * p.seq_len_stride];
+      if (ctid == 0 && u % (2 * max_s) == 0) {
+        const uint32_t L = p.seq_len[(size_t)(u / (2 * max_s)) * p.seq_len_stride];
         if (L == 0 || L > p.max_ctx) raise_error(p.err, kDevBadArgument);
       }
       continue;
     }
+    const int h = w.kvh;
     // q (and in a decode step's fused mode the new k / v rows) in shared
     // memory of the merge: q in wo (read into registers before the first tile;
     // the merge writes wo after the last), the rows in sc (used by the last
@@ -280,19 +287,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t pos = p.seq_len[(size_t)w.seq * p.seq_len_stride] - 1;
     __half* qs = reinterpret_cast<__half*>(&s.wo[0][0][0]);
     __half* kvn = reinterpret_cast<__half*>(&s.sc[0][0][0]);
-    static_assert(sizeof(s.sc) >= 2 * kKVDim * sizeof(__half), "new k / v rows exceed sc");
-    static_assert(sizeof(s.wo) >= kHidden * sizeof(__half), "q exceeds wo");
+    static_assert(sizeof(s.sc) >= 2 * kHeadDim * sizeof(__half), "new k / v rows exceed sc");
+    static_assert(sizeof(s.wo) >= 6 * kHeadDim * sizeof(__half), "q exceeds wo");
     const bool fused_qkv = p.qkv_part != nullptr;
     const bool owns_pos = fused_qkv && pos >= w.p0 && pos < w.p1;
     if (fused_qkv) {
-      form_qkv(p, w.seq, pos, qs, kvn, ctid);
+      form_qkv(p, w.seq, h, pos, qs, kvn, ctid);
       consumers_sync();
-      if (owns_pos && ctid < 64) {
-        // the new rows into the caches, for the steps after this one
+      if (owns_pos && ctid < 32) {
+        // this head's new rows into the caches, for the steps after this one
         const int kvs = p.row_seq ? p.row_seq[w.seq] : w.seq;
-        const size_t off = (size_t)kvs * p.kv_seq_stride + (size_t)pos * p.kv_pos_stride;
-        __half* dst = const_cast<__half*>(ctid < 32 ? p.k : p.v) + off;
-        reinterpret_cast<uint4*>(dst)[ctid & 31] = reinterpret_cast<const uint4*>(kvn)[ctid];
+        const size_t off = (size_t)kvs * p.kv_seq_stride + (size_t)pos * p.kv_pos_stride +
+                           (size_t)h * p.kv_head_stride;
+        __half* dst = const_cast<__half*>(ctid < 16 ? p.k : p.v) + off;
+        reinterpret_cast<uint4*>(dst)[ctid & 15] = reinterpret_cast<const uint4*>(kvn)[ctid];
       }
     }
     // q fragments: lane (g,t) holds q[head 6h + g][32t .. 32t+31] (zero for g >= 6).
@@ -300,7 +308,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     {
       const bool hv = g < 6;
       const uint4* qp = reinterpret_cast<const uint4*>(
-          (fused_qkv ? qs : p.q + (size_t)w.seq * p.q_seq_stride) + (size_t)(6 * h + (hv ? g : 0)) * kHeadDim +
+          (fused_qkv ? qs + (size_t)(hv ? g : 0) * kHeadDim
+                     : p.q + (size_t)w.seq * p.q_seq_stride + (size_t)(6 * h + (hv ? g : 0)) * kHeadDim) +
           32 * t);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -329,9 +338,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // (the cache may not hold them yet): lane -> (k|v, 64-element box,
         // 16-byte chunk), swizzled as the tensor map lays the box out.
         const int r = (int)(pos - tb), kv = lane >> 4, half = (lane >> 3) & 1, ch = lane & 7;
-        uint8_t* box = kv ? s.v[st][2 * h + half] : s.k[st][2 * h + half];
+        uint8_t* box = kv ? s.v[st][half] : s.k[st][half];
         *reinterpret_cast<uint4*>(box + swz(r, ch)) =
-            *reinterpret_cast<const uint4*>(kvn + kv * kKVDim + h * kHeadDim + half * 64 + ch * 8);
+            *reinterpret_cast<const uint4*>(kvn + kv * kHeadDim + half * 64 + ch * 8);
         zeroed = true;   // generic stores into the stage: proxy fence before its release
         __syncwarp();
       }
@@ -340,8 +349,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         float sv[4] = {0.f, 0.f, 0.f, 0.f};
         {
           uint32_t kg[16], kg8[16];
-          // d = 32t + 8j: box 2h + t/2, chunk 4(t&1) + j of rows r0+g, r0+g+8.
-          const uint8_t* kbox = s.k[st][2 * h + (t >> 1)];
+          // d = 32t + 8j: box t/2, chunk 4(t&1) + j of rows r0+g, r0+g+8.
+          const uint8_t* kbox = s.k[st][t >> 1];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint4 a = *reinterpret_cast<const uint4*>(kbox + swz(r0 + g, 4 * (t & 1) + j));
@@ -405,7 +414,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (base + 16 > w.p1) {
           for (int r = (int)(w.p1 - base); r < 16; ++r)
             if (lane < 16)  // both boxes of this head, whole 128-byte rows
-              *reinterpret_cast<uint4*>(s.v[st][2 * h + (lane >> 3)] + (r0 + r) * 128 +
+              *reinterpret_cast<uint4*>(s.v[st][lane >> 3] + (r0 + r) * 128 +
                                         (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
           zeroed = true;
         }
@@ -431,7 +440,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 8; ++i) {
             // d = 16i + dcol: box 2h + i/4, chunk 2(i&3) + dcol/8.
             uint32_t a[4];
-            ldmatrix_x4_trans(a, s.v[st][2 * h + (i >> 2)] + swz(r0 + prow, 2 * (i & 3) + (dcol >> 3)));
+            ldmatrix_x4_trans(a, s.v[st][i >> 2] + swz(r0 + prow, 2 * (i & 3) + (dcol >> 3)));
             mma_16816(o[i], a, bh0, bh1, o[i]);
             mma_16816(o[i], a, bl0, bl1, o[i]);
           }
@@ -444,7 +453,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
 
-    // ---- merge the 4 warps of each head group.  o[i][0]: (d 16i+g, head 2t)
+    // ---- merge the 8 warps (all on the unit's head group).  o[i][0]: (d 16i+g, head 2t)
     // o[i][1]: (d 16i+g, head 2t+1) o[i][2]: (d 16i+g+8, head 2t) o[i][3]: (d 16i+g+8, head 2t+1)
     if (g == 0) {
       s.wm[warp][2 * t] = m_run[0];
@@ -464,22 +473,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (ctid == 0) s.unit_abort = *((volatile int*)&s.abort);
     consumers_sync();
     const bool aborting = s.unit_abort != 0;
+    // partials of split (seq, split) of head group h at [seq][split][h]
     const size_t pidx = ((size_t)w.seq * max_s + w.split) * 2 + h;
     float* part_o = p.part_o + pidx * (6 * kHeadDim);
     float* part_ml = p.part_ml + pidx * 12;
-    for (int idx = htid; idx < 6 * kHeadDim && !aborting; idx += 128) {
+    for (int idx = ctid; idx < 6 * kHeadDim && !aborting; idx += 256) {
       const int head = idx / kHeadDim, d = idx % kHeadDim;
       float M = -INFINITY;
 #pragma unroll
-      for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, s.wm[4 * h + ww][head]);
+      for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, s.wm[ww][head]);
       float Lsum = 0.f, O = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < 4; ++ww) {
-        const float m = s.wm[4 * h + ww][head];
+      for (int ww = 0; ww < kConsumerWarps; ++ww) {
+        const float m = s.wm[ww][head];
         if (m == -INFINITY) continue;
         const float c = expf(m - M);
-        Lsum += s.wl[4 * h + ww][head] * c;
-        O += s.wo[4 * h + ww][head][d] * c;
+        Lsum += s.wl[ww][head] * c;
+        O += s.wo[ww][head][d] * c;
       }
       if (w.s_eff == 1) {
         store_out(p, w.seq, (6 * h + head) * kHeadDim + d, O / Lsum);
@@ -492,17 +502,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     if (w.s_eff > 1 && !aborting) {
-      // ---- ticket: the last CTA of this sequence merges its splits in order.
+      // ---- ticket: the last CTA of this (sequence, head) merges its splits
+      // in order.
       __threadfence();
       consumers_sync();
-      if (ctid == 0) s.ticket = atomicAdd(&p.counters[w.seq], 1u);
+      if (ctid == 0) s.ticket = atomicAdd(&p.counters[w.seq * 2 + h], 1u);
       consumers_sync();
       if (s.ticket == w.s_eff - 1) {
         __threadfence();
         const float* all_ml = p.part_ml + (size_t)w.seq * max_s * 2 * 12;
         const float* all_o = p.part_o + (size_t)w.seq * max_s * 2 * (6 * kHeadDim);
-        if (warp < 2) {  // warp hg: head group hg, lane = split
-          const int hg = warp;
+        if (warp == 0) {  // lane = split
+          const int hg = h;
           const bool have = (uint32_t)lane < w.s_eff;
           // the split's 6 (m, l) pairs in one go (48 bytes, 16-byte aligned)
           float ml[12];
@@ -524,7 +535,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
             const float c = m == -INFINITY ? 0.f : expf(m - M);
-            s.sc[hg][lane][head] = c;
+            s.sc[0][lane][head] = c;
             // fixed-order tree sum over splits (lane order) for determinism
             float L = l * c;
 #pragma unroll
@@ -532,52 +543,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               const float o2 = __shfl_down_sync(0xffffffffu, L, off);
               if ((lane & (2 * off - 1)) == 0) L += o2;
             }
-            if (lane == 0) s.hsum[hg][head] = L;
+            if (lane == 0) s.hsum[0][head] = L;
           }
         }
         consumers_sync();
         {
-          // The thread's six outputs (idx = ctid + 256 j), summed over the
-          // splits in split order; each split's six partials are loaded
-          // together, so the merge waits one L2 round trip per split rather
-          // than one per output.
-          constexpr int kPer = 2 * 6 * kHeadDim / 256;
-          static_assert(kPer * 256 == 2 * 6 * kHeadDim, "merge outputs per thread");
+          // The thread's three outputs (idx = ctid + 256 j), summed over the
+          // splits in split order; each split's partials are loaded together,
+          // so the merge waits one L2 round trip per split rather than one per
+          // output.
+          constexpr int kPer = 6 * kHeadDim / 256;
+          static_assert(kPer * 256 == 6 * kHeadDim, "merge outputs per thread");
           float O[kPer];
-          int hgj[kPer], rj[kPer];
 #pragma unroll
-          for (int j = 0; j < kPer; ++j) {
-            const int idx = ctid + 256 * j;
-            hgj[j] = idx / (6 * kHeadDim);
-            rj[j] = idx % (6 * kHeadDim);
-            O[j] = 0.f;
-          }
+          for (int j = 0; j < kPer; ++j) O[j] = 0.f;
 #pragma unroll 2
           for (uint32_t sp = 0; sp < w.s_eff; ++sp) {
             float v[kPer];
 #pragma unroll
             for (int j = 0; j < kPer; ++j)
-              v[j] = __ldcg(all_o + ((size_t)sp * 2 + hgj[j]) * (6 * kHeadDim) + rj[j]);
+              v[j] = __ldcg(all_o + ((size_t)sp * 2 + h) * (6 * kHeadDim) + ctid + 256 * j);
 #pragma unroll
-            for (int j = 0; j < kPer; ++j) O[j] += v[j] * s.sc[hgj[j]][sp][rj[j] / kHeadDim];
+            for (int j = 0; j < kPer; ++j) O[j] += v[j] * s.sc[0][sp][(ctid + 256 * j) / kHeadDim];
           }
 #pragma unroll
-          for (int j = 0; j < kPer; ++j)
-            store_out(p, w.seq, (6 * hgj[j]) * kHeadDim + rj[j],
-                      O[j] / s.hsum[hgj[j]][rj[j] / kHeadDim]);
+          for (int j = 0; j < kPer; ++j) {
+            const int r = ctid + 256 * j;
+            store_out(p, w.seq, 6 * h * kHeadDim + r, O[j] / s.hsum[0][r / kHeadDim]);
+          }
         }
-        if (ctid == 0) p.counters[w.seq] = 0;  // re-arm for the next launch
+        if (ctid == 0) p.counters[w.seq * 2 + h] = 0;  // re-arm for the next launch
       }
     }
     consumers_sync();  // wo / wm / sc are reused by the next unit
   }
 }
 
-// Splits per sequence for a launch: ~1 work unit per SM over the batch, at
-// most one per 64-position tile, at most 32 (the merge reads them all).
+// Splits per (sequence, kv head) for a launch: ~1 work unit per SM over the
+// batch's 2 n_seq heads, at most one per 128-position tile, at most 32 (the
+// merge reads them all).
 int attn_max_splits(int max_ctx, int n_seq) {
   const int tiles = (max_ctx + kTilePos - 1) / kTilePos;
-  int target = (148 * kUnitsPerSm) / (n_seq > 0 ? n_seq : 1);
+  int target = (148 * kUnitsPerSm) / (2 * (n_seq > 0 ? n_seq : 1));   // units per (sequence, kv head)
   if (target < 1) target = 1;
   const int s = tiles < target ? tiles : target;
   return s < kMaxSplits ? s : kMaxSplits;
@@ -618,7 +625,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// rows x 256 fp16 (512-byte rows), boxes of 64 rows x 64 elements, 128-byte
+// rows x 256 fp16 (512-byte rows), boxes of 128 rows x 64 elements, 128-byte
 // swizzle, zero fill past the last row.
 bool encode_kv_map(CUtensorMap* map, const __half* base, uint64_t rows) {
   auto enc = tensor_map_encoder();
@@ -650,7 +657,7 @@ int launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cuda
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return -1;
-  const int n_units = n_seq * max_splits;
+  const int n_units = n_seq * kKVHeads * max_splits;
   const size_t smem = sizeof(AttnSmem) + 1024;
   if (cudaFuncSetAttribute(k_attention_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)

@@ -35,8 +35,9 @@ def test_noalloc_matches_allocating_entry_point(cuda):
     L.qwen_ops_status.argtypes = [ctypes.c_void_p]
     rng = np.random.default_rng(99)
     # calls in a row that each reuse the array the one before left behind, with
-    # different lengths and split counts: 13 of 16, 1, 32 of 32 (the split count
-    # that sizes the array, max_ctx >= 2048), then 16 of 32 and 1 of 1 again
+    # different lengths and split counts per kv head (128-position tiles): 7 of
+    # 8, 1, 32 of 32 (the split count that sizes the array, max_ctx >= 4096),
+    # then 8 of 32 and 1 of 1 again
     for L_ctx, max_ctx in ((777, 1024), (40, 1024), (4000, 4096), (1000, 4096), (50, 64)):
         q = torch.from_numpy(rng.standard_normal(1536).astype(np.float16)).cuda()
         kc = torch.from_numpy(rng.standard_normal((max_ctx, 256)).astype(np.float16)).cuda()
