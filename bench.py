@@ -691,7 +691,7 @@ def run_ours(args):
                          "algorithmic_bytes": algo,
                          "ms_model": ms_model, "ms_step_unfused_launch": ms_step_prof},
             "e2e": {"value": world * n_e2e / (e2e_ms * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": 4 + 4,
+                    "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 8,
                     "steps": n_e2e, "api": "QwenEngine.forward(token, position)"},
             "clocks": clk.summary(),
             "gpu_launches": launches,

@@ -284,9 +284,12 @@ int InferenceManager::allocate(int b, int nl, int mc, int mo) {
   QWEN_TRY(alloc(B * sizeof(SeqCtl), (void**)&ctl));
   QWEN_TRY(alloc(B * mc * sizeof(int32_t), (void**)&prompt));
   QWEN_TRY(alloc(B * mo * sizeof(int32_t), (void**)&out_tokens));
-  QWEN_TRY(alloc(B * sizeof(int32_t), (void**)&sampled));
+  // sampled[B] and the error words in one allocation, the error words right
+  // after the ids: a batch-1 forward() reads the id and error word 0 back in
+  // one 8-byte copy
+  QWEN_TRY(alloc(B * sizeof(int32_t) + sizeof(int) * 32, (void**)&sampled));
+  err = reinterpret_cast<int*>(sampled + B);
   QWEN_TRY(alloc(B * sizeof(uint32_t) + 64, (void**)&u24_));
-  QWEN_TRY(alloc(sizeof(int) * 32, (void**)&err));
   QWEN_TRY(alloc(sizeof(uint32_t) * 4, (void**)&epoch));
   attn_splits = attn_max_splits(mc, b);
   QWEN_TRY(alloc(attn_scratch_bytes(attn_splits, b), &attn_scratch));
@@ -540,20 +543,22 @@ int QwenEngine::forward(int32_t token, int32_t position, int32_t* next) {
                      state_.max_ctx);
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_TRY(ensure_graph());
-  // One step that reads `token` as a prompt token at `position`; positions
-  // past max_ctx-1 reuse the last slot, as InferenceEngine.swift:55 clamps.
-  // Inputs and the result travel through pinned host staging.
+  // One step that reads `token` at `position` (as the step's last token, past
+  // the prompt); positions past max_ctx-1 reuse the last slot, as
+  // InferenceEngine.swift:55 clamps.  One copy in (the sequence's control
+  // block, token included) and one out (the id and error word 0, adjacent).
   HostStaging* hs = pinned_;
   std::memset(&hs->ctl, 0, sizeof(hs->ctl));
   hs->ctl.pos = position;
-  hs->ctl.n_prompt = position + 1;
-  hs->token = token;
-  const int slot = std::min(position, state_.max_ctx - 1);
-  QWEN_CUDA(cudaMemcpyAsync(state_.prompt + slot, &hs->token, 4, cudaMemcpyHostToDevice, stream_), "memcpy");
+  hs->ctl.n_prompt = position;
+  hs->ctl.last_token = token;
   QWEN_CUDA(cudaMemcpyAsync(state_.ctl, &hs->ctl, sizeof(SeqCtl), cudaMemcpyHostToDevice, stream_), "memcpy");
   QWEN_TRY(run_steps(1));
-  QWEN_CUDA(cudaMemcpyAsync(&hs->result, state_.sampled, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
-  QWEN_CUDA(cudaMemcpyAsync(&hs->err, state_.err, 4, cudaMemcpyDeviceToHost, stream_), "memcpy");
+  static_assert(offsetof(HostStaging, err) == offsetof(HostStaging, result) + sizeof(int32_t),
+                "the id and the error word are read back together");
+  QWEN_CUDA(cudaMemcpyAsync(&hs->result, state_.sampled, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                            stream_),
+            "memcpy");
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
   if (hs->err != 0) return check_device_error();
   *next = hs->result;
