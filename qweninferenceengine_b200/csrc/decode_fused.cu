@@ -716,6 +716,9 @@ __device__ __noinline__ void issue_item(int i, const FusedItem* items, const Fus
 }  // namespace
 
 // 256 threads = 8 warps, 2 per SM sub-partition: up to 255 registers a thread.
+// kTrace: the phase trace's stamps are compiled in (a launch with
+// FusedParams::trace set); without it the step carries none of their code.
+template <bool kTrace>
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
@@ -753,7 +756,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(FusedParams p
   }
   __syncthreads();
 
-  unsigned long long* trace_out = p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
+  unsigned long long* trace_out =
+      kTrace && p.trace ? p.trace + (size_t)blockIdx.x * p.trace_stride : nullptr;
   unsigned long long* trace =
       trace_out ? reinterpret_cast<unsigned long long*>(smem + kOffTrace) : nullptr;
   if (trace)
@@ -1238,15 +1242,15 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
   p.kv_layer_stride = (int)s.kv_layer_stride();
   p.wait_ns = a.wait_ns;
   p.stall_site = a.stall_site;
-  if (int rc = cuda_status(cudaFuncSetAttribute(k_decode_fused,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+  void (*kern)(FusedParams) = p.trace ? k_decode_fused<true> : k_decode_fused<false>;
+  if (int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 kSmemBytes),
                            "cudaFuncSetAttribute(k_decode_fused)"))
     return rc;
-  cudaFuncSetAttribute(k_decode_fused, cudaFuncAttributePreferredSharedMemoryCarveout,
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                        (int)cudaSharedmemCarveoutMaxShared);
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_fused, kFusedThreads, kSmemBytes);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFusedThreads, kSmemBytes);
   if (per_sm < 1) {
     int dev = 0, smem_sm = 0, smem_optin = 0, smem_rsv = 0;
     cudaGetDevice(&dev);
@@ -1254,7 +1258,7 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
     cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&smem_rsv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
     cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, k_decode_fused);
+    cudaFuncGetAttributes(&fa, kern);
     return set_error(QWEN_ERR_CUDA,
                      "k_decode_fused does not fit on an SM (%d B dynamic + %zu B static shared memory, "
                      "%d threads x %d registers; SM: %d B shared, %d B per block opt-in, %d B reserved)",
@@ -1271,7 +1275,7 @@ int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, k_decode_fused, p), "launch k_decode_fused");
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, p), "launch k_decode_fused");
 }
 
 }  // namespace qwen
