@@ -48,7 +48,7 @@ def headline_config(world: int) -> dict:
 # 1.004 x the algorithmic bytes there).  Weights and LM head are read once per
 # launch, so the traffic at another context adds the KV bytes of the extra
 # positions.
-FUSED_TRAFFIC_CTX8 = 1_210_368_256
+FUSED_TRAFFIC_CTX8 = 1_209_005_312
 
 
 def fused_traffic(ctx: float) -> float:
