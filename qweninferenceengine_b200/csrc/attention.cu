@@ -215,6 +215,10 @@ __device__ __forceinline__ bool unit_of(const AttnParams& p, int u, int max_s, U
 
 }  // namespace
 
+// kFusedQkv: q and the new k / v rows formed from the QKV partials
+// (AttnParams::qkv_part set, the batched decode step); each launch runs the
+// instantiation of its mode, without the other's code.
+template <bool kFusedQkv>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     k_attention_decode(AttnParams p, int max_s, int n_units, int rows_per_seq,
                        const __grid_constant__ CUtensorMap tmk,
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __half* kvn = reinterpret_cast<__half*>(&s.sc[0][0][0]);
     static_assert(sizeof(s.sc) >= 2 * kHeadDim * sizeof(__half), "new k / v rows exceed sc");
     static_assert(sizeof(s.wo) >= 6 * kHeadDim * sizeof(__half), "q exceeds wo");
-    const bool fused_qkv = p.qkv_part != nullptr;
+    constexpr bool fused_qkv = kFusedQkv;
     const bool owns_pos = fused_qkv && pos >= w.p0 && pos < w.p1;
     if (fused_qkv) {
       form_qkv(p, w.seq, h, pos, qs, kvn, ctid);
@@ -659,7 +663,9 @@ int launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cuda
     return -1;
   const int n_units = n_seq * kKVHeads * max_splits;
   const size_t smem = sizeof(AttnSmem) + 1024;
-  if (cudaFuncSetAttribute(k_attention_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  void (*kern)(AttnParams, int, int, int, const CUtensorMap, const CUtensorMap) =
+      p.qkv_part ? k_attention_decode<true> : k_attention_decode<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
     return -1;
   cudaLaunchConfig_t cfg = {};
@@ -672,7 +678,7 @@ int launch_attention_decode(const AttnParams& p, int max_splits, int n_seq, cuda
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_attention_decode, p, max_splits, n_units, rows_per_seq, tmk,
+  return cudaLaunchKernelEx(&cfg, kern, p, max_splits, n_units, rows_per_seq, tmk,
                             tmv) == cudaSuccess
              ? 0
              : -1;
