@@ -66,19 +66,25 @@ struct SampShared {
   static constexpr int kC = C;
   static constexpr int kChunk = (kVocab + C - 1) / C;                           // 37984 / 18992 / 9496
   static constexpr int kPerThread = (kChunk + kSampThreads - 1) / kSampThreads;  // 38 / 19 / 10
-  // One digit histogram per warp, or per pair of warps when the CTA's weights
-  // take most of shared memory (C = 4).
-  static constexpr int kHist = C >= 8 ? kSampWarps : kSampWarps / 2;
+  // With 8 or 16 CTAs the draw select runs beside the cutoff select: a pass
+  // then histograms both member sets (disjoint once the draw's prefix has left
+  // the cutoff's), the draw's in bins 256..511.  With 4 the weights take most
+  // of shared memory and the draw runs after the cutoff.
+  static constexpr bool kSpec = C >= 8;
+  static constexpr int kBins = kSpec ? 512 : 256;
+  // One digit histogram per pair of warps.
+  static constexpr int kHist = kSampWarps / 2;
   static constexpr int kWarpsPerHist = kSampWarps / kHist;
   uint32_t e[kChunk];                        // scaled floats, then fixed-point weights
   // Digit weights of the running pass as two exact halves (E & 0xFFFF, E >> 16):
   // a histogram sees at most 2 * 38 * 32 elements, so each half fits 32 bits.
-  uint32_t whist[kHist][2][256];
-  unsigned long long qsum[4][256];           // quarter-block merges of whist
-  unsigned long long inbox[2][C][256];       // each rank's digit weights, pushed by that rank
-  uint64_t xbar[2];                          // inbox barriers (transaction bytes)
-  unsigned long long tot[256];               // cluster totals of the running pass
-  unsigned long long tot1[4][256];           // the nucleus select's totals per pass
+  uint32_t whist[kHist][2][kBins];
+  unsigned long long qsum[kSampThreads];     // partial merges of whist, [groups][bins]
+  alignas(16) unsigned long long send[kBins];  // this rank's digit weights, copied to every rank
+  alignas(16) unsigned long long inbox[C][kBins];  // each rank's digit weights of the last exchange
+  uint64_t xbar;                             // inbox barrier (transaction bytes)
+  unsigned long long tot[kBins];             // cluster totals of the running pass
+  unsigned long long tot1[4][256];           // the cutoff select's totals per pass
   unsigned long long above1[4];              // its weight above the prefix after each pass
   float red_f[32];
   int red_i[32];
@@ -86,9 +92,13 @@ struct SampShared {
   uint32_t red_c[32];
   float cl_f[C];                             // per-CTA partials read by the cluster
   int cl_i;
-  uint32_t cl_cnt;
   uint32_t sel;
   unsigned long long sel_above;
+  // select state, written by warp 0 after each pass
+  unsigned long long thr, an, ad, R;         // cutoff target, weight above the cutoff / draw prefix
+  uint32_t pn, pd;                           // cutoff and draw prefixes
+  int dmode, dfail, don, dhi;                // draw mode, pass it left the speculation, on e_star
+                                             // then, its pass-3 weights in bins 256..511
 };
 
 static_assert(sizeof(SampShared<4>) <= 232448, "4-CTA sampler layout exceeds shared memory");
@@ -134,20 +144,14 @@ __device__ __forceinline__ uint32_t block_incl_scan_u32(uint32_t v, SS& s) {
 // halves), sums the histograms over the cluster, and picks the digit at which
 // the running weight from the top first reaches the target.
 
-// Zeroes the digit histograms: each warp its own, or the whole block (and a
-// block barrier) when warps share them.
+// Zeroes bins [0, nb) of the digit histograms (warps share them: block barrier).
 template <class SS>
-__device__ __forceinline__ void hist_clear(SS& s) {
-  if constexpr (SS::kWarpsPerHist == 1) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-#pragma unroll
-    for (int d = lane; d < 256; d += 32) s.whist[wid][0][d] = s.whist[wid][1][d] = 0;
-    __syncwarp();
-  } else {
-    uint32_t* h = &s.whist[0][0][0];
-    for (int i = threadIdx.x; i < SS::kHist * 512; i += kSampThreads) h[i] = 0;
-    __syncthreads();
-  }
+__device__ __forceinline__ void hist_clear(SS& s, int nb) {
+  const int lg = nb == 512 ? 9 : 8;
+  uint32_t* h = &s.whist[0][0][0];
+  for (int i = threadIdx.x; i < SS::kHist * 2 * nb; i += kSampThreads)
+    h[(i >> lg) * SS::kBins + (i & (nb - 1))] = 0;
+  __syncthreads();
 }
 
 // Adds weight e at digit d to this warp's histogram for each lane that is a
@@ -198,45 +202,59 @@ __device__ __forceinline__ void hist_add(SS& s, bool member, uint32_t e, uint32_
   }
 }
 
-// Cluster totals of exchange n into s.tot.  Every CTA merges its warp
-// histograms and pushes the 256 sums into inbox[n & 1][its rank] of every CTA
-// of the cluster (itself included) with st.async, which completes transaction
-// bytes on the receiver's xbar[n & 1]; each CTA then waits for the C ranks'
-// bytes and sums them in rank order (so every CTA holds the same totals).
-// A CTA pushes exchange n + 2 only after it has received exchange n + 1 from
-// every rank, which each rank sends after it has read its inbox of exchange
-// n: two inboxes suffice.  A push may land before the receiver's expect_tx of
-// that exchange; the phase cannot complete before the receiver's own arrival.
+// Cluster totals of exchange n (bins [0, nb)) into s.tot.  Every CTA merges
+// its histograms into s.send and copies it into inbox[its rank] of every CTA
+// of the cluster (itself included) with one bulk shared-to-shared copy per
+// rank, which completes transaction bytes on the receiver's xbar (one copy of
+// nb * 8 bytes instead of nb remote 8-byte stores: the stores measured ~1.5 us
+// per exchange of 256 bins on 16 ranks).  Each CTA then waits for the C ranks'
+// bytes and sums them in rank order (so every CTA holds the same totals), and
+// arrives on the cluster barrier once it has read its inbox.  A CTA waits on
+// that barrier before it copies exchange n + 1, so one inbox suffices and the
+// per-rank weights of the last exchange stay readable.  A copy may land before
+// the receiver's expect_tx of that exchange; the phase cannot complete before
+// the receiver's own arrival.  s.send is rewritten only after that barrier,
+// when every copy that read it has landed.
 template <class SS>
-__device__ void hist_totals(SS& s, int rank, uint32_t n, int* err) {
+__device__ void hist_totals(SS& s, int rank, uint32_t n, int nb, int* err) {
   __syncthreads();
   {
-    const int d = threadIdx.x & 255, q = threadIdx.x >> 8;
+    const int lg = nb == 512 ? 9 : 8;
+    const int d = threadIdx.x & (nb - 1), q = threadIdx.x >> lg;
+    const int per = SS::kHist >> (10 - lg);   // histograms per merge group
     uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int w = 0; w < SS::kHist / 4; ++w) {
-      lo += s.whist[q * (SS::kHist / 4) + w][0][d];
-      hi += s.whist[q * (SS::kHist / 4) + w][1][d];
+    for (int w = 0; w < per; ++w) {
+      lo += s.whist[q * per + w][0][d];
+      hi += s.whist[q * per + w][1][d];
     }
-    s.qsum[q][d] = ((unsigned long long)hi << 16) + lo;
+    s.qsum[threadIdx.x] = ((unsigned long long)hi << 16) + lo;
   }
   __syncthreads();
-  const int buf = n & 1;
-  if (threadIdx.x == 0)
-    mbar_arrive_expect_tx(&s.xbar[buf], (uint32_t)(SS::kC * 256 * sizeof(unsigned long long)));
-  if (threadIdx.x < 256) {
+  // every rank has read the previous exchange: its copies (which read s.send)
+  // have all landed
+  if (n > 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (threadIdx.x < nb) {
+    unsigned long long h = 0;
+    for (int q = threadIdx.x; q < kSampThreads; q += nb) h += s.qsum[q];
+    s.send[threadIdx.x] = h;
+    fence_proxy_async();   // the generic writes, visible to the bulk copies
+  }
+  __syncthreads();
+  const uint32_t bar = smem_u32(&s.xbar);
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(&s.xbar, (uint32_t)(SS::kC * nb * sizeof(unsigned long long)));
+  if (threadIdx.x < SS::kC) {
+    const int r = threadIdx.x;
+    uint32_t rdst, rbar;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(smem_u32(&s.inbox[rank][0])), "r"(r));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(bar), "r"(r));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(rdst), "r"(smem_u32(s.send)), "r"((uint32_t)(nb * sizeof(unsigned long long))), "r"(rbar)
+        : "memory");
+  }
+  if (threadIdx.x < nb) {
     const int d = threadIdx.x;
-    const unsigned long long h = s.qsum[0][d] + s.qsum[1][d] + s.qsum[2][d] + s.qsum[3][d];
-    const uint32_t src = smem_u32(&s.inbox[buf][rank][d]), bar = smem_u32(&s.xbar[buf]);
-#pragma unroll
-    for (int r = 0; r < SS::kC; ++r) {
-      uint32_t rdst, rbar;
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(src), "r"(r));
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(bar), "r"(r));
-      asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u64 [%0], %1, [%2];"
-                   ::"r"(rdst), "l"(h), "r"(rbar) : "memory");
-    }
-    const uint32_t parity = (n >> 1) & 1;
+    const uint32_t parity = n & 1;
     uint32_t ok = 0;
     for (uint32_t it = 0; it < (1u << 22) && !ok; ++it)
       asm volatile(
@@ -249,10 +267,50 @@ __device__ void hist_totals(SS& s, int rank, uint32_t n, int* err) {
     if (!ok) raise_error(err, kDevWaitTimeout);
     unsigned long long sum = 0;
 #pragma unroll
-    for (int r = 0; r < SS::kC; ++r) sum += s.inbox[buf][r][d];
+    for (int r = 0; r < SS::kC; ++r) sum += s.inbox[r][d];
     s.tot[d] = sum;
   }
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   __syncthreads();
+}
+
+// Warp-wide digit scan of 256 digit weights w (descending digits): lane l
+// holds digits 255-8l .. 248-8l in v, their sum in mine and the inclusive sum
+// over lanes 0..l in incl.
+__device__ __forceinline__ void digit_scan(const unsigned long long* w, unsigned long long (&v)[8],
+                                           unsigned long long& mine, unsigned long long& incl) {
+  const int lane = threadIdx.x & 31;
+  mine = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    v[j] = w[255 - 8 * lane - j];
+    mine += v[j];
+  }
+  incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+}
+
+// The largest digit d with above + sum(w[d..255]) >= target (digit 0 when the
+// total falls short) and above + sum(w[d+1..255]), in every lane.
+__device__ __forceinline__ void digit_pick(const unsigned long long (&v)[8], unsigned long long mine,
+                                           unsigned long long incl, unsigned long long above,
+                                           unsigned long long target, uint32_t& sel,
+                                           unsigned long long& sel_above) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t hit = __ballot_sync(0xffffffffu, above + incl >= target);
+  const int L = hit ? __ffs(hit) - 1 : 31;
+  unsigned long long run = above + incl - mine;
+  int j = 0;
+  for (; j < 7; ++j) {
+    if (run + v[j] >= target) break;
+    run += v[j];
+  }
+  sel = (uint32_t)__shfl_sync(0xffffffffu, 255 - 8 * lane - j, L);
+  sel_above = __shfl_sync(0xffffffffu, run, L);
 }
 
 // Selected digit of the pass: the largest d with above + sum(tot[d..255]) >=
@@ -308,8 +366,7 @@ __global__ void __launch_bounds__(kSampThreads)
   const int lo = rank * chunk;
   const int n_local = max(0, min(vocab, lo + chunk) - lo);
   if (threadIdx.x == 0) {   // visible to the cluster after the first cluster.sync below
-    mbar_init(&s.xbar[0], 1);
-    mbar_init(&s.xbar[1], 1);
+    mbar_init(&s.xbar, 1);
     fence_mbar_init();
   }
 
@@ -423,9 +480,9 @@ __global__ void __launch_bounds__(kSampThreads)
     return;
   }
   // ---- fixed-point weights, histogrammed by their first digit -----------
-  // The first pass of the nucleus select needs every weight, so it is built
+  // The first pass of the cutoff select needs every weight, so it is built
   // here; the total S is the sum of its cluster totals.
-  hist_clear(s);
+  hist_clear(s, 256);
 #pragma unroll
   for (int k = 0; k < kSampPerThread; ++k) {
     const int i = k * kSampThreads + (int)threadIdx.x;
@@ -441,112 +498,231 @@ __global__ void __launch_bounds__(kSampThreads)
     hist_add(s, E != 0u, E, E >> 24);
   }
   uint32_t xn = 0;   // exchanges so far
-  hist_totals(s, rank, xn++, err);
-  const unsigned long long S = block_sum_u64(threadIdx.x < 256 ? s.tot[threadIdx.x] : 0ull, s);
+  hist_totals(s, rank, xn++, 256, err);
   const float pc = fminf(fmaxf(top_p, 0.0f), 1.0f);
   const uint32_t p24 = (uint32_t)__float2uint_rz(__fmul_rn(pc, 16777216.0f));
-  unsigned long long thr = mul_shift24(S, p24);
-  if (thr == 0) thr = 1;
+  const uint32_t u = u24[seq] & 0xFFFFFFu;
+  const int warp = threadIdx.x >> 5;
 
-  // ---- nucleus cutoff: the value e_star where the weight from the top first
-  // reaches thr, and the weight strictly above it ------------------------------
-  uint32_t prefix = 0, mask = 0;
-  unsigned long long above = 0;
+  // ---- the cutoff select (the value e_star where the weight from the top
+  // first reaches thr) and, beside it, the draw select -----------------------
+  // The draw wants the first kept id whose running weight exceeds
+  // R = floor(kept * u / 2^24), kept = the cutoff's kept weight, which lies in
+  // [thr, thr + e_star - 1]; after pass p the cutoff's prefix bounds e_star,
+  // so R lies in a known range.  When both ends of the range pick the same
+  // digit, that digit is the draw's (the pick is monotone in the target) and
+  // the next pass histograms the draw's members too.  While the draw's prefix
+  // equals the cutoff's ("on e_star") its digit weights follow from the
+  // cutoff's histogram.  Pass 3 has the exact R.  When the ends part, the draw
+  // resumes at that pass after the cutoff select, exactly as below.
+  if (threadIdx.x == 0) {
+    s.an = 0;
+    s.ad = 0;
+    s.pn = 0;
+    s.pd = 0;
+    s.dmode = SS::kSpec ? 0 : 2;   // 0 on e_star, 1 parted, 2 left the speculation
+    s.dfail = 0;
+    s.don = 1;
+    s.dhi = 0;
+  }
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
+    const uint32_t mask = pass == 0 ? 0u : 0xFFFFFFFFu << (shift + 8);
     if (pass > 0) {
-      hist_clear(s);
+      __syncthreads();
+      const uint32_t pn = s.pn, pd = s.pd;
+      const bool dact = SS::kSpec && s.dmode == 1;
+      hist_clear(s, dact ? 512 : 256);
 #pragma unroll
       for (int k = 0; k < kSampPerThread; ++k) {
         const int i = k * kSampThreads + (int)threadIdx.x;
         const uint32_t e = i < n_local ? s.e[i] : 0u;
-        hist_add(s, e != 0u && (e & mask) == prefix, e, (e >> shift) & 255u);
+        const bool mn = e != 0u && (e & mask) == pn;
+        const bool md = dact && (e & mask) == pd;   // members of the two never overlap
+        hist_add(s, mn || md, e, ((e >> shift) & 255u) | (md ? 256u : 0u));
       }
-      hist_totals(s, rank, xn++, err);
+      hist_totals(s, rank, xn++, dact ? 512 : 256, err);
     }
     if (threadIdx.x < 256) s.tot1[pass][threadIdx.x] = s.tot[threadIdx.x];
-    pick_digit(s, above, thr);
-    prefix |= s.sel << shift;
-    mask |= 255u << shift;
-    above = s.sel_above;
-    if (threadIdx.x == 0) s.above1[pass] = above;
-  }
-  const uint32_t e_star = prefix;
-  const unsigned long long above_star = above;   // weight of E > e_star
-  const unsigned long long need = thr - above_star;
-  const unsigned long long k_tie = (need + e_star - 1) / e_star;  // e_star >= 1
-  const unsigned long long kept = above_star + k_tie * e_star;
-
-  // ---- draw: the same select over the kept set (E > e_star, plus k_tie
-  // copies of e_star as one weight at e_star) for R + 1 ----------------------
-  // While the draw's prefix equals e_star's, its digit totals follow from the
-  // nucleus select's: above e_star's digit they are the same members; at that
-  // digit they are the weight above e_star not yet counted above the prefix,
-  // plus the tie weight; below it there are none.  Only passes after the
-  // prefixes part scan the weights (and those members all exceed e_star).
-  const unsigned long long R = mul_shift24(kept, u24[seq] & 0xFFFFFFu);
-  prefix = 0;
-  mask = 0;
-  above = 0;
-  bool on_star = true;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    const uint32_t ds = (e_star >> shift) & 255u;
-    if (on_star) {
-      if (threadIdx.x < 256) {
-        const uint32_t d = threadIdx.x;
-        s.tot[d] = d > ds ? s.tot1[pass][d]
-                 : d == ds ? (above_star - s.above1[pass]) + k_tie * e_star : 0ull;
+    if (warp == 0) {
+      const int lane = threadIdx.x & 31;
+      unsigned long long v[8], mine, incl;
+      digit_scan(s.tot, v, mine, incl);
+      if (pass == 0) {
+        const unsigned long long S = __shfl_sync(0xffffffffu, incl, 31);
+        unsigned long long t = mul_shift24(S, p24);
+        if (t == 0) t = 1;
+        if (lane == 0) s.thr = t;
       }
-      __syncthreads();
-    } else {
-      hist_clear(s);
-#pragma unroll
-      for (int k = 0; k < kSampPerThread; ++k) {
-        const int i = k * kSampThreads + (int)threadIdx.x;
-        const uint32_t e = i < n_local ? s.e[i] : 0u;
-        hist_add(s, e > e_star && (e & mask) == prefix, e, (e >> shift) & 255u);
+      __syncwarp();
+      const unsigned long long thr = s.thr, an = s.an;
+      uint32_t seln;
+      unsigned long long aboven;
+      digit_pick(v, mine, incl, an, thr, seln, aboven);
+      const uint32_t pn = s.pn | (seln << shift);
+      unsigned long long tl = 0, th = 0;
+      if (pass == 3) {   // e_star = pn, exact kept and R
+        const unsigned long long need = thr - aboven;
+        const unsigned long long k_tie = (need + pn - 1) / pn;
+        const unsigned long long R = mul_shift24(aboven + k_tie * pn, u);
+        tl = th = R + 1;
+        if (lane == 0) s.R = R;
+      } else {
+        const uint32_t e_hi = pn | ((1u << shift) - 1u);
+        tl = mul_shift24(thr, u) + 1;
+        th = mul_shift24(thr + e_hi - 1, u) + 1;
       }
-      hist_totals(s, rank, xn++, err);
+      int dmode = s.dmode;
+      uint32_t pd = s.pd;
+      unsigned long long ad = s.ad;
+      int dhi = 0;
+      if (dmode == 0) {
+        // on e_star: the draw stays there when its target lies below the
+        // weight above the cutoff's digit, else picks among the digits above it
+        if (tl > aboven) {
+          pd = pn;
+          ad = aboven;
+        } else if (th <= aboven) {
+          uint32_t sl, sh;
+          unsigned long long al, ah;
+          digit_pick(v, mine, incl, ad, tl, sl, al);
+          digit_pick(v, mine, incl, ad, th, sh, ah);
+          if (sl == sh) {
+            dmode = 1;
+            pd |= sl << shift;
+            ad = al;
+          } else {
+            dmode = 2;
+          }
+        } else {
+          dmode = 2;
+        }
+      } else if (dmode == 1) {
+        unsigned long long w[8], dm, di;
+        digit_scan(s.tot + (SS::kBins - 256), w, dm, di);
+        uint32_t sl, sh;
+        unsigned long long al, ah;
+        digit_pick(w, dm, di, ad, tl, sl, al);
+        digit_pick(w, dm, di, ad, th, sh, ah);
+        if (sl == sh) {
+          pd |= sl << shift;
+          ad = al;
+          dhi = 1;
+        } else {
+          dmode = 2;
+        }
+      }
+      if (lane == 0) {
+        s.an = aboven;
+        s.above1[pass] = aboven;
+        s.pn = pn;
+        if (s.dmode != 2) {
+          if (dmode == 2) {   // left at this pass: its state before the pass stays
+            s.dfail = pass;
+            s.don = s.dmode == 0;
+          } else {
+            s.pd = pd;
+            s.ad = ad;
+            s.dhi = dhi;
+          }
+          s.dmode = dmode;
+        }
+      }
     }
-    pick_digit(s, above, R + 1);
-    const uint32_t sel = s.sel;
-    on_star = on_star && sel == ds;
-    prefix |= sel << shift;
-    mask |= 255u << shift;
-    above = s.sel_above;
   }
-  const uint32_t e2 = prefix;
+  __syncthreads();
+  const uint32_t e_star = s.pn;
+  const unsigned long long above_star = s.an;   // weight of E > e_star
+  const unsigned long long R = s.R;
+  uint32_t e2;
+  unsigned long long above;
+  uint32_t bin3;   // bin of the draw's value in the last exchange
+  if (s.dmode != 2) {
+    e2 = s.pd;
+    above = s.ad;
+    bin3 = (e2 & 255u) | (s.dhi ? 256u : 0u);
+  } else {
+    // ---- the draw from the pass at which it left the speculation: the same
+    // select over the kept set (E > e_star, plus k_tie copies of e_star as one
+    // weight at e_star) for R + 1 --------------------------------------------
+    // While the draw's prefix equals e_star's, its digit totals follow from
+    // the cutoff select's: above e_star's digit they are the same members; at
+    // that digit they are the weight above e_star not yet counted above the
+    // prefix, plus the tie weight; below it there are none.  Only passes after
+    // the prefixes part scan the weights (and those members all exceed e_star).
+    const unsigned long long thr = s.thr;
+    const unsigned long long k_tie = (thr - above_star + e_star - 1) / e_star;  // e_star >= 1
+    const int pf = s.dfail;
+    uint32_t prefix = s.pd;
+    above = s.ad;
+    bool on_star = s.don != 0;
+    for (int pass = pf; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      const uint32_t mask = pass == 0 ? 0u : 0xFFFFFFFFu << (shift + 8);
+      const uint32_t ds = (e_star >> shift) & 255u;
+      if (on_star) {
+        __syncthreads();
+        if (threadIdx.x < 256) {
+          const uint32_t d = threadIdx.x;
+          s.tot[d] = d > ds ? s.tot1[pass][d]
+                   : d == ds ? (above_star - s.above1[pass]) + k_tie * e_star : 0ull;
+        }
+        __syncthreads();
+      } else {
+        hist_clear(s, 256);
+#pragma unroll
+        for (int k = 0; k < kSampPerThread; ++k) {
+          const int i = k * kSampThreads + (int)threadIdx.x;
+          const uint32_t e = i < n_local ? s.e[i] : 0u;
+          hist_add(s, e > e_star && (e & mask) == prefix, e, (e >> shift) & 255u);
+        }
+        hist_totals(s, rank, xn++, 256, err);
+      }
+      pick_digit(s, above, R + 1);
+      const uint32_t sel = s.sel;
+      on_star = on_star && sel == ds;
+      prefix |= sel << shift;
+      above = s.sel_above;
+    }
+    e2 = prefix;
+    bin3 = e2 & 255u;
+  }
   const unsigned long long j = (R - above) / e2;   // index inside the tie group (id order)
 
   // ---- j-th smallest id with E == e2 ---------------------------------------
-  // Threads own contiguous id ranges so that block order = id order.
-  const int per = (n_local + (int)blockDim.x - 1) / (int)blockDim.x;
-  const int b0 = threadIdx.x * per, b1 = min(n_local, b0 + per);
-  uint32_t cnt = 0;
-  for (int i = b0; i < b1; ++i) cnt += (s.e[i] == e2);
-  const uint32_t incl = block_incl_scan_u32(cnt, s), excl = incl - cnt;
-  if (threadIdx.x == blockDim.x - 1) s.cl_cnt = incl;
-  cluster.sync();
-  __shared__ unsigned long long s_before;
-  if (threadIdx.x == 0) {
-    unsigned long long t = 0;
-    for (int r = 0; r < rank; ++r) t += cluster.map_shared_rank(&s, r)->cl_cnt;
-    s_before = t;
+  // The last exchange holds every rank's weight at e2's final digit, which is
+  // that rank's count of E == e2 times e2: the ranks before this one hold
+  // `before` of them, this one `cnt`.  Threads own contiguous id ranges so that
+  // block order = id order.
+  unsigned long long before = 0, cnt = 0;
+  for (int r = 0; r < C; ++r) {
+    const unsigned long long w = s.inbox[r][bin3];
+    if (r < rank) before += w;
+    if (r == rank) cnt = w;
   }
-  __syncthreads();
-  const unsigned long long before = s_before;
-  if (j >= before + excl && j < before + incl) {
-    unsigned long long want = j - before - excl;
-    for (int i = b0; i < b1; ++i) {
-      if (s.e[i] == e2) {
-        if (want == 0) { out_ids[seq] = lo + i; break; }
-        --want;
+  before /= e2;
+  cnt /= e2;
+  if (j >= before && j < before + cnt) {
+    const int per = (n_local + (int)blockDim.x - 1) / (int)blockDim.x;
+    const int b0 = threadIdx.x * per, b1 = min(n_local, b0 + per);
+    uint32_t c = 0;
+    for (int i = b0; i < b1; ++i) c += (s.e[i] == e2);
+    const uint32_t incl = block_incl_scan_u32(c, s), excl = incl - c;
+    if (j >= before + excl && j < before + incl) {
+      unsigned long long want = j - before - excl;
+      for (int i = b0; i < b1; ++i) {
+        if (s.e[i] == e2) {
+          if (want == 0) { out_ids[seq] = lo + i; break; }
+          --want;
+        }
       }
     }
   }
-  cluster.sync();
+  // pairs with the last exchange's arrival: no CTA leaves while a peer may
+  // still read its shared memory
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+
 
 size_t sampler_scratch_bytes(int) { return 0; }
 
