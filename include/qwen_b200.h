@@ -181,6 +181,20 @@ int qwen_sample(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uin
                 float temperature, float top_p, const uint32_t* u24, int32_t* out_ids,
                 void* stream);
 
+/* Device scratch bytes for qwen_sample_scratch (0 when n_seq > 1). */
+size_t qwen_sample_scratch_bytes(uint32_t n_seq);
+
+/* qwen_sample with device scratch of qwen_sample_scratch_bytes(n_seq) bytes,
+ * zero before its first use (every call leaves it zero).  With one sequence
+ * and temperature > 0 the sequence runs on every SM at once (a cooperative
+ * launch; the CTAs exchange digit totals through the scratch), otherwise as
+ * qwen_sample.  Calls that share a scratch must be ordered on one stream.
+ * The same ids as qwen_sample (InferenceEngine.swift:273-368); the batch-1
+ * engine step samples this way. */
+int qwen_sample_scratch(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uint32_t vocab,
+                        float temperature, float top_p, const uint32_t* u24, int32_t* out_ids,
+                        void* scratch, void* stream);
+
 /* 24-bit uniform for (seed, sequence, step), SplitMix64 based; host helper. */
 uint32_t qwen_uniform24(uint64_t seed, uint64_t sequence, uint64_t step);
 

@@ -77,6 +77,9 @@ SIGNATURES = {
     "qwen_quantize_q4": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
     "qwen_sample": (c_int, [c_void_p, c_uint32, c_uint32, c_uint32, c_float, c_float, c_void_p,
                             c_void_p, c_void_p]),
+    "qwen_sample_scratch_bytes": (c_size_t, [c_uint32]),
+    "qwen_sample_scratch": (c_int, [c_void_p, c_uint32, c_uint32, c_uint32, c_float, c_float,
+                                    c_void_p, c_void_p, c_void_p, c_void_p]),
     "qwen_uniform24": (c_uint32, [c_uint64, c_uint64, c_uint64]),
     "qwen_engine_config_default": (None, [ctypes.POINTER(EngineConfig)]),
     "qwen_engine_create": (c_int, [ctypes.POINTER(EngineConfig), ctypes.POINTER(c_void_p)]),

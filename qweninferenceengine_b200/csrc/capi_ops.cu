@@ -233,6 +233,27 @@ int qwen_sample(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uin
   return QWEN_OK;
 }
 
+size_t qwen_sample_scratch_bytes(uint32_t n_seq) { return sampler_scratch_bytes((int)n_seq); }
+
+int qwen_sample_scratch(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uint32_t vocab,
+                        float temperature, float top_p, const uint32_t* u24, int32_t* out_ids,
+                        void* scratch, void* stream) {
+  if (!logits || !out_ids) return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: null buffer");
+  if (vocab == 0 || vocab > (uint32_t)kVocab || row_stride < vocab)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: vocab=%u row_stride=%u", vocab, row_stride);
+  if (temperature > 0.0f && !u24) return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: top-p needs u24");
+  if (sampler_scratch_bytes((int)n_seq) && !scratch)
+    return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: null scratch");
+  if (n_seq == 0) return QWEN_OK;
+  if (n_seq > 65535) return set_error(QWEN_ERR_INVALID_ARGUMENT, "sample: n_seq=%u", n_seq);
+  int* status = nullptr;
+  if (int rc = ops_status_word(&status)) return rc;
+  if (launch_sample(H(logits), (int)n_seq, (int)row_stride, (int)vocab, temperature, top_p, u24,
+                    out_ids, scratch, status, reinterpret_cast<cudaStream_t>(stream)) != 0)
+    return launch_status("sample");
+  return QWEN_OK;
+}
+
 uint32_t qwen_uniform24(uint64_t seed, uint64_t sequence, uint64_t step) {
   return uniform24(seed, sequence, step);
 }

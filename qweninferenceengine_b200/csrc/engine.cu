@@ -293,6 +293,8 @@ int InferenceManager::allocate(int b, int nl, int mc, int mo) {
   QWEN_TRY(alloc(sizeof(uint32_t) * 4, (void**)&epoch));
   attn_splits = attn_max_splits(mc, b);
   QWEN_TRY(alloc(attn_scratch_bytes(attn_splits, b), &attn_scratch));
+  samp_scratch_bytes = sampler_scratch_bytes(b);
+  if (samp_scratch_bytes) QWEN_TRY(alloc(samp_scratch_bytes, &samp_scratch));
   return QWEN_OK;
 }
 
@@ -417,7 +419,7 @@ int QwenEngine::enqueue_step_ops(cudaEvent_t* ev) {
   launch_gemv_fp16_rowmajor(m.embed, s.residual, s.logits, kVocab, kHidden, vs);
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, nullptr, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   if (ev) cudaEventRecord(ev[3], st);
@@ -435,7 +437,7 @@ int QwenEngine::enqueue_step_fused(cudaEvent_t* ev) {
   QWEN_TRY(enqueue_fused_step(a, st));
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, nullptr, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   if (ev) cudaEventRecord(ev[3], st);
@@ -452,7 +454,7 @@ int QwenEngine::enqueue_step_tc(cudaEvent_t* ev) {
   QWEN_TRY(enqueue_tc_model(model_, state_, tc_decode_rows(state_), sm_count_, st));
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, nullptr, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   if (ev) cudaEventRecord(ev[3], st);
@@ -497,6 +499,8 @@ int QwenEngine::check_device_error() {
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
   if (h[0] == 0) return QWEN_OK;
   cudaMemsetAsync(state_.err, 0, sizeof(h), stream_);
+  // a wait that gave up can leave the grid sampler's exchange words set
+  if (state_.samp_scratch) cudaMemsetAsync(state_.samp_scratch, 0, state_.samp_scratch_bytes, stream_);
   cudaStreamSynchronize(stream_);
   if (h[0] == kDevWaitTimeout)
     return set_error(QWEN_ERR_DEVICE_TIMEOUT,
@@ -684,7 +688,7 @@ int QwenEngine::profile_step(float* ms, int cap, int* n) {
   int rc = enqueue_tc_model(model_, state_, tc_decode_rows(state_), sm_count_, st, ev.data() + 1,
                             &marks);
   if (rc == QWEN_OK && launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature,
-                                     cfg_.top_p, s.u24_, s.sampled, nullptr, s.err, st) != 0)
+                                     cfg_.top_p, s.u24_, s.sampled, s.samp_scratch, s.err, st) != 0)
     rc = launch_status("sample");
   if (rc == QWEN_OK)
     k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
@@ -756,7 +760,7 @@ int QwenEngine::prefill_chunked(const int32_t* ids, int32_t n) {
                               (size_t)last * kVocab * 2, (size_t)kVocab * 2, B, cudaMemcpyDeviceToDevice,
                               st), "memcpy logits");
   if (launch_sample(s.logits, B, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, nullptr, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st) != 0)
     return launch_status("sample");
   k_step_end<<<1, B, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   QWEN_TRY(launch_status("chunked prefill"));

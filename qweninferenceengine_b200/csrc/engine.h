@@ -145,6 +145,8 @@ class InferenceManager {
   unsigned long long* trace = nullptr;  // optional fused-step phase stamps
   void* attn_scratch = nullptr;
   int attn_splits = 0;
+  void* samp_scratch = nullptr;  // batch-1 grid sampler's exchanges (zero between launches)
+  size_t samp_scratch_bytes = 0;
   void* fused_scratch = nullptr;
   size_t fused_scratch_bytes = 0;
   // tensor-core batched step (tc_gemm.h layouts)

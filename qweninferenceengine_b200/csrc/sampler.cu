@@ -349,6 +349,206 @@ __device__ void pick_digit(SS& s, unsigned long long above, unsigned long long t
   __syncthreads();
 }
 
+// The cutoff select (the value e_star where the weight from the top first
+// reaches thr) with the draw select beside it, then the draw's exact
+// remainder; shared by the cluster and grid kernels.  On entry s.tot holds the
+// totals of pass 0 (built with the weights).  clear(nb) zeroes bins [0, nb) of
+// the histograms; totals(nb) runs the next exchange of bins [0, nb) into
+// s.tot.  Leaves the drawn value e2, the kept weight above it, R, e2's bin in
+// the last exchange, and whether s.tot still holds that exchange's totals
+// (else they are the cutoff's pass-3 totals, s.tot1[3]).
+template <class SS, int kThreads, int kPer, class ClearF, class TotalsF>
+__device__ __forceinline__ void select_draw(SS& s, int n_local, uint32_t p24, uint32_t u,
+                                            ClearF&& clear, TotalsF&& totals, uint32_t& e2,
+                                            unsigned long long& above, unsigned long long& R,
+                                            uint32_t& bin3, bool& tot_real) {
+  const int warp = threadIdx.x >> 5;
+
+  // ---- the cutoff select (the value e_star where the weight from the top
+  // first reaches thr) and, beside it, the draw select -----------------------
+  // The draw wants the first kept id whose running weight exceeds
+  // R = floor(kept * u / 2^24), kept = the cutoff's kept weight, which lies in
+  // [thr, thr + e_star - 1]; after pass p the cutoff's prefix bounds e_star,
+  // so R lies in a known range.  When both ends of the range pick the same
+  // digit, that digit is the draw's (the pick is monotone in the target) and
+  // the next pass histograms the draw's members too.  While the draw's prefix
+  // equals the cutoff's ("on e_star") its digit weights follow from the
+  // cutoff's histogram.  Pass 3 has the exact R.  When the ends part, the draw
+  // resumes at that pass after the cutoff select, exactly as below.
+  if (threadIdx.x == 0) {
+    s.an = 0;
+    s.ad = 0;
+    s.pn = 0;
+    s.pd = 0;
+    s.dmode = SS::kSpec ? 0 : 2;   // 0 on e_star, 1 parted, 2 left the speculation
+    s.dfail = 0;
+    s.don = 1;
+    s.dhi = 0;
+  }
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t mask = pass == 0 ? 0u : 0xFFFFFFFFu << (shift + 8);
+    if (pass > 0) {
+      __syncthreads();
+      const uint32_t pn = s.pn, pd = s.pd;
+      const bool dact = SS::kSpec && s.dmode == 1;
+      clear(dact ? 512 : 256);
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int i = k * kThreads + (int)threadIdx.x;
+        const uint32_t e = i < n_local ? s.e[i] : 0u;
+        const bool mn = e != 0u && (e & mask) == pn;
+        const bool md = dact && (e & mask) == pd;   // members of the two never overlap
+        hist_add(s, mn || md, e, ((e >> shift) & 255u) | (md ? 256u : 0u));
+      }
+      totals(dact ? 512 : 256);
+    }
+    if (threadIdx.x < 256) s.tot1[pass][threadIdx.x] = s.tot[threadIdx.x];
+    if (warp == 0) {
+      const int lane = threadIdx.x & 31;
+      unsigned long long v[8], mine, incl;
+      digit_scan(s.tot, v, mine, incl);
+      if (pass == 0) {
+        const unsigned long long S = __shfl_sync(0xffffffffu, incl, 31);
+        unsigned long long t = mul_shift24(S, p24);
+        if (t == 0) t = 1;
+        if (lane == 0) s.thr = t;
+      }
+      __syncwarp();
+      const unsigned long long thr = s.thr, an = s.an;
+      uint32_t seln;
+      unsigned long long aboven;
+      digit_pick(v, mine, incl, an, thr, seln, aboven);
+      const uint32_t pn = s.pn | (seln << shift);
+      unsigned long long tl = 0, th = 0;
+      if (pass == 3) {   // e_star = pn, exact kept and R
+        const unsigned long long need = thr - aboven;
+        const unsigned long long k_tie = (need + pn - 1) / pn;
+        const unsigned long long R = mul_shift24(aboven + k_tie * pn, u);
+        tl = th = R + 1;
+        if (lane == 0) s.R = R;
+      } else {
+        const uint32_t e_hi = pn | ((1u << shift) - 1u);
+        tl = mul_shift24(thr, u) + 1;
+        th = mul_shift24(thr + e_hi - 1, u) + 1;
+      }
+      int dmode = s.dmode;
+      uint32_t pd = s.pd;
+      unsigned long long ad = s.ad;
+      int dhi = 0;
+      if (dmode == 0) {
+        // on e_star: the draw stays there when its target lies below the
+        // weight above the cutoff's digit, else picks among the digits above it
+        if (tl > aboven) {
+          pd = pn;
+          ad = aboven;
+        } else if (th <= aboven) {
+          uint32_t sl, sh;
+          unsigned long long al, ah;
+          digit_pick(v, mine, incl, ad, tl, sl, al);
+          digit_pick(v, mine, incl, ad, th, sh, ah);
+          if (sl == sh) {
+            dmode = 1;
+            pd |= sl << shift;
+            ad = al;
+          } else {
+            dmode = 2;
+          }
+        } else {
+          dmode = 2;
+        }
+      } else if (dmode == 1) {
+        unsigned long long w[8], dm, di;
+        digit_scan(s.tot + (SS::kBins - 256), w, dm, di);
+        uint32_t sl, sh;
+        unsigned long long al, ah;
+        digit_pick(w, dm, di, ad, tl, sl, al);
+        digit_pick(w, dm, di, ad, th, sh, ah);
+        if (sl == sh) {
+          pd |= sl << shift;
+          ad = al;
+          dhi = 1;
+        } else {
+          dmode = 2;
+        }
+      }
+      if (lane == 0) {
+        s.an = aboven;
+        s.above1[pass] = aboven;
+        s.pn = pn;
+        if (s.dmode != 2) {
+          if (dmode == 2) {   // left at this pass: its state before the pass stays
+            s.dfail = pass;
+            s.don = s.dmode == 0;
+          } else {
+            s.pd = pd;
+            s.ad = ad;
+            s.dhi = dhi;
+          }
+          s.dmode = dmode;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t e_star = s.pn;
+  const unsigned long long above_star = s.an;   // weight of E > e_star
+  R = s.R;
+  if (s.dmode != 2) {
+    e2 = s.pd;
+    above = s.ad;
+    bin3 = (e2 & 255u) | (s.dhi ? 256u : 0u);
+    tot_real = true;
+  } else {
+    // ---- the draw from the pass at which it left the speculation: the same
+    // select over the kept set (E > e_star, plus k_tie copies of e_star as one
+    // weight at e_star) for R + 1 --------------------------------------------
+    // While the draw's prefix equals e_star's, its digit totals follow from
+    // the cutoff select's: above e_star's digit they are the same members; at
+    // that digit they are the weight above e_star not yet counted above the
+    // prefix, plus the tie weight; below it there are none.  Only passes after
+    // the prefixes part scan the weights (and those members all exceed e_star).
+    const unsigned long long thr = s.thr;
+    const unsigned long long k_tie = (thr - above_star + e_star - 1) / e_star;  // e_star >= 1
+    const int pf = s.dfail;
+    uint32_t prefix = s.pd;
+    above = s.ad;
+    bool on_star = s.don != 0;
+    tot_real = false;
+    for (int pass = pf; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      const uint32_t mask = pass == 0 ? 0u : 0xFFFFFFFFu << (shift + 8);
+      const uint32_t ds = (e_star >> shift) & 255u;
+      if (on_star) {
+        __syncthreads();
+        if (threadIdx.x < 256) {
+          const uint32_t d = threadIdx.x;
+          s.tot[d] = d > ds ? s.tot1[pass][d]
+                   : d == ds ? (above_star - s.above1[pass]) + k_tie * e_star : 0ull;
+        }
+        __syncthreads();
+      } else {
+        clear(256);
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int i = k * kThreads + (int)threadIdx.x;
+          const uint32_t e = i < n_local ? s.e[i] : 0u;
+          hist_add(s, e > e_star && (e & mask) == prefix, e, (e >> shift) & 255u);
+        }
+        totals(256);
+        tot_real = pass == 3;
+      }
+      pick_digit(s, above, R + 1);
+      const uint32_t sel = s.sel;
+      on_star = on_star && sel == ds;
+      prefix |= sel << shift;
+      above = s.sel_above;
+    }
+    e2 = prefix;
+    bin3 = e2 & 255u;
+  }
+}
+
 template <int C>
 __global__ void __launch_bounds__(kSampThreads)
     k_sample(const __half* __restrict__ logits, int row_stride, int vocab, float temperature,
@@ -502,191 +702,12 @@ __global__ void __launch_bounds__(kSampThreads)
   const float pc = fminf(fmaxf(top_p, 0.0f), 1.0f);
   const uint32_t p24 = (uint32_t)__float2uint_rz(__fmul_rn(pc, 16777216.0f));
   const uint32_t u = u24[seq] & 0xFFFFFFu;
-  const int warp = threadIdx.x >> 5;
-
-  // ---- the cutoff select (the value e_star where the weight from the top
-  // first reaches thr) and, beside it, the draw select -----------------------
-  // The draw wants the first kept id whose running weight exceeds
-  // R = floor(kept * u / 2^24), kept = the cutoff's kept weight, which lies in
-  // [thr, thr + e_star - 1]; after pass p the cutoff's prefix bounds e_star,
-  // so R lies in a known range.  When both ends of the range pick the same
-  // digit, that digit is the draw's (the pick is monotone in the target) and
-  // the next pass histograms the draw's members too.  While the draw's prefix
-  // equals the cutoff's ("on e_star") its digit weights follow from the
-  // cutoff's histogram.  Pass 3 has the exact R.  When the ends part, the draw
-  // resumes at that pass after the cutoff select, exactly as below.
-  if (threadIdx.x == 0) {
-    s.an = 0;
-    s.ad = 0;
-    s.pn = 0;
-    s.pd = 0;
-    s.dmode = SS::kSpec ? 0 : 2;   // 0 on e_star, 1 parted, 2 left the speculation
-    s.dfail = 0;
-    s.don = 1;
-    s.dhi = 0;
-  }
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    const uint32_t mask = pass == 0 ? 0u : 0xFFFFFFFFu << (shift + 8);
-    if (pass > 0) {
-      __syncthreads();
-      const uint32_t pn = s.pn, pd = s.pd;
-      const bool dact = SS::kSpec && s.dmode == 1;
-      hist_clear(s, dact ? 512 : 256);
-#pragma unroll
-      for (int k = 0; k < kSampPerThread; ++k) {
-        const int i = k * kSampThreads + (int)threadIdx.x;
-        const uint32_t e = i < n_local ? s.e[i] : 0u;
-        const bool mn = e != 0u && (e & mask) == pn;
-        const bool md = dact && (e & mask) == pd;   // members of the two never overlap
-        hist_add(s, mn || md, e, ((e >> shift) & 255u) | (md ? 256u : 0u));
-      }
-      hist_totals(s, rank, xn++, dact ? 512 : 256, err);
-    }
-    if (threadIdx.x < 256) s.tot1[pass][threadIdx.x] = s.tot[threadIdx.x];
-    if (warp == 0) {
-      const int lane = threadIdx.x & 31;
-      unsigned long long v[8], mine, incl;
-      digit_scan(s.tot, v, mine, incl);
-      if (pass == 0) {
-        const unsigned long long S = __shfl_sync(0xffffffffu, incl, 31);
-        unsigned long long t = mul_shift24(S, p24);
-        if (t == 0) t = 1;
-        if (lane == 0) s.thr = t;
-      }
-      __syncwarp();
-      const unsigned long long thr = s.thr, an = s.an;
-      uint32_t seln;
-      unsigned long long aboven;
-      digit_pick(v, mine, incl, an, thr, seln, aboven);
-      const uint32_t pn = s.pn | (seln << shift);
-      unsigned long long tl = 0, th = 0;
-      if (pass == 3) {   // e_star = pn, exact kept and R
-        const unsigned long long need = thr - aboven;
-        const unsigned long long k_tie = (need + pn - 1) / pn;
-        const unsigned long long R = mul_shift24(aboven + k_tie * pn, u);
-        tl = th = R + 1;
-        if (lane == 0) s.R = R;
-      } else {
-        const uint32_t e_hi = pn | ((1u << shift) - 1u);
-        tl = mul_shift24(thr, u) + 1;
-        th = mul_shift24(thr + e_hi - 1, u) + 1;
-      }
-      int dmode = s.dmode;
-      uint32_t pd = s.pd;
-      unsigned long long ad = s.ad;
-      int dhi = 0;
-      if (dmode == 0) {
-        // on e_star: the draw stays there when its target lies below the
-        // weight above the cutoff's digit, else picks among the digits above it
-        if (tl > aboven) {
-          pd = pn;
-          ad = aboven;
-        } else if (th <= aboven) {
-          uint32_t sl, sh;
-          unsigned long long al, ah;
-          digit_pick(v, mine, incl, ad, tl, sl, al);
-          digit_pick(v, mine, incl, ad, th, sh, ah);
-          if (sl == sh) {
-            dmode = 1;
-            pd |= sl << shift;
-            ad = al;
-          } else {
-            dmode = 2;
-          }
-        } else {
-          dmode = 2;
-        }
-      } else if (dmode == 1) {
-        unsigned long long w[8], dm, di;
-        digit_scan(s.tot + (SS::kBins - 256), w, dm, di);
-        uint32_t sl, sh;
-        unsigned long long al, ah;
-        digit_pick(w, dm, di, ad, tl, sl, al);
-        digit_pick(w, dm, di, ad, th, sh, ah);
-        if (sl == sh) {
-          pd |= sl << shift;
-          ad = al;
-          dhi = 1;
-        } else {
-          dmode = 2;
-        }
-      }
-      if (lane == 0) {
-        s.an = aboven;
-        s.above1[pass] = aboven;
-        s.pn = pn;
-        if (s.dmode != 2) {
-          if (dmode == 2) {   // left at this pass: its state before the pass stays
-            s.dfail = pass;
-            s.don = s.dmode == 0;
-          } else {
-            s.pd = pd;
-            s.ad = ad;
-            s.dhi = dhi;
-          }
-          s.dmode = dmode;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  const uint32_t e_star = s.pn;
-  const unsigned long long above_star = s.an;   // weight of E > e_star
-  const unsigned long long R = s.R;
-  uint32_t e2;
-  unsigned long long above;
-  uint32_t bin3;   // bin of the draw's value in the last exchange
-  if (s.dmode != 2) {
-    e2 = s.pd;
-    above = s.ad;
-    bin3 = (e2 & 255u) | (s.dhi ? 256u : 0u);
-  } else {
-    // ---- the draw from the pass at which it left the speculation: the same
-    // select over the kept set (E > e_star, plus k_tie copies of e_star as one
-    // weight at e_star) for R + 1 --------------------------------------------
-    // While the draw's prefix equals e_star's, its digit totals follow from
-    // the cutoff select's: above e_star's digit they are the same members; at
-    // that digit they are the weight above e_star not yet counted above the
-    // prefix, plus the tie weight; below it there are none.  Only passes after
-    // the prefixes part scan the weights (and those members all exceed e_star).
-    const unsigned long long thr = s.thr;
-    const unsigned long long k_tie = (thr - above_star + e_star - 1) / e_star;  // e_star >= 1
-    const int pf = s.dfail;
-    uint32_t prefix = s.pd;
-    above = s.ad;
-    bool on_star = s.don != 0;
-    for (int pass = pf; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      const uint32_t mask = pass == 0 ? 0u : 0xFFFFFFFFu << (shift + 8);
-      const uint32_t ds = (e_star >> shift) & 255u;
-      if (on_star) {
-        __syncthreads();
-        if (threadIdx.x < 256) {
-          const uint32_t d = threadIdx.x;
-          s.tot[d] = d > ds ? s.tot1[pass][d]
-                   : d == ds ? (above_star - s.above1[pass]) + k_tie * e_star : 0ull;
-        }
-        __syncthreads();
-      } else {
-        hist_clear(s, 256);
-#pragma unroll
-        for (int k = 0; k < kSampPerThread; ++k) {
-          const int i = k * kSampThreads + (int)threadIdx.x;
-          const uint32_t e = i < n_local ? s.e[i] : 0u;
-          hist_add(s, e > e_star && (e & mask) == prefix, e, (e >> shift) & 255u);
-        }
-        hist_totals(s, rank, xn++, 256, err);
-      }
-      pick_digit(s, above, R + 1);
-      const uint32_t sel = s.sel;
-      on_star = on_star && sel == ds;
-      prefix |= sel << shift;
-      above = s.sel_above;
-    }
-    e2 = prefix;
-    bin3 = e2 & 255u;
-  }
+  uint32_t e2, bin3;
+  unsigned long long above, R;
+  bool tot_real;
+  select_draw<SS, kSampThreads, kSampPerThread>(
+      s, n_local, p24, u, [&](int nb) { hist_clear(s, nb); },
+      [&](int nb) { hist_totals(s, rank, xn++, nb, err); }, e2, above, R, bin3, tot_real);
   const unsigned long long j = (R - above) / e2;   // index inside the tie group (id order)
 
   // ---- j-th smallest id with E == e2 ---------------------------------------
@@ -724,7 +745,250 @@ __global__ void __launch_bounds__(kSampThreads)
 }
 
 
-size_t sampler_scratch_bytes(int) { return 0; }
+// ---- one sequence over the whole GPU ----------------------------------------
+// Batch-1 top-p: a 16-CTA cluster leaves 132 SMs idle while each of its CTAs
+// histograms 9,496 ids a pass.  Here every SM takes ceil(vocab / grid) ids (at
+// most 5 a thread), and the exchanges go through device memory: each CTA adds
+// its nonzero digit sums into the exchange's totals with 64-bit reductions
+// (integer sums: the order of the adds cannot change them), then passes a
+// bounded grid barrier.  The launch is cooperative (every CTA resident).  The
+// scratch is zero before the first launch and is left zero: exchange n-1's
+// totals are cleared by one CTA after exchange n's barrier (every CTA has read
+// them by then), the rest by the last CTA to finish.
+constexpr int kGridThreads = 256;
+constexpr int kGridPerThread = 5;
+constexpr int kGridMaxIds = kGridThreads * kGridPerThread;   // 1,280: grids of >= 119 CTAs
+constexpr int kGridMaxX = 8;                                 // 4 cutoff passes + at most 3 draw passes
+constexpr int kGridMaxCtas = 1024;
+
+struct GridScratch {
+  unsigned long long tot[kGridMaxX][512];   // grid-wide digit totals per exchange
+  uint32_t cnt[kGridMaxCtas];               // per-CTA counts of the drawn value (tie groups)
+  uint32_t bar;                             // grid barrier arrivals
+  uint32_t done;                            // CTAs finished
+  uint32_t maxbits;                         // order-preserving bits of the largest scaled logit
+  uint32_t pad;
+};
+
+struct GridShared {
+  static constexpr bool kSpec = true;
+  static constexpr int kBins = 512;
+  static constexpr int kHist = kGridThreads / 32;   // one digit histogram per warp
+  static constexpr int kWarpsPerHist = 1;
+  uint32_t e[kGridMaxIds];
+  uint32_t whist[kHist][2][kBins];
+  unsigned long long tot[kBins];
+  unsigned long long tot1[4][256];
+  unsigned long long above1[4];
+  float red_f[32];
+  uint32_t red_c[32];
+  unsigned long long red_u[32];
+  uint32_t sel;
+  unsigned long long sel_above;
+  unsigned long long thr, an, ad, R;
+  uint32_t pn, pd;
+  int dmode, dfail, don, dhi;
+  uint32_t cta_cnt;
+  int last;
+};
+
+__device__ __forceinline__ uint32_t float_order(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float float_unorder(uint32_t m) {
+  return __uint_as_float((m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m);
+}
+
+// Every CTA arrives, then waits (bounded) until `target` arrivals.
+__device__ __forceinline__ void grid_sync(GridScratch* g, uint32_t target, int* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    red_release_add_u32(&g->bar, 1u);
+    spin_until_geq(&g->bar, target, err);
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void grid_hist_clear(GridShared& s, int nb) {
+  const int lg = nb == 512 ? 9 : 8;
+  uint32_t* h = &s.whist[0][0][0];
+  for (int i = threadIdx.x; i < GridShared::kHist * 2 * nb; i += kGridThreads)
+    h[(i >> lg) * GridShared::kBins + (i & (nb - 1))] = 0;
+  __syncthreads();
+}
+
+// Exchange n of bins [0, nb): barrier n + 1 (barrier 0 is the maximum's).
+__device__ void grid_totals(GridShared& s, GridScratch* g, uint32_t n, int nb, int nblk, int* err) {
+  __syncthreads();
+  for (int b = threadIdx.x; b < nb; b += kGridThreads) {
+    uint32_t lo = 0, hi = 0;   // at most 1,280 weights: each half fits 32 bits
+#pragma unroll
+    for (int w = 0; w < GridShared::kHist; ++w) {
+      lo += s.whist[w][0][b];
+      hi += s.whist[w][1][b];
+    }
+    const unsigned long long h = ((unsigned long long)hi << 16) + lo;
+    if (h) atomicAdd(&g->tot[n][b], h);
+  }
+  grid_sync(g, (uint32_t)nblk * (n + 2), err);
+  if (n > 0 && (int)blockIdx.x == (int)(n % (uint32_t)nblk))
+    for (int b = threadIdx.x; b < 512; b += kGridThreads) g->tot[n - 1][b] = 0ull;
+  for (int b = threadIdx.x; b < nb; b += kGridThreads) s.tot[b] = __ldcg(&g->tot[n][b]);
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kGridThreads, 1)
+    k_sample_grid(const __half* __restrict__ logits, int vocab, float temperature, float top_p,
+                  const uint32_t* __restrict__ u24, int32_t* __restrict__ out_ids,
+                  GridScratch* __restrict__ g, int* err) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  GridShared& s = *reinterpret_cast<GridShared*>(smem_raw);
+  const int nblk = gridDim.x, rank = blockIdx.x;
+  const int chunk = (vocab + nblk - 1) / nblk;
+  const int lo = rank * chunk;
+  const int n_local = max(0, min(vocab, lo + chunk) - lo);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint32_t xn = 0;   // exchanges so far
+
+  // ---- scale + max (NaN logits keep 0.0 and stay out of the maximum) ----
+  float sc[kGridPerThread];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kGridPerThread; ++k) {
+    const int i = k * kGridThreads + tid;
+    sc[k] = i < n_local ? h2f(logits[lo + i]) : __int_as_float(0x7fc00000);
+  }
+#pragma unroll
+  for (int k = 0; k < kGridPerThread; ++k) {
+    float x = 0.0f;
+    if (!isnan(sc[k])) {
+      x = __fdiv_rn(sc[k], temperature);
+      mx = fmaxf(mx, x);
+    }
+    sc[k] = x;
+  }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) s.red_f[warp] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < kGridThreads / 32; ++w) m = fmaxf(m, s.red_f[w]);
+    if (m != -INFINITY) atomicMax(&g->maxbits, float_order(m));
+  }
+  grid_sync(g, (uint32_t)nblk, err);
+  const uint32_t mb = __ldcg(&g->maxbits);
+  if (mb == 0u) {   // every logit NaN (InferenceEngine.swift:311-315)
+    if (rank == 0 && tid == 0) out_ids[0] = kStopToken;
+  } else {
+    const float M = float_unorder(mb);
+    // ---- fixed-point weights, histogrammed by their first digit ----------
+    grid_hist_clear(s, 256);
+#pragma unroll
+    for (int k = 0; k < kGridPerThread; ++k) {
+      const int i = k * kGridThreads + tid;
+      uint32_t E = 0u;
+      if (i < n_local) {
+        const float e = sampler_exp(__fsub_rn(sc[k], M));
+        E = __float2uint_rz(__fmul_rn(e, 2147483648.0f));
+        s.e[i] = E;
+      }
+      hist_add(s, E != 0u, E, E >> 24);
+    }
+    grid_totals(s, g, xn++, 256, nblk, err);
+    const float pc = fminf(fmaxf(top_p, 0.0f), 1.0f);
+    const uint32_t p24 = (uint32_t)__float2uint_rz(__fmul_rn(pc, 16777216.0f));
+    const uint32_t u = u24[0] & 0xFFFFFFu;
+    uint32_t e2, bin3;
+    unsigned long long above, R;
+    bool tot_real;
+    select_draw<GridShared, kGridThreads, kGridPerThread>(
+        s, n_local, p24, u, [&](int nb) { grid_hist_clear(s, nb); },
+        [&](int nb) { grid_totals(s, g, xn++, nb, nblk, err); }, e2, above, R, bin3, tot_real);
+    const unsigned long long j = (R - above) / e2;   // index inside the tie group (id order)
+    const unsigned long long total = (tot_real ? s.tot[bin3] : s.tot1[3][bin3]) / e2;
+
+    // ---- j-th smallest id with E == e2: threads own contiguous id ranges so
+    // that block order = id order; with more than one such id the CTAs'
+    // counts go through device memory behind one more barrier ---------------
+    const int per = (n_local + kGridThreads - 1) / kGridThreads;
+    const int b0 = tid * per, b1 = min(n_local, b0 + per);
+    uint32_t c = 0;
+    for (int i = b0; i < b1; ++i) c += (s.e[i] == e2);
+    const uint32_t incl = block_incl_scan_u32(c, s), excl = incl - c;
+    if (tid == kGridThreads - 1) s.cta_cnt = incl;
+    __syncthreads();
+    unsigned long long before = 0;
+    if (total > 1) {
+      if (tid == 0) g->cnt[rank] = s.cta_cnt;
+      grid_sync(g, (uint32_t)nblk * (xn + 2), err);
+      unsigned long long part = 0;
+      for (int r = tid; r < rank; r += kGridThreads) part += __ldcg(&g->cnt[r]);
+      before = block_sum_u64(part, s);
+    }
+    if (j >= before + excl && j < before + incl) {
+      unsigned long long want = j - before - excl;
+      for (int i = b0; i < b1; ++i) {
+        if (s.e[i] == e2) {
+          if (want == 0) { out_ids[0] = lo + i; break; }
+          --want;
+        }
+      }
+    }
+  }
+
+  // ---- leave the scratch zero for the next launch ----
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s.last = atomicAdd(&g->done, 1u) == (uint32_t)(nblk - 1);
+  }
+  __syncthreads();
+  if (s.last) {
+    __threadfence();
+    if (xn > 0)
+      for (int b = tid; b < 512; b += kGridThreads) g->tot[xn - 1][b] = 0ull;
+    for (int r = tid; r < nblk; r += kGridThreads) g->cnt[r] = 0u;
+    if (tid == 0) {
+      g->maxbits = 0u;
+      g->bar = 0u;
+      g->done = 0u;
+    }
+  }
+}
+
+size_t sampler_scratch_bytes(int n_seq) { return n_seq == 1 ? sizeof(GridScratch) : 0; }
+
+// Cooperative launch over every SM; 1 when the grid path does not apply
+// (a device with too few SMs for 1,280 ids a CTA).
+static int launch_sample_grid(const __half* logits, int vocab, float temperature, float top_p,
+                              const uint32_t* u24, int32_t* out_ids, void* scratch, int* err,
+                              cudaStream_t st) {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return -1;
+  const int nblk = min(sms, kGridMaxCtas);
+  if (nblk < 1 || (vocab + nblk - 1) / nblk > kGridMaxIds) return 1;
+  const size_t smem = sizeof(GridShared);
+  if (cudaFuncSetAttribute(k_sample_grid, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nblk);
+  cfg.blockDim = dim3(kGridThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_sample_grid, logits, vocab, temperature, top_p, u24, out_ids,
+                            reinterpret_cast<GridScratch*>(scratch), err) == cudaSuccess ? 0 : -1;
+}
 
 template <int C>
 static int launch_sample_c(const __half* logits, int n_seq, int row_stride, int vocab,
@@ -804,9 +1068,13 @@ void sampler_prepare() {
 }
 
 int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
-                  float top_p, const uint32_t* u24, int32_t* out_ids, void*, int* err,
+                  float top_p, const uint32_t* u24, int32_t* out_ids, void* scratch, int* err,
                   cudaStream_t st) {
   if (vocab <= 0 || vocab > kVocab || n_seq <= 0) return -1;
+  if (scratch && n_seq == 1 && temperature > 0.0f) {
+    const int rc = launch_sample_grid(logits, vocab, temperature, top_p, u24, out_ids, scratch, err, st);
+    if (rc <= 0) return rc;
+  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   switch (sample_cluster_size(dev, n_seq)) {

@@ -147,17 +147,30 @@ def quantize_q4(w: torch.Tensor):
 
 
 def sample(logits: torch.Tensor, temperature: float, top_p: float,
-           u24: torch.Tensor | None = None, vocab: int = ACTUAL_VOCAB) -> torch.Tensor:
+           u24: torch.Tensor | None = None, vocab: int = ACTUAL_VOCAB,
+           scratch: torch.Tensor | None = None) -> torch.Tensor:
     """extractNextTokenID (InferenceEngine.swift:273-368) on the device.
 
-    logits: [n_seq, row_stride] fp16; u24: [n_seq] 24-bit uniforms (int32)."""
+    logits: [n_seq, row_stride] fp16; u24: [n_seq] 24-bit uniforms (int32).
+    scratch: device bytes from sample_scratch(n_seq) (qwen_sample_scratch: one
+    sequence over every SM); None runs qwen_sample (one cluster per sequence)."""
     if logits.dim() == 1:
         logits = logits.view(1, -1)
     n_seq, stride = logits.shape
     out = torch.empty(n_seq, dtype=torch.int32, device=logits.device)
-    check(lib().qwen_sample(_ptr(logits), n_seq, stride, vocab, temperature, top_p, _ptr(u24),
-                            _ptr(out), _stream()))
+    if scratch is None:
+        check(lib().qwen_sample(_ptr(logits), n_seq, stride, vocab, temperature, top_p, _ptr(u24),
+                                _ptr(out), _stream()))
+    else:
+        check(lib().qwen_sample_scratch(_ptr(logits), n_seq, stride, vocab, temperature, top_p,
+                                        _ptr(u24), _ptr(out), _ptr(scratch), _stream()))
     return out
+
+
+def sample_scratch(n_seq: int, device) -> torch.Tensor | None:
+    """Zeroed scratch for sample(..., scratch=...) (None when n_seq needs none)."""
+    n = lib().qwen_sample_scratch_bytes(n_seq)
+    return torch.zeros(n, dtype=torch.uint8, device=device) if n else None
 
 
 def uniform24(seed: int, sequence: int, step: int) -> int:

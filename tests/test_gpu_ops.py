@@ -180,6 +180,41 @@ def test_sampler_top_p_bitexact(cuda, oracle, temp, top_p):
     assert got.tolist() == want
 
 
+@pytest.mark.parametrize("vocab", [151936, 151666, 4099, 1])
+def test_sampler_grid_bitexact(cuda, oracle, vocab):
+    """One sequence over every SM (qwen_sample_scratch, the batch-1 engine
+    step's sampler; digit totals exchanged through device memory): the
+    oracle's ids on flat, peaked, tied, all-equal, NaN and all-NaN rows, with
+    u24 and top_p at their ends, and the scratch back at zero after every
+    call.  The all-equal row puts the draw in a tie group spread over every
+    CTA (the per-CTA counts go through one more barrier); 4,099 ids leave the
+    last CTAs none."""
+    rng = np.random.default_rng(vocab)
+    rows = [(rng.standard_normal(151936) * sc).astype(np.float16) for sc in (0.05, 0.5, 1.0, 3.0, 8.0)]
+    r = rng.standard_normal(151936).astype(np.float16)
+    r[:100] = 3.0                       # ties in the nucleus
+    rows.append(r)
+    r = rng.standard_normal(151936).astype(np.float16)
+    r[10] = np.nan                      # NaN quirk
+    rows.append(r)
+    rows.append(np.full(151936, 0.25, np.float16))
+    rows.append(np.full(151936, np.nan, np.float16))
+    scr = ops.sample_scratch(1, "cuda")
+    assert scr is not None and ops.sample_scratch(4, "cuda") is None
+    for i, lg in enumerate(rows):
+        for temp, top_p, u in ((0.7, 0.8, oracle.uniform24(5, i, 9)), (1.0, 1.0, 0),
+                               (0.3, 0.0, (1 << 24) - 1), (0.7, 0.95, (1 << 24) - 1)):
+            uu = T(np.array([u], np.uint32).view(np.int32))
+            got = int(N(ops.sample(T(lg[None, :]), temp, top_p, uu, vocab=vocab, scratch=scr))[0])
+            want = oracle.sample_top_p(lg, temp, top_p, int(u), vocab=vocab)
+            assert got == want, (i, temp, top_p, u)
+            assert not N(scr).any(), (i, temp, top_p, u)
+    # greedy with a scratch runs the cluster path
+    if vocab <= 151666:
+        got = N(ops.sample(T(rows[3][None, :]), 0.0, 0.9, vocab=vocab, scratch=scr))
+        assert got.tolist() == [oracle.sample_greedy(rows[3][:vocab])]
+
+
 @pytest.mark.parametrize("n", [1, 3, 12, 17, 64])
 def test_sampler_batch_sizes_bitexact(cuda, oracle, n):
     """Batches run on 16-, 8- or 4-CTA clusters by size (the largest cluster
