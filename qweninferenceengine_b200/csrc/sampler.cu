@@ -66,14 +66,15 @@ struct SampShared {
   static constexpr int kC = C;
   static constexpr int kChunk = (kVocab + C - 1) / C;                           // 37984 / 18992 / 9496
   static constexpr int kPerThread = (kChunk + kSampThreads - 1) / kSampThreads;  // 38 / 19 / 10
-  // With 8 or 16 CTAs the draw select runs beside the cutoff select: a pass
-  // then histograms both member sets (disjoint once the draw's prefix has left
-  // the cutoff's), the draw's in bins 256..511.  With 4 the weights take most
-  // of shared memory and the draw runs after the cutoff.
-  static constexpr bool kSpec = C >= 8;
+  // The draw select runs beside the cutoff select: a pass then histograms
+  // both member sets (disjoint once the draw's prefix has left the cutoff's),
+  // the draw's in bins 256..511.
+  static constexpr bool kSpec = true;
   static constexpr int kBins = kSpec ? 512 : 256;
-  // One digit histogram per pair of warps.
-  static constexpr int kHist = kSampWarps / 2;
+  // One digit histogram per pair of warps; per four warps with 4 CTAs, whose
+  // 38K weights take most of shared memory (the 64-sequence step: the draw
+  // beside the cutoff there measured 2.081 -> 2.055 ms a step).
+  static constexpr int kHist = C >= 8 ? kSampWarps / 2 : kSampWarps / 4;
   static constexpr int kWarpsPerHist = kSampWarps / kHist;
   uint32_t e[kChunk];                        // scaled floats, then fixed-point weights
   // Digit weights of the running pass as two exact halves (E & 0xFFFF, E >> 16):

@@ -8,12 +8,12 @@ sum K and return the first kept id whose running sum exceeds R.  The kernel find
 the cutoff and the draw with two 4-pass weighted radix selects (8-bit digits).
 It builds the first pass of the cutoff select while it computes the weights (S
 is the sum of that pass's totals), and it derives the draw's digit totals from
-the cutoff select's while the draw's prefix equals the cutoff value's.  With 8-
-or 16-CTA clusters the draw runs beside the cutoff select: after each pass R is
+the cutoff select's while the draw's prefix equals the cutoff value's.  The
+kernels run the draw beside the cutoff select: after each pass R is
 bounded (the kept sum lies in [thr, thr + e_star - 1] and the cutoff's prefix
 bounds e_star), and while both ends of that range pick the same digit the next
-pass histograms the draw's members beside the cutoff's; otherwise, and with
-4-CTA clusters, the draw resumes after the cutoff select, scanning the weights
+pass histograms the draw's members beside the cutoff's; otherwise the draw
+resumes after the cutoff select, scanning the weights
 only after the prefixes part.  The final id is located from the per-rank
 weights of the last exchange.  This file checks that restatement,
 pass for pass as the kernel runs it, against a plain sort over many weight
@@ -68,9 +68,9 @@ def pick(tot, above, target):
 def kernel(E: np.ndarray, p24: int, u24: int, scans: list, spec: bool = False, C: int = 4,
            fails: list | None = None) -> int:
     """k_sample's select on C ranks' chunks of E.  spec: the draw select runs
-    beside the cutoff select (8- and 16-CTA clusters) while both ends of R's
-    range pick the same digit; without it (4-CTA clusters), or from the pass
-    at which the ends part, the draw runs after the cutoff select."""
+    beside the cutoff select (the kernels' mode) while both ends of R's range
+    pick the same digit; without it, or from the pass at which the ends part,
+    the draw runs after the cutoff select."""
     E = E.astype(np.uint32)
     n = E.size
     chunk = -(-n // C)
@@ -199,7 +199,7 @@ def weights(rng, kind, n):
     return np.floor(e * 2.0 ** 31).astype(np.uint64).clip(0, 2 ** 31).astype(np.uint32)
 
 
-@pytest.mark.parametrize("spec,C", [(False, 4), (True, 8), (True, 16)])
+@pytest.mark.parametrize("spec,C", [(False, 4), (True, 4), (True, 8), (True, 16)])
 @pytest.mark.parametrize("kind", ["flat", "peaked", "ties", "equal", "dominant", "underflow"])
 def test_select_matches_rule(kind, spec, C):
     rng = np.random.default_rng(len(kind))
