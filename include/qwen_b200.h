@@ -189,6 +189,8 @@ size_t qwen_sample_scratch_bytes(uint32_t n_seq);
  * and temperature > 0 the sequence runs on every SM at once (a cooperative
  * launch; the CTAs exchange digit totals through the scratch), otherwise as
  * qwen_sample.  Calls that share a scratch must be ordered on one stream.
+ * After a device-side wait gives up (qwen_ops_status reports
+ * QWEN_ERR_DEVICE_TIMEOUT) the scratch may hold partial totals: zero it again.
  * The same ids as qwen_sample (InferenceEngine.swift:273-368); the batch-1
  * engine step samples this way. */
 int qwen_sample_scratch(const uint16_t* logits, uint32_t n_seq, uint32_t row_stride, uint32_t vocab,
