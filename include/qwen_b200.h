@@ -347,9 +347,13 @@ int qwen_engine_set_wait_timeout(qwen_engine* e, uint64_t timeout_ns);
 
 /* Test hook, no reference counterpart: site 9 makes the fused step's waits for
  * the down projection's partial sums expect data that nothing writes, so the
- * waits run out and the timeout path runs; site 0 turns the hook off. */
+ * waits run out and the timeout path runs; site 20 makes one CTA of the batch-1
+ * grid sampler skip its arrival at the first exchange's barrier, so the other
+ * CTAs' waits run out (reported as site 20, barrier 1); site 0 turns the hook
+ * off.  The limit of both is qwen_engine_set_wait_timeout's. */
 #define QWEN_STALL_NONE 0
 #define QWEN_STALL_FUSED_DOWN 9
+#define QWEN_STALL_SAMPLER 20
 int qwen_engine_test_stall(qwen_engine* e, int32_t site);
 
 /* Device and stream the engine runs on (for callers that time it). */

@@ -419,7 +419,8 @@ int QwenEngine::enqueue_step_ops(cudaEvent_t* ev) {
   launch_gemv_fp16_rowmajor(m.embed, s.residual, s.logits, kVocab, kHidden, vs);
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, s.samp_scratch, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st, wait_ns_,
+                    stall_site_ == kSamplerStallSite) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   if (ev) cudaEventRecord(ev[3], st);
@@ -437,7 +438,8 @@ int QwenEngine::enqueue_step_fused(cudaEvent_t* ev) {
   QWEN_TRY(enqueue_fused_step(a, st));
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, s.samp_scratch, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st, wait_ns_,
+                    stall_site_ == kSamplerStallSite) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   if (ev) cudaEventRecord(ev[3], st);
@@ -454,7 +456,8 @@ int QwenEngine::enqueue_step_tc(cudaEvent_t* ev) {
   QWEN_TRY(enqueue_tc_model(model_, state_, tc_decode_rows(state_), sm_count_, st));
   if (ev) cudaEventRecord(ev[2], st);
   if (launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, s.samp_scratch, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st, wait_ns_,
+                    stall_site_ == kSamplerStallSite) != 0)
     return launch_status("sample");
   k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   if (ev) cudaEventRecord(ev[3], st);
@@ -606,7 +609,7 @@ int QwenEngine::set_wait_timeout(uint64_t ns) {
 
 int QwenEngine::test_stall(int site) {
   if (!initialised_) return set_error(QWEN_ERR_STATE, "engine not initialised");
-  if (site != 0 && site != kFusedStallDownPart)
+  if (site != 0 && site != kFusedStallDownPart && site != kSamplerStallSite)
     return set_error(QWEN_ERR_INVALID_ARGUMENT, "no stall hook for wait site %d", site);
   QWEN_CUDA(cudaSetDevice(cfg_.device), "cudaSetDevice");
   QWEN_CUDA(cudaStreamSynchronize(stream_), "sync");
@@ -688,7 +691,8 @@ int QwenEngine::profile_step(float* ms, int cap, int* n) {
   int rc = enqueue_tc_model(model_, state_, tc_decode_rows(state_), sm_count_, st, ev.data() + 1,
                             &marks);
   if (rc == QWEN_OK && launch_sample(s.logits, s.batch, kVocab, kActualVocab, cfg_.temperature,
-                                     cfg_.top_p, s.u24_, s.sampled, s.samp_scratch, s.err, st) != 0)
+                                     cfg_.top_p, s.u24_, s.sampled, s.samp_scratch, s.err, st, wait_ns_,
+                    stall_site_ == kSamplerStallSite) != 0)
     rc = launch_status("sample");
   if (rc == QWEN_OK)
     k_step_end<<<1, s.batch, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
@@ -760,7 +764,8 @@ int QwenEngine::prefill_chunked(const int32_t* ids, int32_t n) {
                               (size_t)last * kVocab * 2, (size_t)kVocab * 2, B, cudaMemcpyDeviceToDevice,
                               st), "memcpy logits");
   if (launch_sample(s.logits, B, kVocab, kActualVocab, cfg_.temperature, cfg_.top_p, s.u24_,
-                    s.sampled, s.samp_scratch, s.err, st) != 0)
+                    s.sampled, s.samp_scratch, s.err, st, wait_ns_,
+                    stall_site_ == kSamplerStallSite) != 0)
     return launch_status("sample");
   k_step_end<<<1, B, 0, st>>>(s.ctl, s.sampled, s.out_tokens, s.max_out, cfg_.stop_on_eos);
   QWEN_TRY(launch_status("chunked prefill"));

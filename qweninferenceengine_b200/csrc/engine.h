@@ -246,6 +246,8 @@ struct FusedStepArgs {
 // Wait site of the fused step's poll for the down partial sums, for the
 // stall test hook.
 constexpr int kFusedStallDownPart = 9;
+// Stall hook site of the batch-1 grid sampler's first exchange barrier.
+constexpr int kSamplerStallSite = 20;
 int fused_scratch_bytes(int batch, int max_ctx, int sm_count, size_t* bytes);
 int enqueue_fused_step(const FusedStepArgs& a, cudaStream_t st);
 int build_fused_weights(QwenModel& m, int max_ctx, cudaStream_t st);

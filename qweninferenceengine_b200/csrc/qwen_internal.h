@@ -94,9 +94,12 @@ size_t sampler_scratch_bytes(int n_seq);
 // Host set-up of the sampler for the current device (cluster-size query); call
 // before capturing a launch_sample into a CUDA graph.
 void sampler_prepare();
+// wait_ns bounds the grid path's barrier waits; stall: test hook (CTA 0
+// skips one arrival so that the others' waits run out).
 int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
                   float top_p, const uint32_t* u24, int32_t* out_ids, void* scratch,
-                  int* err, cudaStream_t st);
+                  int* err, cudaStream_t st, unsigned long long wait_ns = 2000000000ull,
+                  int stall = 0);
 
 // ------------------------------------------------------ weight helpers ----
 int launch_quantize_q4(const float* w, size_t n, uint8_t* packed, __half* scales,

@@ -801,15 +801,58 @@ __device__ __forceinline__ float float_unorder(uint32_t m) {
   return __uint_as_float((m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m);
 }
 
-// Every CTA arrives, then waits (bounded) until `target` arrivals.  The
-// block barrier orders the CTA's writes before thread 0's release add, and
-// its acquire load before the CTA's later reads (explicit fences around them
-// measured 2 us slower a call).
-__device__ __forceinline__ void grid_sync(GridScratch* g, uint32_t target, int* err) {
+// Limits of the grid kernel's barrier waits: wait_ns of %globaltimer; stall
+// (test hook, the engine's test_stall): CTA 0 does not arrive at barrier
+// kGridStallBarrier, so the others' waits run out.
+struct GridWait {
+  unsigned long long wait_ns;
+  int stall;
+  int* err;
+};
+constexpr int kGridWaitSite = 20;       // wait site reported in err[1] (x 100 + barrier)
+constexpr int kGridStallBarrier = 1;    // the first exchange's barrier
+
+__device__ __forceinline__ unsigned long long grid_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Thread 0's wait for `target` arrivals.  Every 64th poll looks at the error
+// word (a CTA that gave up ends the others' waits) and the clock; a timeout
+// records err[1] = site, err[2] = CTA (the first failure wins).
+__device__ __noinline__ void grid_wait(const uint32_t* bar, uint32_t target, const GridWait& w,
+                                       int site) {
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_u32(bar) >= target) return;
+    if ((it & 63) == 63) {
+      if (w.err && *reinterpret_cast<volatile int*>(w.err) != 0) return;
+      const unsigned long long now = grid_now();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > w.wait_ns) {
+        if (w.err && atomicCAS(w.err, 0, kDevWaitTimeout) == 0) {
+          w.err[1] = site;
+          w.err[2] = blockIdx.x;
+          w.err[3] = 0;
+        }
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+// Every CTA arrives at barrier `index` (its target is index + 1 arrivals of
+// every CTA), then waits.  The block barrier orders the CTA's writes before
+// thread 0's release add, and its acquire load before the CTA's later reads
+// (explicit fences around them measured 2 us slower a call).
+__device__ __forceinline__ void grid_sync(GridScratch* g, uint32_t index, const GridWait& w) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    red_release_add_u32(&g->bar, 1u);
-    spin_until_geq(&g->bar, target, err);
+    if (!(w.stall && blockIdx.x == 0 && index == kGridStallBarrier)) red_release_add_u32(&g->bar, 1u);
+    grid_wait(&g->bar, gridDim.x * (index + 1), w, kGridWaitSite * 100 + (int)index);
   }
   __syncthreads();
 }
@@ -825,7 +868,8 @@ __device__ __forceinline__ void grid_hist_clear(GridShared& s, int nb) {
 }
 
 // Exchange n of bins [0, nb): barrier n + 1 (barrier 0 is the maximum's).
-__device__ void grid_totals(GridShared& s, GridScratch* g, uint32_t n, int nb, int nblk, int* err) {
+__device__ void grid_totals(GridShared& s, GridScratch* g, uint32_t n, int nb, int nblk,
+                            const GridWait& w) {
   __syncthreads();
   for (int b = threadIdx.x; b < nb; b += kGridThreads) {
     uint32_t lo = 0, hi = 0;   // at most 1,280 weights: each half fits 32 bits
@@ -839,7 +883,7 @@ __device__ void grid_totals(GridShared& s, GridScratch* g, uint32_t n, int nb, i
     const unsigned long long h = ((unsigned long long)hi << 16) + lo;
     if (h) atomicAdd(&g->tot[n][b], h);
   }
-  grid_sync(g, (uint32_t)nblk * (n + 2), err);
+  grid_sync(g, n + 1, w);
   if (n > 0 && (int)blockIdx.x == (int)(n % (uint32_t)nblk))
     for (int b = threadIdx.x; b < 512; b += kGridThreads) g->tot[n - 1][b] = 0ull;
   for (int b = threadIdx.x; b < nb; b += kGridThreads) s.tot[b] = __ldcg(&g->tot[n][b]);
@@ -849,7 +893,7 @@ __device__ void grid_totals(GridShared& s, GridScratch* g, uint32_t n, int nb, i
 __global__ void __launch_bounds__(kGridThreads, 1)
     k_sample_grid(const __half* __restrict__ logits, int vocab, float temperature, float top_p,
                   const uint32_t* __restrict__ u24, int32_t* __restrict__ out_ids,
-                  GridScratch* __restrict__ g, int* err) {
+                  GridScratch* __restrict__ g, int* err, unsigned long long wait_ns, int stall) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   GridShared& s = *reinterpret_cast<GridShared*>(smem_raw);
   const int nblk = gridDim.x, rank = blockIdx.x;
@@ -858,6 +902,7 @@ __global__ void __launch_bounds__(kGridThreads, 1)
   const int n_local = max(0, min(vocab, lo + chunk) - lo);
   const int tid = threadIdx.x, warp = tid >> 5;
   uint32_t xn = 0;   // exchanges so far
+  const GridWait w{wait_ns, stall, err};
 
   // ---- scale + max (NaN logits keep 0.0 and stay out of the maximum) ----
   float sc[kGridPerThread];
@@ -884,7 +929,7 @@ __global__ void __launch_bounds__(kGridThreads, 1)
     for (int w = 0; w < kGridThreads / 32; ++w) m = fmaxf(m, s.red_f[w]);
     if (m != -INFINITY) atomicMax(&g->maxbits, float_order(m));
   }
-  grid_sync(g, (uint32_t)nblk, err);
+  grid_sync(g, 0, w);
   const uint32_t mb = __ldcg(&g->maxbits);
   if (mb == 0u) {   // every logit NaN (InferenceEngine.swift:311-315)
     if (rank == 0 && tid == 0) out_ids[0] = kStopToken;
@@ -903,7 +948,7 @@ __global__ void __launch_bounds__(kGridThreads, 1)
       }
       hist_add(s, E != 0u, E, E >> 24);
     }
-    grid_totals(s, g, xn++, 256, nblk, err);
+    grid_totals(s, g, xn++, 256, nblk, w);
     const float pc = fminf(fmaxf(top_p, 0.0f), 1.0f);
     const uint32_t p24 = (uint32_t)__float2uint_rz(__fmul_rn(pc, 16777216.0f));
     const uint32_t u = u24[0] & 0xFFFFFFu;
@@ -912,7 +957,7 @@ __global__ void __launch_bounds__(kGridThreads, 1)
     bool tot_real;
     select_draw<GridShared, kGridThreads, kGridPerThread>(
         s, n_local, p24, u, [&](int) {},
-        [&](int nb) { grid_totals(s, g, xn++, nb, nblk, err); }, e2, above, R, bin3, tot_real);
+        [&](int nb) { grid_totals(s, g, xn++, nb, nblk, w); }, e2, above, R, bin3, tot_real);
     const unsigned long long j = (R - above) / e2;   // index inside the tie group (id order)
     const unsigned long long total = (tot_real ? s.tot[bin3] : s.tot1[3][bin3]) / e2;
 
@@ -929,7 +974,7 @@ __global__ void __launch_bounds__(kGridThreads, 1)
     unsigned long long before = 0;
     if (total > 1) {
       if (tid == 0) g->cnt[rank] = s.cta_cnt;
-      grid_sync(g, (uint32_t)nblk * (xn + 2), err);
+      grid_sync(g, xn + 1, w);
       unsigned long long part = 0;
       for (int r = tid; r < rank; r += kGridThreads) part += __ldcg(&g->cnt[r]);
       before = block_sum_u64(part, s);
@@ -971,7 +1016,7 @@ size_t sampler_scratch_bytes(int n_seq) { return n_seq == 1 ? sizeof(GridScratch
 // (a device with too few SMs for 1,280 ids a CTA).
 static int launch_sample_grid(const __half* logits, int vocab, float temperature, float top_p,
                               const uint32_t* u24, int32_t* out_ids, void* scratch, int* err,
-                              cudaStream_t st) {
+                              cudaStream_t st, unsigned long long wait_ns, int stall) {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -993,7 +1038,9 @@ static int launch_sample_grid(const __half* logits, int vocab, float temperature
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_sample_grid, logits, vocab, temperature, top_p, u24, out_ids,
-                            reinterpret_cast<GridScratch*>(scratch), err) == cudaSuccess ? 0 : -1;
+                            reinterpret_cast<GridScratch*>(scratch), err, wait_ns, stall) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 template <int C>
@@ -1075,10 +1122,11 @@ void sampler_prepare() {
 
 int launch_sample(const __half* logits, int n_seq, int row_stride, int vocab, float temperature,
                   float top_p, const uint32_t* u24, int32_t* out_ids, void* scratch, int* err,
-                  cudaStream_t st) {
+                  cudaStream_t st, unsigned long long wait_ns, int stall) {
   if (vocab <= 0 || vocab > kVocab || n_seq <= 0) return -1;
   if (scratch && n_seq == 1 && temperature > 0.0f) {
-    const int rc = launch_sample_grid(logits, vocab, temperature, top_p, u24, out_ids, scratch, err, st);
+    const int rc = launch_sample_grid(logits, vocab, temperature, top_p, u24, out_ids, scratch, err,
+                                      st, wait_ns, stall);
     if (rc <= 0) return rc;
   }
   int dev = 0;

@@ -160,6 +160,32 @@ def test_positions_past_the_window_in_error_mode(cuda, one_layer):
     eng.close()
 
 
+def test_sampler_wait_runs_out_and_the_engine_recovers(cuda, oracle, one_layer):
+    """The batch-1 top-p sampler (every SM, digit totals exchanged through
+    device memory behind grid barriers) bounds its barrier waits by the
+    engine's wait limit: with one CTA held back from the first exchange's
+    barrier (test hook site 20) the others give up, forward() returns
+    QWEN_ERR_DEVICE_TIMEOUT naming the site and barrier, and once the hook is
+    off the next steps draw the oracle sampler's ids on the engine's logits
+    (the engine cleared the sampler's scratch)."""
+    from qweninferenceengine_b200 import ops
+    eng = QwenEngine(one_layer, cfg(kernels="fused", temperature=0.7, top_p=0.8, seed=3))
+    nxt = eng.forward(7, 0)
+    assert nxt == oracle.sample_top_p(eng.logits(), 0.7, 0.8, ops.uniform24(3, 0, 0))
+    eng.set_wait_timeout(20_000_000)                          # 20 ms
+    eng.test_stall(20)
+    with pytest.raises(QwenError) as ei:
+        eng.forward(8, 1)
+    assert ei.value.code == QWEN_ERR_DEVICE_TIMEOUT
+    assert re.search(r"timed out \(site 20, phase 1,", str(ei.value)), str(ei.value)
+    eng.test_stall(0)
+    eng.set_wait_timeout(2_000_000_000)
+    for pos, tok in ((1, 8), (2, 9), (3, 10)):                # position 1 again, then on
+        nxt = eng.forward(tok, pos)
+        assert nxt == oracle.sample_top_p(eng.logits(), 0.7, 0.8, ops.uniform24(3, 0, pos)), pos
+    eng.close()
+
+
 def test_device_wait_runs_out_and_the_engine_recovers(cuda, oracle, one_layer):
     eng = QwenEngine(one_layer, cfg(kernels="fused"))
     om = OracleModel(oracle, one_layer, 1, 32)
