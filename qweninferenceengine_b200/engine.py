@@ -213,11 +213,14 @@ class QwenEngine:
         return out
 
     def set_wait_timeout(self, ns: int) -> None:
-        """Device wait limit of the fused step (qwen_engine_set_wait_timeout)."""
+        """Device wait limit of the fused step and the batch-1 sampler
+        (qwen_engine_set_wait_timeout)."""
         check(lib().qwen_engine_set_wait_timeout(self._h, int(ns)))
 
     def test_stall(self, site: int) -> None:
-        """Test hook: make the fused step's waits at `site` run out (0: off)."""
+        """Test hook: make device waits run out (qwen_engine_test_stall): 9, the
+        fused step's wait for the down partial sums; 20, the batch-1 sampler's
+        first exchange barrier; 0, off."""
         check(lib().qwen_engine_test_stall(self._h, site))
 
     def stream(self) -> int:
