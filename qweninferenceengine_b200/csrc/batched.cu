@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(64) k_qkv_finish(const float* __restrict__ par
 // cluster of kFinCtas CTAs per row, one column per thread, so every thread
 // issues all its split loads at once (one CTA per row kept 84 of 148 SMs idle
 // and walked three columns per thread); the row's sum of squares meets in
-// distributed shared memory, added in rank order.
+// distributed shared memory (each rank pushes its partial to every rank), added in rank order.
 constexpr int kFinCtas = 4;
 constexpr int kFinThreads = kHidden / kFinCtas;  // 384
 __global__ void __launch_bounds__(kFinThreads) k_resid_norm_finish(
@@ -202,10 +202,11 @@ __global__ void __launch_bounds__(kFinThreads) k_resid_norm_finish(
   pdl_prologue();
   namespace cg = cooperative_groups;
   __shared__ float red[kFinThreads / 32];
-  __shared__ float cta_ss;  // this CTA's sum of squares, read by the cluster
+  __shared__ float ss_in[kFinCtas];  // every rank's sum of squares, written by that rank
   cg::cluster_group cluster = cg::this_cluster();
   const int b = blockIdx.y;
-  const int i = (int)cluster.block_rank() * kFinThreads + (int)threadIdx.x;
+  const int rank = (int)cluster.block_rank();
+  const int i = rank * kFinThreads + (int)threadIdx.x;
   __half* xr = x + (size_t)b * kHidden;
   const __half y = f2h(sum_splits(part, splits, nbv, kHidden, b, i) + h2f(bias[i]));
   const __half xn = __hadd(xr[i], y);
@@ -218,15 +219,18 @@ __global__ void __launch_bounds__(kFinThreads) k_resid_norm_finish(
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < kFinThreads / 32; ++w) t += red[w];
-    cta_ss = t;
+#pragma unroll
+    for (int r = 0; r < kFinCtas; ++r) *cluster.map_shared_rank(&ss_in[rank], r) = t;
   }
+  // the pushes land before the barrier and the sums are then read locally, so
+  // no CTA touches another's shared memory after it (no second barrier before
+  // exit)
   cluster.sync();
   float tot = 0.f;
 #pragma unroll
-  for (int r = 0; r < kFinCtas; ++r) tot += *cluster.map_shared_rank(&cta_ss, r);
+  for (int r = 0; r < kFinCtas; ++r) tot += ss_in[r];
   const float sc = 1.0f / sqrtf(tot / 1536.0f + kRmsEps);
   *reinterpret_cast<__half*>(act + act_off(b, i, nb)) = __hmul(f2h(v * sc), gamma[i]);
-  cluster.sync();  // peers may still be reading cta_ss
 }
 
 // Row r = position p0 + r of sequence 0: x[r] = embedding of its prompt id,
