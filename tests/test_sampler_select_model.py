@@ -15,7 +15,8 @@ bounds e_star), and while both ends of that range pick the same digit the next
 pass histograms the draw's members beside the cutoff's; otherwise the draw
 resumes after the cutoff select, scanning the weights
 only after the prefixes part.  The final id is located from the per-rank
-weights of the last exchange.  This file checks that restatement,
+weights of the last exchange (the grid kernel's count of the drawn value from that exchange's totals, or
+the cutoff's pass-3 totals when the draw ended without a scan).  This file checks that restatement,
 pass for pass as the kernel runs it, against a plain sort over many weight
 distributions (ties at the cutoff, all-equal weights, one dominant weight, zero
 weights, u24 and top-p at their ends).
@@ -148,12 +149,14 @@ def kernel(E: np.ndarray, p24: int, u24: int, scans: list, spec: bool = False, C
     n_scans = 0
     if dmode != 2:
         e2, above, bin3 = pd, ad, (pd & 255) | (256 if dhi else 0)
+        tot_real = True
     else:
         if fails is not None and spec:
             fails.append(dfail)
         # draw: derived totals while on e_star's prefix, scans after
         k_tie = (thr - above_star + e_star - 1) // e_star
         prefix, above, on_star = pd, ad, don
+        tot_real = False
         for p in range(dfail, 4):
             shift, mask = 24 - 8 * p, mask_of(p)
             ds = (e_star >> shift) & 255
@@ -165,12 +168,17 @@ def kernel(E: np.ndarray, p24: int, u24: int, scans: list, spec: bool = False, C
                 last = exchange((E > e_star) & ((E & mask) == prefix), None, shift)
                 tot = last.sum(0)
                 n_scans += 1
+                tot_real = p == 3
             d, above = pick(tot, above, R + 1)
             on_star = on_star and d == ds
             prefix |= d << shift
         e2, bin3 = prefix, prefix & 255
     scans.append(n_scans)
     j = (R - above) // e2
+    # the grid kernel's count of the drawn value: the last exchange's total at
+    # its bin, or the cutoff's pass-3 total when the draw ended without a scan
+    total = int(last.sum(0)[bin3]) if tot_real else int(tot1[3][bin3])
+    assert total == int(np.count_nonzero(E == e2)) * int(e2)
     # the owning rank from the last exchange's per-rank weights at e2
     w = last[:, bin3]
     assert np.all(w % e2 == 0)
